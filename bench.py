@@ -1,0 +1,375 @@
+#!/usr/bin/env python3
+"""bench.py — Qwen3-0.6B w8a8 greedy decode throughput on B200.
+
+Workload (one "step"): one greedy decode token for each of 64 sequences whose
+2048-token prefixes already sit in the paged int8 KV cache (32-token pages,
+shuffled page tables), 28 layers, vocab 151936, fused lm_head+argmax — the
+reference's per-layer chain rmsnorm -> QKV GEMMs with norm/rope/quant -> paged
+GQA attention -> O GEMM + residual -> gate/up SwiGLU quant -> down GEMM +
+residual, then final norm + lm_head argmax.  Weights are random-init
+(N(0,0.02), per-row int8) and the KV prefixes seeded int8; both are generated
+on the device.  Each step streams ~8.6 GB of KV (far larger than L2), so no
+L2 flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs N independent replicas (one process per GPU, torchrun env), the
+path has no data-path collective in this mode: scaling is weak.
+``--impl reference`` times the reference algorithm's CPU restatement (the
+oracle port of tools/ref_qwen3.py) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+METRIC = "Qwen3-0.6B w8a8 prefill & decode tokens/s at 1/2/4/8 B200; % int8/HBM roofline"
+SEQS, CTX, LAYERS, VOCAB = 64, 2048, 28, 151936
+KV_BYTES_PER_TOKEN_LAYER = 2 * 1024 + 2 * 8 * 4   # K+V int8 rows + f32 per-head scales
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--seqs", type=int, default=SEQS)
+    ap.add_argument("--ctx", type=int, default=CTX)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layer count (only for small profiling captures; the metric needs 28)")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        self.tmp.flush()
+        rows = [ln.split(",") for ln in Path(self.tmp.name).read_text().splitlines() if ln.strip()]
+        os.unlink(self.tmp.name)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+                for nm, val in zip(names, r[5:9]):
+                    if val.strip().lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    sys.path.insert(0, str(REPO))
+    import __graft_entry__ as ge
+    q3 = ge.load_package()
+    from q3b200 import synthetic
+    from q3b200.model import Dims
+    lib = q3._lib.lib()
+    dev = torch.device("cuda", local_rank)
+
+    B, K, W = args.seqs, args.steps, args.warmup
+    max_seq = ((args.ctx + W + 2 * K + 2 + 31) // 32) * 32
+    dims = Dims(layers=args.layers, vocab=VOCAB, max_seq=max_seq)
+    bm = synthetic.random_blob_model(dims, seed=1000 + rank, device=dev)
+    max_pages = max_seq // 32
+    pool = synthetic.KVPoolTensors(args.layers, B * max_pages, 8, device=dev)
+    pool.fill_random(seed=2000 + rank)
+    g = torch.Generator().manual_seed(3000 + rank)
+    tables = torch.randperm(B * max_pages, generator=g).reshape(B, max_pages).to(torch.int16)
+    tab_d = tables.to(dev)
+    ids_d = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32).to(dev)
+    pos_d = torch.full((B,), args.ctx, dtype=torch.int32, device=dev)
+    nxt_d = torch.zeros(B, dtype=torch.int32, device=dev)
+    wsb = lib.q3_decode_workspace_bytes(C.byref(bm.L), B)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+    cpool = pool.c()
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(s):
+        q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
+            bm.blob.data_ptr(), C.byref(bm.L), C.byref(cpool), tab_d.data_ptr(), max_pages,
+            ids_d.data_ptr(), pos_d.data_ptr(), B, nxt_d.data_ptr(), ws.data_ptr(), wsb,
+            s.cuda_stream))
+
+    def advance():
+        ids_d.copy_(nxt_d)
+        pos_d.add_(1)
+
+    with torch.cuda.stream(stream):
+        for _ in range(W):
+            step(stream)
+            advance()
+    torch.cuda.synchronize(dev)
+
+    # attention launches of one step are timed live with CUDA events
+    n_ev = args.layers
+    ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    for e in ev_s + ev_e:
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    hs = (C.c_void_p * n_ev)(*[e.cuda_event for e in ev_s])
+    he = (C.c_void_p * n_ev)(*[e.cuda_event for e in ev_e])
+
+    use_graph = not args.no_graph
+    graph = None
+    l0 = lib.q3_launch_count()
+    if use_graph:
+        graph = torch.cuda.CUDAGraph()
+        lib.q3_timer_attach(b"attention", hs, he, n_ev)
+        with torch.cuda.graph(graph, stream=stream):
+            step(stream)
+        lib.q3_timer_detach()
+        launches_per_step = lib.q3_launch_count() - l0
+        graph.replay()          # one untimed replay (graph upload)
+        torch.cuda.synchronize(dev)
+    else:
+        with torch.cuda.stream(stream):
+            step(stream)
+        torch.cuda.synchronize(dev)
+        launches_per_step = lib.q3_launch_count() - l0
+
+    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    clocks = ClockSampler(vis[local_rank].strip() if local_rank < len(vis) else local_rank)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    if not use_graph:
+        lib.q3_timer_attach(b"attention", hs, he, n_ev)
+    torch.cuda.nvtx.range_push("q3_timed")
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(K):
+            if use_graph:
+                graph.replay()
+            else:
+                step(stream)
+            advance()
+        t1.record(stream)
+    torch.cuda.synchronize(dev)
+    torch.cuda.nvtx.range_pop()
+    ck = clocks.stop()
+    if not use_graph:
+        lib.q3_timer_detach()
+    if dist:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    try:
+        att_ms = [a.elapsed_time(b) for a, b in zip(ev_s, ev_e)]
+    except RuntimeError:    # events of graph nodes not timeable: time one eager step
+        lib.q3_timer_attach(b"attention", hs, he, n_ev)
+        with torch.cuda.stream(stream):
+            step(stream)
+        torch.cuda.synchronize(dev)
+        lib.q3_timer_detach()
+        att_ms = [a.elapsed_time(b) for a, b in zip(ev_s, ev_e)]
+    att_avg = sum(att_ms) / len(att_ms)
+
+    # e2e: host feeds ids/pos from pinned memory and reads the next ids back
+    ids_h = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    pos_h = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    out_h = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    ids_h.copy_(ids_d.cpu())
+    pos_h.copy_(pos_d.cpu())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(K):
+            ids_d.copy_(ids_h, non_blocking=True)
+            pos_d.copy_(pos_h, non_blocking=True)
+            if use_graph:
+                graph.replay()
+            else:
+                step(stream)
+            out_h.copy_(nxt_d, non_blocking=True)
+            stream.synchronize()
+            ids_h.copy_(out_h)
+            pos_h.add_(1)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+
+    if dist:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    if graph is not None:
+        del graph
+    if dist:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
+        REPO / "MEASURED_PEAKS.json").exists() else {}
+    peak_gbs = float(peaks.get("hbm_gbs", 6650.0))
+    # one attention launch = one layer for all sequences at the last timed position
+    ctx_last = args.ctx + W + K - 1 + 1
+    att_bytes = B * ctx_last * KV_BYTES_PER_TOKEN_LAYER + B * (2048 + 2048 + 16 * 4 * 2)
+    achieved = att_bytes / (att_avg * 1e-3) / 1e9
+    tokens = world * B * K
+    line = {
+        "metric": METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+        "data": "synthetic (random-init w8a8 weights, seeded int8 KV prefixes)",
+        "config": {"workload": "config 4: batched paged greedy decode, 64 seqs x 2048-token "
+                               "prefix, 28 layers, vocab 151936 (decode tokens/s)",
+                   "seqs_per_gpu": B, "context": args.ctx, "page_tokens": 32,
+                   "cuda_graph": use_graph, "l2": "inputs larger than L2 (~8.6 GB KV read per step)",
+                   "parallelism": f"replicas x{world}"},
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * 4 * B, "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": int(launches_per_step) * K,
+        "roofline": {"bound": "hbm", "kernel": "k_attention_paged (decode, one layer, 64 seqs)",
+                     "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+                     "frac": round(achieved / peak_gbs, 4), "traffic": None,
+                     "avg_launch_ms": round(att_avg, 4), "bytes_per_launch": att_bytes,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650"},
+        "clocks": ck,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(args.ctx)
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# CPU: the oracle port of tools/ref_qwen3.py on the host cores
+# ---------------------------------------------------------------------------
+def _oracle_setup(ctx: int, seqs: int):
+    import numpy as np
+    sys.path.insert(0, str(REPO))
+    from oracle import q3_oracle as O
+    from oracle import synth
+    shape = synth.Shape(max_seq=((ctx + 64 + 31) // 32) * 32)
+    w = synth.build_model(shape)
+    rng = np.random.default_rng(7)
+    kvs = []
+    for _ in range(seqs):
+        kv = O.KV.empty(w, shape.max_seq)
+        for L in range(LAYERS):
+            kv.k8[L][:ctx] = rng.integers(-127, 128, (ctx, 1024), dtype=np.int8)
+            kv.v8[L][:ctx] = rng.integers(-127, 128, (ctx, 1024), dtype=np.int8)
+            kv.ks[L][:ctx] = rng.uniform(1e-3, 1e-2, (ctx, 8)).astype(np.float32)
+            kv.vs[L][:ctx] = rng.uniform(1e-3, 1e-2, (ctx, 8)).astype(np.float32)
+        kvs.append(kv)
+    return O, w, kvs
+
+
+def cpu_baseline_sample(ctx: int) -> dict:
+    O, w, kvs = _oracle_setup(ctx, 1)
+    t = time.perf_counter()
+    lg = O.forward_chunk(w, [123], kvs[0], ctx, 1, True)
+    O.argmax_logits(lg)
+    dt = time.perf_counter() - t
+    return {"value": round(1.0 / dt, 4), "unit": "tokens/s", "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"1 sequence x 1 greedy decode step at context {ctx} (28 layers, vocab "
+                      f"151936), numpy oracle with BLAS on {os.cpu_count()} threads: {dt:.2f} s"}
+
+
+def run_reference(args) -> None:
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    O, w, kvs = _oracle_setup(args.ctx, 1)
+    kv = kvs[0]
+    times = []
+    for i in range(args.warmup + args.steps):
+        pos = args.ctx + i
+        t = time.perf_counter()
+        lg = O.forward_chunk(w, [100 + i], kv, pos, 1, True)
+        O.argmax_logits(lg)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t)
+    total = sum(times)
+    val = round(len(times) / total, 4)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * total / len(times), 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+        "data": "synthetic (random-init w8a8 weights, seeded int8 KV prefix)",
+        "config": {"workload": "config 4: batched paged greedy decode, 64 seqs x 2048-token "
+                               "prefix, 28 layers, vocab 151936 (decode tokens/s)",
+                   "sample_per_step": "1 sequence x 1 decode step"},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"per step 1 sequence x 1 greedy decode step at context "
+                                   f"{args.ctx}+i (28 layers, vocab 151936), numpy oracle port of "
+                                   f"tools/ref_qwen3.py, BLAS on {os.cpu_count()} threads"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)

@@ -1,0 +1,253 @@
+/*
+ * q3_ops.h — C ABI of the B200-native Qwen3 w8a8 forward path.
+ *
+ * One entry point per operator of the reference's operator API (kernels/*.h
+ * of mland2333/qwen3-tile-ops), plus its forward_chunk()/greedy-generate entry
+ * points (src/main_big.cpp) and a batched paged-decode extension.  Every
+ * function is `extern "C"`, takes plain pointers and sizes, enqueues work on the
+ * given CUDA stream (`cudaStream_t` passed as `void *`, NULL = legacy default
+ * stream) and returns a status code.  All data pointers inside views are
+ * DEVICE pointers.  Operators allocate nothing: where an operator needs scratch
+ * memory the caller passes a workspace whose size the matching *_workspace_bytes()
+ * query returns.
+ *
+ * Numerics follow the reference bit for bit (tools/ref_qwen3.py): int32 group
+ * partials, float32 steps rounded one at a time in the reference's order, and
+ * exp(x) = exp2(f32(x*log2e)) with a correctly rounded float32 exp2.
+ *
+ * Errors: the reference's operators return silently on unsupported shapes
+ * (group_gemm.h:47-49, lm_argmax.h:82); these return a non-zero status instead
+ * and enqueue nothing.
+ */
+#ifndef Q3_OPS_H
+#define Q3_OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* MatrixView dtype codes (kernels/config.h:86-90; tools/pqwf.py:28-33). */
+enum { Q3_DT_I8 = 0, Q3_DT_U8 = 1, Q3_DT_I32 = 2, Q3_DT_U32 = 3, Q3_DT_F32 = 4 };
+
+/* Status codes. */
+enum {
+  Q3_OK = 0,
+  Q3_ERR_NULL = 1,     /* a required view/pointer is null                     */
+  Q3_ERR_MODE = 2,     /* CTRL mode > 1 (main_big.cpp:346-348 returns 2)      */
+  Q3_ERR_SHAPE = 3,    /* sizes do not fit the operator                       */
+  Q3_ERR_DTYPE = 4,    /* view dtype code does not match the operand          */
+  Q3_ERR_ALIGN = 5,    /* pointer/stride alignment the kernels need is missing */
+  Q3_ERR_CUDA = 6,     /* a CUDA launch or call failed (q3_last_cuda_error)   */
+  Q3_ERR_CAPACITY = 7, /* workspace too small, or position beyond max_seq     */
+  Q3_ERR_ARCH = 8      /* device is not sm_100                                */
+};
+
+/* kernels/matrix.h:27-34 — a strided 2-D view; strides in BYTES. */
+typedef struct q3_view {
+  void *data;
+  int32_t row_bytes;
+  int32_t col_bytes;
+  uint32_t rows;
+  uint32_t cols;
+  uint8_t dtype;
+} q3_view;
+
+/* kernels/kv_pages.h:13-24 — paged KV cache: 32-token pages, logical->physical
+ * page table (device memory). */
+typedef struct q3_paged_kv {
+  void *k;                    /* [page][page_tokens][row_bytes] i8            */
+  void *v;
+  void *ks;                   /* [page][page_tokens][kv_heads] f32            */
+  void *vs;
+  const uint16_t *table;      /* logical page -> physical page (device)      */
+  uint32_t page_tokens;       /* 32                                          */
+  uint32_t page_bytes;        /* page_tokens * row_bytes                     */
+  uint32_t row_bytes;         /* kv_heads * head_dim                         */
+  uint32_t scale_page_bytes;  /* page_tokens * scale_row_bytes               */
+  uint32_t scale_row_bytes;   /* kv_heads * 4                                */
+} q3_paged_kv;
+
+/* ---- operators (kernels/*.h) -------------------------------------------- */
+
+/* kernels/rmsnorm.h:34-81 — out = x * rsqrt(mean(x^2)+eps) * w, row-wise. */
+int q3_rmsnorm_rows(const q3_view *x, const q3_view *w, const q3_view *out,
+                    float inv, void *stream);
+
+/* kernels/quant.h:89-138 — per-row, per-group_cols int8 quantisation:
+ * scale = absmax * (1/127), q = sat127(rne(x / scale)). */
+int q3_quant_rows_heads(const q3_view *x, const q3_view *qi8,
+                        const q3_view *scale, uint32_t group_cols, void *stream);
+
+/* kernels/embedding.h:99-168 — gather int8 rows by id, dequantise into tmp
+ * (the residual stream x), fused RMSNorm with w into out. */
+int q3_embedding_rmsnorm_rows(const q3_view *table, const q3_view *scale,
+                              const q3_view *ids, const q3_view *tmp,
+                              const q3_view *w, const q3_view *out, float inv,
+                              void *stream);
+
+/* kernels/group_gemm.h:27-222 — per-K-group w8a8 GEMM
+ *   out[m][n] = sum_g ((f32(A_g . B_g) * b_scale[n]) * a_scale[m][g])
+ * Epilogue by which optional views are non-null (same precedence as the
+ * reference): nw -> per-head RMSNorm(inv_hd)*nw + RoPE(cos, sin) + per-head
+ * int8 quant into q8/qs; else q8 -> per-head int8 quant into q8/qs; else
+ * add -> add += result (residual); else store into out.  The reference's
+ * NPU-register outputs (Acc* ao0..ao3) have no counterpart. */
+int q3_gemm_nt_group_store(const q3_view *a, const q3_view *a_scale,
+                           const q3_view *b, const q3_view *b_scale,
+                           const q3_view *out, uint32_t group_k,
+                           const q3_view *add, const q3_view *q8,
+                           const q3_view *qs, const q3_view *nw,
+                           const q3_view *cos, const q3_view *sin, float inv_hd,
+                           void *stream);
+
+/* kernels/swiglu_quant.h:164-255 — gate and up GEMMs (per group), SwiGLU,
+ * per-256-column int8 quant into s8/ss. */
+int q3_gemm_gate_up_swiglu_quant(const q3_view *a, const q3_view *a_scale,
+                                 const q3_view *wg, const q3_view *wgs,
+                                 const q3_view *wu, const q3_view *wus,
+                                 const q3_view *s8, const q3_view *ss,
+                                 uint32_t group_k, void *stream);
+
+/* kernels/attention_gqa.h:549-572 (+404-547) — GQA hd128 attention over a
+ * paged int8 KV cache, online softmax over 32-key blocks with P requantised
+ * per block; output quantised per head into o8/os. */
+int q3_attention_heads_gqa_tokscale_paged(const q3_view *q8,
+                                          const q3_view *q_scale,
+                                          const q3_paged_kv *kv,
+                                          uint32_t kv_len, const q3_view *o8,
+                                          const q3_view *os, int heads,
+                                          int kv_heads, int head_dim,
+                                          int causal, float qk_scale,
+                                          void *stream);
+
+/* kernels/kv_pages.h:63-93 — scatter contiguous K/V rows (+scales) into pages. */
+int q3_paged_kv_scatter(const q3_view *k, const q3_view *v, const q3_view *ks,
+                        const q3_view *vs, const q3_paged_kv *kv,
+                        uint32_t start_token, uint32_t rows, uint32_t kv_dim,
+                        uint32_t kv_heads, void *stream);
+
+/* kernels/kv_pages.h:98-131 — batch scatter: row r goes to tables[r] at
+ * tokens[r].  `tables` and `tokens` are HOST arrays of `rows` entries
+ * (rows <= 128); the page tables they point to are device memory. */
+int q3_paged_kv_scatter_batch(const q3_view *k, const q3_view *v,
+                              const q3_view *ks, const q3_view *vs,
+                              const q3_paged_kv *tables, const uint32_t *tokens,
+                              uint32_t rows, uint32_t kv_dim, uint32_t kv_heads,
+                              void *stream);
+
+/* kernels/lm_argmax.h:72-182 — lm_head per-group GEMM fused with a running
+ * (best, bidx) per row: in/out device arrays of a->rows entries, updated like
+ * the reference's `best < tmax` per-32-column-block rule (net effect: the
+ * first index of the row maximum replaces (best, bidx) when it exceeds best).
+ * Needs q3_gemm_nt_group_argmax_workspace_bytes(a->rows) bytes of workspace. */
+size_t q3_gemm_nt_group_argmax_workspace_bytes(uint32_t rows);
+int q3_gemm_nt_group_argmax(const q3_view *a, const q3_view *a_scale,
+                            const q3_view *b, const q3_view *b_scale,
+                            float *best, int32_t *bidx, uint32_t group_k,
+                            void *workspace, size_t workspace_bytes,
+                            void *stream);
+
+/* src/main_big.cpp:300-322 — greedy pick over a logits row by 32-column blocks
+ * (monotone float key); writes the id to *out_id (device). */
+int q3_argmax_logits(const q3_view *logits, int32_t *out_id, void *stream);
+
+/* ---- model level (src/main_big.cpp, tools/pqwf.py) ---------------------- */
+
+/* tools/pqwf.py:95-218 — model dimensions; q3_layout_compute fills `off` with
+ * the blob offsets of config/model_big.h (indices Q3_OFF_*). */
+enum {
+  Q3_OFF_IDS, Q3_OFF_CTRL, Q3_OFF_X, Q3_OFF_EMB, Q3_OFF_LM, Q3_OFF_NF,
+  Q3_OFF_COS, Q3_OFF_SIN, Q3_OFF_LAYERW_BASE, Q3_OFF_LAYERW_STRIDE,
+  Q3_OFF_LQ, Q3_OFF_LQ_SCALE, Q3_OFF_LK, Q3_OFF_LK_SCALE, Q3_OFF_LV,
+  Q3_OFF_LV_SCALE, Q3_OFF_LO, Q3_OFF_LO_SCALE, Q3_OFF_LG, Q3_OFF_LG_SCALE,
+  Q3_OFF_LU, Q3_OFF_LU_SCALE, Q3_OFF_LD, Q3_OFF_LD_SCALE,
+  Q3_OFF_LAYERN_BASE, Q3_OFF_LAYERN_STRIDE, Q3_OFF_N1, Q3_OFF_NQ, Q3_OFF_NK,
+  Q3_OFF_N2, Q3_OFF_LOGITS, Q3_OFF_BLOCK_END,
+  Q3_OFF_H, Q3_OFF_H8, Q3_OFF_HS, Q3_OFF_Q, Q3_OFF_K, Q3_OFF_V, Q3_OFF_Q8,
+  Q3_OFF_K8, Q3_OFF_V8, Q3_OFF_QS, Q3_OFF_KS, Q3_OFF_VS, Q3_OFF_ATTN,
+  Q3_OFF_O, Q3_OFF_O8, Q3_OFF_OS, Q3_OFF_G, Q3_OFF_U, Q3_OFF_SW, Q3_OFF_S8,
+  Q3_OFF_SS, Q3_OFF_ARGF, Q3_OFF_ARGI, Q3_OFF_KV_BASE, Q3_OFF_KV_STRIDE,
+  Q3_OFF_KV_VOFF, Q3_OFF_KV_SOFF, Q3_OFF_SCRATCH_END, Q3_OFF_COUNT
+};
+
+typedef struct q3_layout {
+  uint32_t hidden, layers, heads, kv_heads, head_dim, inter, vocab, seq, max_seq;
+  int64_t off[Q3_OFF_COUNT];
+} q3_layout;
+
+int q3_layout_compute(q3_layout *layout);
+
+/* LmHeadOut of main_big.cpp:142. */
+enum { Q3_LM_NONE = 0, Q3_LM_LOGITS = 1, Q3_LM_ARGMAX = 2 };
+
+/* Workspace (device) needed by q3_forward_chunk / q3_generate. */
+size_t q3_forward_workspace_bytes(const q3_layout *layout);
+
+/* src/main_big.cpp:145-296 — one prefill chunk or decode step over the blob
+ * (device copy of the pqwf blob).  pos = absolute position of the first row,
+ * rows <= layout->seq.  KV goes into the blob's per-layer cache through the
+ * reference's reversed page table (main_big.cpp:168-171). */
+int q3_forward_chunk(void *blob, const q3_layout *layout, uint32_t pos,
+                     uint32_t rows, int lm_out, int optimize_tail,
+                     void *workspace, size_t workspace_bytes, void *stream);
+
+/* src/main_big.cpp:332-369 — the greedy loop: reads CTRL [n_prompt, n_gen,
+ * max_seq, mode] from the blob (one 16-byte device->host read), then runs
+ * every chunk asynchronously, writing each picked id into ids[pos].
+ * Returns Q3_ERR_MODE for mode > 1. */
+int q3_generate(void *blob, const q3_layout *layout, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/* ---- batched paged decode (extension; kernels/kv_pages.h:98-131) --------- */
+
+/* A pool of 32-token KV pages for every layer, shared by many sequences.
+ * Page p of layer L: K at k + L*layer_stride + p*32*kv_width, its scales at
+ * ks + L*scale_layer_stride + p*32*kv_heads*4; V likewise. */
+typedef struct q3_kv_pool {
+  void *k, *v, *ks, *vs;
+  uint64_t layer_stride;        /* bytes between layers in k / v             */
+  uint64_t scale_layer_stride;  /* bytes between layers in ks / vs           */
+  uint32_t num_pages;
+} q3_kv_pool;
+
+/* One decode step for n_seqs independent sequences (one new token each):
+ * ids[s] at position pos[s] of sequence s, whose page table is
+ * tables[s*max_pages ...] (device).  Writes the greedy next id of every
+ * sequence to next_ids[s] (device).  Weights come from the blob. */
+size_t q3_decode_workspace_bytes(const q3_layout *layout, uint32_t n_seqs);
+int q3_decode_step_batch(void *blob, const q3_layout *layout,
+                         const q3_kv_pool *pool, const uint16_t *tables,
+                         uint32_t max_pages, const int32_t *ids,
+                         const int32_t *pos, uint32_t n_seqs, int32_t *next_ids,
+                         void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---- value ops (include/tile.h exp_/exp2 semantics; tests/guest/value_ops.cpp)
+ * out[i] = exp(x[i]) as the path computes it: exp2(f32(x * log2e))
+ * (tools/ref_qwen3.py:27-29), or out[i] = exp2(x[i]); both correctly rounded
+ * float32.  Element-wise over every element of a view (f32). */
+int q3_exp_rows(const q3_view *x, const q3_view *out, void *stream);
+int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream);
+
+/* ---- misc ---------------------------------------------------------------- */
+const char *q3_last_cuda_error(void);
+int q3_device_check(void); /* Q3_OK on an sm_100 device, else Q3_ERR_ARCH */
+
+/* Number of kernels this library has launched in this process (all threads). */
+uint64_t q3_launch_count(void);
+
+/* Kernel timing hook for benchmarks: while attached, the i-th launch of the
+ * named kernel family ("attention", "gemm") records cudaEvent_t start[i]
+ * before it and stop[i] after it on its own stream, for i < capacity.
+ * q3_timer_detach() returns how many launches were recorded. */
+int q3_timer_attach(const char *family, void *const *start_events,
+                    void *const *stop_events, int capacity);
+int q3_timer_detach(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q3_OPS_H */

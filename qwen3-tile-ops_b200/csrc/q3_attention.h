@@ -1,0 +1,31 @@
+// Internal attention interface (single sequence or a batch of sequences).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace q3 {
+
+struct AttnArgs {
+  const char *q8;      // [n_seqs*q_rows][heads*128] i8
+  long q_rb;
+  const char *qs;      // [n_seqs*q_rows][heads] f32
+  long qs_rb;
+  char *o8;
+  long o_rb;
+  char *os;
+  long os_rb;
+  const char *k, *v, *ks, *vs;   // page pool (this layer)
+  const uint16_t *table;         // [n_seqs][table_stride]
+  long table_stride;
+  uint32_t page_tokens, page_bytes, row_bytes, scale_page_bytes, scale_row_bytes;
+  int heads, kv_heads, q_rows;
+  int kv_len;                    // when kv_len_dev is null
+  const int *kv_len_dev;         // [n_seqs] per-sequence kv length
+  int causal;
+  float qk_scale;
+};
+
+int attention_launch(const AttnArgs &p, int n_seqs, cudaStream_t s);
+
+}  // namespace q3

@@ -1,0 +1,235 @@
+// Batched paged decode: one new token for each of n_seqs independent
+// sequences, every sequence with its own page table into a shared KV page
+// pool (kernels/kv_pages.h:98-131 semantics, tools/engine.py's PagePool
+// layout).  Per row the arithmetic is exactly forward_chunk's for rows = 1
+// (src/main_big.cpp:145-296): rows never interact, so batching them through
+// one GEMM is bit-identical to running the sequences one by one.
+#include "q3_attention.h"
+#include "q3_common.cuh"
+
+namespace {
+
+constexpr uint32_t kPT = 32;   // page tokens
+constexpr float kInvSqrt128 = 0.08838834764831845f;
+
+struct DecodeWs {
+  float *x, *h;          // [B][H]
+  int8_t *h8;            // [B][H]
+  float *hs;             // [B][H/256]
+  int8_t *q8, *o8;       // [B][QW]
+  float *qs, *os;        // [B][heads]
+  int8_t *k8, *v8;       // [B][KW] staging of the new K/V rows
+  float *ks, *vs;        // [B][kv_heads]
+  int8_t *s8;            // [B][I]
+  float *ss;             // [B][I/256]
+  float *cos, *sin;      // [B][64] rows at each sequence's position
+  int *kv_len;           // [B]
+  float *best;           // [B]
+  unsigned long long *keys;  // [B]
+  size_t total;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+DecodeWs carve(const q3_layout &L, uint32_t B, char *base) {
+  const size_t H = L.hidden, QW = L.heads * L.head_dim, KW = L.kv_heads * L.head_dim, I = L.inter;
+  DecodeWs w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
+  w.x = (float *)take(4 * B * H);
+  w.h = (float *)take(4 * B * H);
+  w.h8 = (int8_t *)take(B * H);
+  w.hs = (float *)take(4 * B * (H / 256));
+  w.q8 = (int8_t *)take(B * QW);
+  w.o8 = (int8_t *)take(B * QW);
+  w.qs = (float *)take(4 * B * L.heads);
+  w.os = (float *)take(4 * B * L.heads);
+  w.k8 = (int8_t *)take(B * KW);
+  w.v8 = (int8_t *)take(B * KW);
+  w.ks = (float *)take(4 * B * L.kv_heads);
+  w.vs = (float *)take(4 * B * L.kv_heads);
+  w.s8 = (int8_t *)take(B * I);
+  w.ss = (float *)take(4 * B * (I / 256));
+  w.cos = (float *)take(4 * B * (L.head_dim / 2));
+  w.sin = (float *)take(4 * B * (L.head_dim / 2));
+  w.kv_len = (int *)take(4 * B);
+  w.best = (float *)take(4 * B);
+  w.keys = (unsigned long long *)take(8 * B);
+  w.total = off;
+  return w;
+}
+
+q3_view v2(void *p, uint32_t rows, uint32_t cols, uint8_t dt) {
+  const int es = (dt == Q3_DT_I8 || dt == Q3_DT_U8) ? 1 : 4;
+  return q3_view{p, static_cast<int32_t>(cols * es), es, rows, cols, dt};
+}
+
+// rope rows at each sequence's position; kv_len = pos + 1; best = -3e38
+__global__ void k_decode_prep(const int32_t *pos, const float *cos_t, const float *sin_t, int half,
+                              float *cos, float *sin, int *kv_len, float *best,
+                              int32_t *next_ids, int B) {
+  const int s = blockIdx.x;
+  const int p = pos[s];
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    cos[s * half + j] = cos_t[p * half + j];
+    sin[s * half + j] = sin_t[p * half + j];
+  }
+  if (threadIdx.x == 0) {
+    kv_len[s] = p + 1;
+    best[s] = -3.0e38f;
+    next_ids[s] = 0;
+  }
+}
+
+// new K/V row of sequence s -> its page (tables[s][pos/32], slot pos%32)
+__global__ void k_decode_scatter(const int8_t *k8, const int8_t *v8, const float *ks,
+                                 const float *vs, const int32_t *pos, const uint16_t *tables,
+                                 uint32_t max_pages, char *pk, char *pv, char *pks, char *pvs,
+                                 int kw, int kvh) {
+  const int s = blockIdx.x;
+  const int p = pos[s];
+  const uint32_t page = tables[static_cast<size_t>(s) * max_pages + p / kPT], slot = p % kPT;
+  const size_t row = static_cast<size_t>(page) * kPT + slot;
+  for (int i = threadIdx.x; i < kw / 16; i += blockDim.x) {
+    reinterpret_cast<int4 *>(pk + row * kw)[i] = reinterpret_cast<const int4 *>(k8 + (size_t)s * kw)[i];
+    reinterpret_cast<int4 *>(pv + row * kw)[i] = reinterpret_cast<const int4 *>(v8 + (size_t)s * kw)[i];
+  }
+  for (int h = threadIdx.x; h < kvh; h += blockDim.x) {
+    reinterpret_cast<float *>(pks + row * kvh * 4)[h] = ks[s * kvh + h];
+    reinterpret_cast<float *>(pvs + row * kvh * 4)[h] = vs[s * kvh + h];
+  }
+}
+
+__global__ void k_keys_to_ids(const unsigned long long *keys, int32_t *next_ids, int B) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s < B) next_ids[s] = static_cast<int32_t>(0xffffffffu - static_cast<unsigned>(keys[s] & 0xffffffffu));
+}
+
+}  // namespace
+
+extern "C" size_t q3_decode_workspace_bytes(const q3_layout *L, uint32_t n_seqs) {
+  if (!L) return 0;
+  return carve(*L, n_seqs, nullptr).total;
+}
+
+extern "C" int q3_decode_step_batch(void *blob, const q3_layout *layout, const q3_kv_pool *pool,
+                                    const uint16_t *tables, uint32_t max_pages,
+                                    const int32_t *ids, const int32_t *pos, uint32_t n_seqs,
+                                    int32_t *next_ids, void *workspace, size_t workspace_bytes,
+                                    void *stream) {
+  if (!blob || !layout || !pool || !tables || !ids || !pos || !next_ids || !workspace)
+    return Q3_ERR_NULL;
+  const q3_layout &L = *layout;
+  // max_seq % 32 keeps every pqwf blob offset 16-byte aligned (the GEMMs load
+  // 16-byte vectors); head_dim 128 and 256-column groups are the path's shapes
+  if (L.head_dim != 128 || L.hidden % 256 || L.inter % 256 || L.max_seq % kPT) return Q3_ERR_SHAPE;
+  if (n_seqs == 0) return Q3_OK;
+  if (workspace_bytes < q3_decode_workspace_bytes(layout, n_seqs)) return Q3_ERR_CAPACITY;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256) return Q3_ERR_ALIGN;
+  if (!pool->k || !pool->v || !pool->ks || !pool->vs) return Q3_ERR_NULL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void *s = st;
+  const int64_t *o = L.off;
+  const uint32_t B = n_seqs, H = L.hidden, HD = L.head_dim, QW = L.heads * HD,
+                 KW = L.kv_heads * HD, I = L.inter, V = L.vocab, HALF = HD / 2;
+  char *bl = static_cast<char *>(blob);
+  DecodeWs w = carve(L, B, static_cast<char *>(workspace));
+
+  k_decode_prep<<<B, 64, 0, st>>>(pos, reinterpret_cast<const float *>(bl + o[Q3_OFF_COS]),
+                                  reinterpret_cast<const float *>(bl + o[Q3_OFF_SIN]), HALF, w.cos,
+                                  w.sin, w.kv_len, w.best, next_ids, B);
+  Q3_TRY(q3h::launch_status());
+
+  const q3_view x = v2(w.x, B, H, Q3_DT_F32), h = v2(w.h, B, H, Q3_DT_F32);
+  const q3_view h8 = v2(w.h8, B, H, Q3_DT_I8), hs = v2(w.hs, B, H / 256, Q3_DT_F32);
+  const q3_view q8 = v2(w.q8, B, QW, Q3_DT_I8), qs = v2(w.qs, B, L.heads, Q3_DT_F32);
+  const q3_view o8 = v2(w.o8, B, QW, Q3_DT_I8), os = v2(w.os, B, L.heads, Q3_DT_F32);
+  const q3_view k8 = v2(w.k8, B, KW, Q3_DT_I8), ks = v2(w.ks, B, L.kv_heads, Q3_DT_F32);
+  const q3_view v8 = v2(w.v8, B, KW, Q3_DT_I8), vs = v2(w.vs, B, L.kv_heads, Q3_DT_F32);
+  const q3_view s8 = v2(w.s8, B, I, Q3_DT_I8), ss = v2(w.ss, B, I / 256, Q3_DT_F32);
+  const q3_view cosv = v2(w.cos, B, HALF, Q3_DT_F32), sinv = v2(w.sin, B, HALF, Q3_DT_F32);
+  const q3_view idv = v2(const_cast<int32_t *>(ids), B, 1, Q3_DT_I32);
+  const q3_view emb = v2(bl + o[Q3_OFF_EMB], V, H, Q3_DT_I8);
+  const q3_view emb_s = v2(bl + o[Q3_OFF_EMB] + (int64_t)V * H, V, 1, Q3_DT_F32);
+  const q3_view lm = v2(bl + o[Q3_OFF_LM], V, H, Q3_DT_I8);
+  const q3_view lm_s = v2(bl + o[Q3_OFF_LM] + (int64_t)V * H, V, 1, Q3_DT_F32);
+  const q3_view nf = v2(bl + o[Q3_OFF_NF], H, 1, Q3_DT_F32);
+  const float inv_h = 1.0f / static_cast<float>(H), inv_hd = 1.0f / static_cast<float>(HD);
+
+  {
+    const q3_view n1_0 = v2(bl + o[Q3_OFF_N1], H, 1, Q3_DT_F32);
+    Q3_TRY(q3_embedding_rmsnorm_rows(&emb, &emb_s, &idv, &x, &n1_0, &h, inv_h, s));
+  }
+  for (uint32_t Li = 0; Li < L.layers; ++Li) {
+    char *lw = bl + o[Q3_OFF_LQ] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERW_STRIDE];
+    char *ln = bl + o[Q3_OFF_N1] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERN_STRIDE];
+    auto W = [&](int key, uint32_t r, uint32_t c) { return v2(lw + (o[key] - o[Q3_OFF_LQ]), r, c, Q3_DT_I8); };
+    auto S = [&](int key, uint32_t r) { return v2(lw + (o[key] - o[Q3_OFF_LQ]), r, 1, Q3_DT_F32); };
+    const q3_view wq = W(Q3_OFF_LQ, QW, H), wk = W(Q3_OFF_LK, KW, H), wv = W(Q3_OFF_LV, KW, H);
+    const q3_view wo = W(Q3_OFF_LO, H, QW), wg = W(Q3_OFF_LG, I, H), wu = W(Q3_OFF_LU, I, H);
+    const q3_view wd = W(Q3_OFF_LD, H, I);
+    const q3_view wqs = S(Q3_OFF_LQ_SCALE, QW), wks = S(Q3_OFF_LK_SCALE, KW);
+    const q3_view wvs = S(Q3_OFF_LV_SCALE, KW), wos = S(Q3_OFF_LO_SCALE, H);
+    const q3_view wgs = S(Q3_OFF_LG_SCALE, I), wus = S(Q3_OFF_LU_SCALE, I);
+    const q3_view wds = S(Q3_OFF_LD_SCALE, H);
+    const q3_view n1 = v2(ln, H, 1, Q3_DT_F32);
+    const q3_view nq = v2(ln + (o[Q3_OFF_NQ] - o[Q3_OFF_N1]), HD, 1, Q3_DT_F32);
+    const q3_view nk = v2(ln + (o[Q3_OFF_NK] - o[Q3_OFF_N1]), HD, 1, Q3_DT_F32);
+    const q3_view n2 = v2(ln + (o[Q3_OFF_N2] - o[Q3_OFF_N1]), H, 1, Q3_DT_F32);
+    char *pk = static_cast<char *>(pool->k) + Li * pool->layer_stride;
+    char *pv = static_cast<char *>(pool->v) + Li * pool->layer_stride;
+    char *pks = static_cast<char *>(pool->ks) + Li * pool->scale_layer_stride;
+    char *pvs = static_cast<char *>(pool->vs) + Li * pool->scale_layer_stride;
+
+    if (Li != 0) Q3_TRY(q3_rmsnorm_rows(&x, &n1, &h, inv_h, s));
+    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wv, &wvs, nullptr, 256, nullptr, &v8, &vs, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wk, &wks, nullptr, 256, nullptr, &k8, &ks, &nk,
+                                  &cosv, &sinv, inv_hd, s));
+    k_decode_scatter<<<B, 64, 0, st>>>(w.k8, w.v8, w.ks, w.vs, pos, tables, max_pages, pk, pv, pks,
+                                       pvs, KW, L.kv_heads);
+    Q3_TRY(q3h::launch_status());
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wq, &wqs, nullptr, 256, nullptr, &q8, &qs, &nq, &cosv,
+                                  &sinv, inv_hd, s));
+    q3::AttnArgs a{};
+    a.q8 = reinterpret_cast<const char *>(w.q8);
+    a.q_rb = QW;
+    a.qs = reinterpret_cast<const char *>(w.qs);
+    a.qs_rb = 4 * L.heads;
+    a.o8 = reinterpret_cast<char *>(w.o8);
+    a.o_rb = QW;
+    a.os = reinterpret_cast<char *>(w.os);
+    a.os_rb = 4 * L.heads;
+    a.k = pk;
+    a.v = pv;
+    a.ks = pks;
+    a.vs = pvs;
+    a.table = tables;
+    a.table_stride = max_pages;
+    a.page_tokens = kPT;
+    a.page_bytes = kPT * KW;
+    a.row_bytes = KW;
+    a.scale_page_bytes = kPT * 4 * L.kv_heads;
+    a.scale_row_bytes = 4 * L.kv_heads;
+    a.heads = L.heads;
+    a.kv_heads = L.kv_heads;
+    a.q_rows = 1;
+    a.kv_len = 0;
+    a.kv_len_dev = w.kv_len;
+    a.causal = 1;
+    a.qk_scale = kInvSqrt128;
+    Q3_TRY(q3::attention_launch(a, B, st));
+    Q3_TRY(q3_gemm_nt_group_store(&o8, &os, &wo, &wos, nullptr, 128, &x, nullptr, nullptr, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+    Q3_TRY(q3_rmsnorm_rows(&x, &n2, &h, inv_h, s));
+    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    Q3_TRY(q3_gemm_gate_up_swiglu_quant(&h8, &hs, &wg, &wgs, &wu, &wus, &s8, &ss, 256, s));
+    Q3_TRY(q3_gemm_nt_group_store(&s8, &ss, &wd, &wds, nullptr, 256, &x, nullptr, nullptr, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+  }
+  Q3_TRY(q3_rmsnorm_rows(&x, &nf, &h, inv_h, s));
+  Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+  Q3_TRY(q3_gemm_nt_group_argmax(&h8, &hs, &lm, &lm_s, w.best, next_ids, 256, w.keys, 8 * B, s));
+  return Q3_OK;
+}

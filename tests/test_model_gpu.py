@@ -1,0 +1,185 @@
+"""Model-level parity on the GPU: the greedy loop (q3_generate) and one chunk
+(q3_forward_chunk) against the golden vectors of the reference's own mirror,
+stage by stage like the reference's tools/compare.py; the batched paged decode
+(q3_decode_step_batch) against the oracle run one sequence at a time."""
+
+from __future__ import annotations
+
+import ctypes as C
+import hashlib
+
+import numpy as np
+import pytest
+
+from conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+F = np.float32
+
+from oracle import q3_oracle as O  # noqa: E402
+from oracle import synth  # noqa: E402
+
+
+def same_bits(a, b, what=""):
+    a, b = np.asarray(a), np.asarray(b)
+    assert a.shape == b.shape, (what, a.shape, b.shape)
+    if a.dtype == np.float32:
+        bad = np.count_nonzero(a.view(np.uint32) != np.asarray(b, F).view(np.uint32))
+    else:
+        bad = np.count_nonzero(a != b)
+    assert bad == 0, f"{what}: {bad}/{a.size} elements differ"
+
+
+@pytest.fixture(scope="module")
+def cfg1(q3):
+    assert torch.cuda.is_available()
+    w = synth.build_model(synth.Shape(layers=1, vocab=1024))
+    dims = q3.model.Dims(layers=1, vocab=1024)
+    bm = q3.model.BlobModel(dims).load_weights(w)
+    return w, bm
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_config1_generate(cfg1, mode):
+    """Config 1: 40-token prompt (32 + 8 rows), 2 greedy tokens; mode 0 is the
+    fused lm_head+argmax production path, mode 1 writes logits."""
+    w, bm = cfg1
+    g = load_golden("model_cfg1_cr.npz")
+    ids = synth.config1_ids()
+    got = bm.generate(ids, 40, 2, mode=mode)
+    assert got == [int(v) for v in g["generated"]]
+    # KV cache of the (only) layer, un-paged through the reversed table
+    k8, ks, v8, vs = bm.kv_layer(0)
+    last = g["c3_kc"].shape[0]
+    same_bits(k8[:last], g["c3_kc"], "kc")
+    same_bits(ks[:last], g["c3_ks"], "ks")
+    same_bits(v8[:last], g["c3_vc"], "vc")
+    same_bits(vs[:last], g["c3_vs"], "vs")
+    # last step (pos 41, 1 row): stage buffers left in the blob
+    for st, key, shape, dt in (("x", "kX", (1, 1024), F), ("s8", "kS8", (1, 3072), np.int8),
+                               ("ss", "kSS", (1, 12), F), ("o8", "kO8", (1, 2048), np.int8),
+                               ("os", "kOS", (1, 16), F)):
+        same_bits(bm.read(key, shape, dt), g[f"c3_{st}"], st)
+    logits = g["c3_logits"].reshape(-1)
+    if mode == 1:
+        same_bits(bm.read("kLOGITS", (1, 1024), F), g["c3_logits"], "logits")
+    else:
+        argf = bm.read("kARGF", (1,), F)
+        argi = bm.read("kARGI", (1,), np.int32)
+        same_bits(argf, logits.max(keepdims=True), "argf")
+        assert int(argi[0]) == int(np.argmax(logits))
+
+
+def test_config1_forward_chunk_stages(cfg1, q3):
+    """The 8-row prompt chunk (pos 32) after the 32-row one, non-fused: every
+    materialised stage of the last layer equals the golden record."""
+    w, bm = cfg1
+    g = load_golden("model_cfg1_cr.npz")
+    ids = [int(v) for v in g["ids"]]
+    bm.set_ids(ids)
+    bm.forward_chunk(0, 32, q3.model.LM_NONE, False)
+    bm.forward_chunk(32, 8, q3.model.LM_LOGITS, False)
+    torch.cuda.synchronize()
+    r = 8
+    for st, key, shape, dt in (("x", "kX", (r, 1024), F), ("h", "kH", (r, 1024), F),
+                               ("h8", "kH8", (r, 1024), np.int8), ("hs", "kHS", (r, 4), F),
+                               ("o8", "kO8", (r, 2048), np.int8), ("os", "kOS", (r, 16), F),
+                               ("s8", "kS8", (r, 3072), np.int8), ("ss", "kSS", (r, 12), F)):
+        same_bits(bm.read(key, shape, dt), g[f"c1_{st}"], st)
+    # q8/qs rows 1.. (row 0 is the final-norm scratch, compare.py:197-205)
+    same_bits(bm.read("kQ8", (r, 2048), np.int8)[1:], g["c1_q8"][1:], "q8")
+    same_bits(bm.read("kQS", (r, 16), F)[1:], g["c1_qs"][1:], "qs")
+    same_bits(bm.read("kLOGITS", (1, 1024), F), g["c1_logits"], "logits")
+    # first chunk's int8 stages went into the KV cache
+    k8, ks, v8, vs = bm.kv_layer(0)
+    same_bits(k8[:32], g["c0_kc"][:32], "kc0")
+    same_bits(v8[:32], g["c0_vc"][:32], "vc0")
+
+
+def test_config3_full_shape_generate(q3):
+    """Config 3: 28 layers, vocab 151936, 32-token seeded prompt, 6 greedy
+    tokens (fused path) and the final logits of the non-fused path."""
+    g = load_golden("model_cfg3_cr.npz")
+    w = synth.build_model(synth.Shape())
+    assert synth.weights_digest(w) == str(g["digest"])
+    bm = q3.model.BlobModel(q3.model.Dims()).load_weights(w)
+    ids = [int(v) for v in np.random.default_rng(1).integers(0, 151936, 32)]
+    assert bm.generate(ids, 32, 6, mode=0) == [int(v) for v in g["generated"]]
+    assert bm.generate(ids, 32, 6, mode=1) == [int(v) for v in g["generated"]]
+    lg = bm.read("kLOGITS", (1, 151936), F)
+    assert hashlib.sha256(np.ascontiguousarray(lg).tobytes()).hexdigest() == str(g["logits_sha"])
+
+
+# ---------------------------------------------------------------- batched decode
+def _decode_case(q3, layers, vocab, lens, seed=0):
+    """Prefill each sequence on the oracle, load its KV into a shared page
+    pool under a shuffled page table, run ONE batched decode step on the GPU
+    and the oracle per sequence; return both."""
+    shape = synth.Shape(layers=layers, vocab=vocab, max_seq=(max(lens) + 64 + 31) // 32 * 32)
+    w = synth.build_model(shape)
+    rng = np.random.default_rng(seed)
+    B = len(lens)
+    max_pages = (shape.max_seq + 31) // 32
+    total_pages = B * max_pages
+    perm = rng.permutation(total_pages)
+    tables = perm.reshape(B, max_pages).astype(np.uint16)
+    kw = 8 * 128
+    pk = np.zeros((layers, total_pages, 32, kw), np.int8)
+    pv = np.zeros_like(pk)
+    pks = np.zeros((layers, total_pages, 32, 8), F)
+    pvs = np.zeros_like(pks)
+    ids_now, want_ids, want_kv = [], [], []
+    for s, n in enumerate(lens):
+        prompt = [int(v) for v in rng.integers(0, vocab, n)]
+        kv = O.KV.empty(w, shape.max_seq)
+        pos = 0
+        while pos < n:                       # oracle prefill in 32-row chunks
+            rows = min(32, n - pos)
+            O.forward_chunk(w, prompt[pos:pos + rows], kv, pos, rows, False)
+            pos += rows
+        for L in range(layers):
+            for t in range(n):
+                p, sl = tables[s, t // 32], t % 32
+                pk[L, p, sl], pv[L, p, sl] = kv.k8[L][t], kv.v8[L][t]
+                pks[L, p, sl], pvs[L, p, sl] = kv.ks[L][t], kv.vs[L][t]
+        tok = int(rng.integers(0, vocab))
+        ids_now.append(tok)
+        lg = O.forward_chunk(w, [tok], kv, n, 1, True)
+        want_ids.append(O.argmax_logits(lg))
+        want_kv.append(kv)
+    dims = q3.model.Dims(layers=layers, vocab=vocab, max_seq=shape.max_seq)
+    bm = q3.model.BlobModel(dims).load_weights(w)
+    d = {k: torch.from_numpy(v).cuda() for k, v in
+         (("pk", pk), ("pv", pv), ("pks", pks), ("pvs", pvs))}
+    pool = q3._lib.KVPool(d["pk"].data_ptr(), d["pv"].data_ptr(), d["pks"].data_ptr(),
+                          d["pvs"].data_ptr(), total_pages * 32 * kw, total_pages * 32 * 8 * 4,
+                          total_pages)
+    tab = torch.from_numpy(tables.view(np.int16)).cuda()
+    ids_d = torch.tensor(ids_now, dtype=torch.int32, device="cuda")
+    pos_d = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    nxt = torch.zeros(B, dtype=torch.int32, device="cuda")
+    lib = q3._lib.lib()
+    wsb = lib.q3_decode_workspace_bytes(C.byref(bm.L), B)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
+        bm.blob.data_ptr(), C.byref(bm.L), C.byref(pool), tab.data_ptr(), max_pages,
+        ids_d.data_ptr(), pos_d.data_ptr(), B, nxt.data_ptr(), ws.data_ptr(), wsb,
+        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return (nxt.cpu().numpy(), want_ids, {k: v.cpu().numpy() for k, v in d.items()}, tables,
+            want_kv)
+
+
+@pytest.mark.parametrize("layers,vocab,lens", [(1, 1024, [5, 40, 64, 33]),
+                                               (2, 4096, [100, 1, 31, 32, 250])])
+def test_decode_step_batch(q3, layers, vocab, lens):
+    got, want, pool, tables, kvs = _decode_case(q3, layers, vocab, lens)
+    assert list(got) == want
+    for s, n in enumerate(lens):          # the new K/V row of every layer
+        p, sl = tables[s, n // 32], n % 32
+        for L in range(layers):
+            assert np.array_equal(pool["pk"][L, p, sl], kvs[s].k8[L][n])
+            assert np.array_equal(pool["pv"][L, p, sl], kvs[s].v8[L][n])
+            same_bits(pool["pks"][L, p, sl], kvs[s].ks[L][n])
+            same_bits(pool["pvs"][L, p, sl], kvs[s].vs[L][n])
