@@ -150,6 +150,22 @@ int q3_gemm_nt_group_argmax(const q3_view *a, const q3_view *a_scale,
                             void *workspace, size_t workspace_bytes,
                             void *stream);
 
+/* No counterpart in the reference: the same lm_head + argmax as
+ * q3_gemm_nt_group_argmax, for callers that cannot call cudaMalloc (a host
+ * that only owns one fixed, pre-planned device buffer, or a serving loop that
+ * must keep allocation calls, which can synchronize the device, off its hot
+ * path).  It allocates nothing: its scratch is a built-in device array of
+ * Q3_NOALLOC_ARGMAX_MAX_ROWS keys (8 bytes each), one per device, shared by
+ * every call.  More rows -> Q3_ERR_CAPACITY.  Each call clears the keys it
+ * uses; calls that overlap on the GPU race on the array.  The first call on a
+ * device looks the array's address up (cudaGetSymbolAddress) with that device
+ * current: make it before any stream capture. */
+#define Q3_NOALLOC_ARGMAX_MAX_ROWS 4096
+int q3_gemm_nt_group_argmax_noalloc(const q3_view *a, const q3_view *a_scale,
+                                    const q3_view *b, const q3_view *b_scale,
+                                    float *best, int32_t *bidx, uint32_t group_k,
+                                    void *stream);
+
 /* src/main_big.cpp:300-322 — greedy pick over a logits row by 32-column blocks
  * (monotone float key); writes the id to *out_id (device). */
 int q3_argmax_logits(const q3_view *logits, int32_t *out_id, void *stream);

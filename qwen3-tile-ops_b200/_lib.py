@@ -77,6 +77,8 @@ SIGS = {
     "q3_gemm_nt_group_argmax_workspace_bytes": [C.c_uint32],
     "q3_gemm_nt_group_argmax": [VP, VP, VP, VP, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p,
                                 C.c_size_t, C.c_void_p],
+    "q3_gemm_nt_group_argmax_noalloc": [VP, VP, VP, VP, C.c_void_p, C.c_void_p, C.c_uint32,
+                                        C.c_void_p],
     "q3_argmax_logits": [VP, C.c_void_p, C.c_void_p],
     "q3_layout_compute": [C.POINTER(Layout)],
     "q3_forward_workspace_bytes": [C.POINTER(Layout)],

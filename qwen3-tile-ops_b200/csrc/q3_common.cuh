@@ -111,6 +111,7 @@ __device__ __forceinline__ float i2f_small(int v) {
 namespace q3h {
 
 const char *set_cuda_error(cudaError_t e);
+void set_error_message(const char *msg);   // text returned by q3_last_cuda_error
 int launch_argmax_row(const float *row, int n, int32_t *out_id, cudaStream_t s);
 void count_launch();
 

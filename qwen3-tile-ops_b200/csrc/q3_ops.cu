@@ -222,6 +222,7 @@ const char *set_cuda_error(cudaError_t e) {
   snprintf(g_err, sizeof g_err, "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
   return g_err;
 }
+void set_error_message(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
 }  // namespace q3h
 
 static inline long vec_stride(const q3_view *v) {
