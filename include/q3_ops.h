@@ -123,6 +123,19 @@ int q3_attention_heads_gqa_tokscale_paged(const q3_view *q8,
                                           int causal, float qk_scale,
                                           void *stream);
 
+/* Batch of decode rows (extension of the operator above with the per-request
+ * page tables of kernels/kv_pages.h:98-131): row s of q8/q_scale is the one new
+ * query row of sequence s, which sees keys 0..kv_len[s]-1 of its own table
+ * tables[s*max_pages ...] (device uint16) in the shared pool `kv` (kv->table is
+ * ignored; pages 0..num_pages-1).  kv_len is a device int32 array.  Output per
+ * head into o8/os exactly as the operator above computes it for that row. */
+int q3_attention_decode_batch(const q3_view *q8, const q3_view *q_scale,
+                              const q3_paged_kv *kv, uint32_t num_pages,
+                              const uint16_t *tables, uint32_t max_pages,
+                              const int32_t *kv_len, uint32_t n_seqs,
+                              const q3_view *o8, const q3_view *os, int heads,
+                              int kv_heads, float qk_scale, void *stream);
+
 /* kernels/kv_pages.h:63-93 — scatter contiguous K/V rows (+scales) into pages. */
 int q3_paged_kv_scatter(const q3_view *k, const q3_view *v, const q3_view *ks,
                         const q3_view *vs, const q3_paged_kv *kv,
@@ -250,6 +263,11 @@ int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream);
 /* ---- misc ---------------------------------------------------------------- */
 const char *q3_last_cuda_error(void);
 int q3_device_check(void); /* Q3_OK on an sm_100 device, else Q3_ERR_ARCH */
+
+/* Device-side error word of the library's kernels (0 = none; bit 0: a bounded
+ * wait on a TMA pipeline barrier timed out and the kernel gave up).  Reading
+ * synchronises with the device and clears the word; -1 if it cannot be read. */
+int q3_device_status(void);
 
 /* Number of kernels this library has launched in this process (all threads). */
 uint64_t q3_launch_count(void);

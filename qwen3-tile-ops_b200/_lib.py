@@ -70,6 +70,9 @@ SIGS = {
     "q3_attention_heads_gqa_tokscale_paged": [VP, VP, C.POINTER(PagedKV), C.c_uint32, VP, VP,
                                               C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                               C.c_void_p],
+    "q3_attention_decode_batch": [VP, VP, C.POINTER(PagedKV), C.c_uint32, C.c_void_p, C.c_uint32,
+                                  C.c_void_p, C.c_uint32, VP, VP, C.c_int, C.c_int, C.c_float,
+                                  C.c_void_p],
     "q3_paged_kv_scatter": [VP, VP, VP, VP, C.POINTER(PagedKV), C.c_uint32, C.c_uint32,
                             C.c_uint32, C.c_uint32, C.c_void_p],
     "q3_paged_kv_scatter_batch": [VP, VP, VP, VP, C.POINTER(PagedKV), C.POINTER(C.c_uint32),
@@ -94,6 +97,7 @@ SIGS = {
     "q3_last_cuda_error": [],
     "q3_device_check": [],
     "q3_launch_count": [],
+    "q3_device_status": [],
     "q3_timer_attach": [C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int],
     "q3_timer_detach": [],
 }

@@ -225,3 +225,82 @@ extern "C" int q3_attention_heads_gqa_tokscale_paged(const q3_view *q8, const q3
   p.qk_scale = qk_scale;
   return attention_launch(p, 1, (cudaStream_t)stream);
 }
+
+extern "C" int q3_attention_decode_batch(const q3_view *q8, const q3_view *q_scale,
+                                         const q3_paged_kv *kv, uint32_t num_pages,
+                                         const uint16_t *tables, uint32_t max_pages,
+                                         const int32_t *kv_len, uint32_t n_seqs,
+                                         const q3_view *o8, const q3_view *os, int heads,
+                                         int kv_heads, float qk_scale, void *stream) {
+  Q3_TRY(check_view(q8, Q3_DT_I8, 4));
+  Q3_TRY(check_view(q_scale, Q3_DT_F32));
+  Q3_TRY(check_view(o8, Q3_DT_I8, 4));
+  Q3_TRY(check_view(os, Q3_DT_F32));
+  if (!kv || !kv->k || !kv->v || !kv->ks || !kv->vs || !tables || !kv_len) return Q3_ERR_NULL;
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > 16 || max_pages == 0)
+    return Q3_ERR_SHAPE;
+  if (q8->rows < n_seqs || o8->rows < n_seqs || q8->cols < (uint32_t)(heads * 128) ||
+      o8->cols < (uint32_t)(heads * 128) || q_scale->cols < (uint32_t)heads ||
+      os->cols < (uint32_t)heads ||
+      (n_seqs > 1 && (q_scale->rows < n_seqs || os->rows < n_seqs)))
+    return Q3_ERR_SHAPE;
+  if (kv->page_tokens == 0 || kv->row_bytes < (uint32_t)(kv_heads * 128) ||
+      kv->scale_row_bytes < (uint32_t)(kv_heads * 4))
+    return Q3_ERR_SHAPE;
+  if (kv->page_bytes % 16 || kv->row_bytes % 16 || reinterpret_cast<uintptr_t>(kv->k) % 16 ||
+      reinterpret_cast<uintptr_t>(kv->v) % 16 || kv->scale_page_bytes % 4 ||
+      kv->scale_row_bytes % 4)
+    return Q3_ERR_ALIGN;
+  if (n_seqs == 0) return Q3_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (heads == 2 * kv_heads && kv->page_tokens == 32 && num_pages > 0) {
+    DecodeAttnArgs d{};
+    d.q8 = (const char *)q8->data;
+    d.q_rb = q8->row_bytes;
+    d.qs = (const char *)q_scale->data;
+    d.qs_rb = q_scale->row_bytes;
+    d.o8 = (char *)o8->data;
+    d.o_rb = o8->row_bytes;
+    d.os = (char *)os->data;
+    d.os_rb = os->row_bytes;
+    d.ks = (const char *)kv->ks;
+    d.vs = (const char *)kv->vs;
+    d.table = tables;
+    d.table_stride = max_pages;
+    d.page_bytes = kv->page_bytes;
+    d.row_bytes = kv->row_bytes;
+    d.scale_page_bytes = kv->scale_page_bytes;
+    d.scale_row_bytes = kv->scale_row_bytes;
+    d.kv_len = kv_len;
+    d.qk_scale = qk_scale;
+    return attention_decode_launch(d, kv->k, kv->v, num_pages, kv_heads, n_seqs, s);
+  }
+  AttnArgs p{};
+  p.q8 = (const char *)q8->data;
+  p.q_rb = q8->row_bytes;
+  p.qs = (const char *)q_scale->data;
+  p.qs_rb = q_scale->row_bytes;
+  p.o8 = (char *)o8->data;
+  p.o_rb = o8->row_bytes;
+  p.os = (char *)os->data;
+  p.os_rb = os->row_bytes;
+  p.k = (const char *)kv->k;
+  p.v = (const char *)kv->v;
+  p.ks = (const char *)kv->ks;
+  p.vs = (const char *)kv->vs;
+  p.table = tables;
+  p.table_stride = max_pages;
+  p.page_tokens = kv->page_tokens;
+  p.page_bytes = kv->page_bytes;
+  p.row_bytes = kv->row_bytes;
+  p.scale_page_bytes = kv->scale_page_bytes;
+  p.scale_row_bytes = kv->scale_row_bytes;
+  p.heads = heads;
+  p.kv_heads = kv_heads;
+  p.q_rows = 1;
+  p.kv_len = 0;
+  p.kv_len_dev = kv_len;
+  p.causal = 1;
+  p.qk_scale = qk_scale;
+  return attention_launch(p, n_seqs, s);
+}

@@ -28,4 +28,27 @@ struct AttnArgs {
 
 int attention_launch(const AttnArgs &p, int n_seqs, cudaStream_t s);
 
+// Decode attention: one query row per sequence, GQA group of 2, head_dim 128,
+// 32-token pages of a page pool (q3_attention_decode.cu).
+struct DecodeAttnArgs {
+  const char *q8;      // [n_seqs][heads*128] i8
+  long q_rb;
+  const char *qs;      // [n_seqs][heads] f32
+  long qs_rb;
+  char *o8;
+  long o_rb;
+  char *os;
+  long os_rb;
+  const char *ks, *vs;           // per-head scale pools of this layer
+  const uint16_t *table;         // [n_seqs][table_stride]
+  long table_stride;
+  uint32_t page_bytes, row_bytes, scale_page_bytes, scale_row_bytes;
+  const int *kv_len;             // [n_seqs]
+  float qk_scale;
+  uint32_t num_pages;            // pages in the pool (page indices are checked)
+};
+
+int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const void *v_pool,
+                            uint32_t num_pages, int kv_heads, int n_seqs, cudaStream_t s);
+
 }  // namespace q3

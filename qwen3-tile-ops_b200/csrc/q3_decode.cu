@@ -192,6 +192,28 @@ extern "C" int q3_decode_step_batch(void *blob, const q3_layout *layout, const q
     Q3_TRY(q3h::launch_status());
     Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wq, &wqs, nullptr, 256, nullptr, &q8, &qs, &nq, &cosv,
                                   &sinv, inv_hd, s));
+    if (L.heads == 2 * L.kv_heads && pool->num_pages > 0) {
+      q3::DecodeAttnArgs d{};
+      d.q8 = reinterpret_cast<const char *>(w.q8);
+      d.q_rb = QW;
+      d.qs = reinterpret_cast<const char *>(w.qs);
+      d.qs_rb = 4 * L.heads;
+      d.o8 = reinterpret_cast<char *>(w.o8);
+      d.o_rb = QW;
+      d.os = reinterpret_cast<char *>(w.os);
+      d.os_rb = 4 * L.heads;
+      d.ks = pks;
+      d.vs = pvs;
+      d.table = tables;
+      d.table_stride = max_pages;
+      d.page_bytes = kPT * KW;
+      d.row_bytes = KW;
+      d.scale_page_bytes = kPT * 4 * L.kv_heads;
+      d.scale_row_bytes = 4 * L.kv_heads;
+      d.kv_len = w.kv_len;
+      d.qk_scale = kInvSqrt128;
+      Q3_TRY(q3::attention_decode_launch(d, pk, pv, pool->num_pages, L.kv_heads, B, st));
+    } else {
     q3::AttnArgs a{};
     a.q8 = reinterpret_cast<const char *>(w.q8);
     a.q_rb = QW;
@@ -220,6 +242,7 @@ extern "C" int q3_decode_step_batch(void *blob, const q3_layout *layout, const q
     a.causal = 1;
     a.qk_scale = kInvSqrt128;
     Q3_TRY(q3::attention_launch(a, B, st));
+    }
     Q3_TRY(q3_gemm_nt_group_store(&o8, &os, &wo, &wos, nullptr, 128, &x, nullptr, nullptr, nullptr,
                                   nullptr, nullptr, 0.0f, s));
     Q3_TRY(q3_rmsnorm_rows(&x, &n2, &h, inv_h, s));

@@ -122,6 +122,17 @@ def attention_heads_gqa_tokscale_paged(q8, q_scale, kv: PagedKV, kv_len: int, o8
                                                       1 if causal else 0, qk_scale, _s(stream)))
 
 
+def attention_decode_batch(q8, q_scale, kv: PagedKV, num_pages: int, tables: torch.Tensor,
+                           max_pages: int, kv_len: torch.Tensor, n_seqs: int, o8, os,
+                           heads: int, kv_heads: int, qk_scale: float, stream=None) -> None:
+    """One decode row per sequence over a shared page pool (per-sequence tables)."""
+    check("q3_attention_decode_batch",
+          lib().q3_attention_decode_batch(_v(q8), _v(q_scale), C.byref(kv), num_pages,
+                                          tables.data_ptr(), max_pages, kv_len.data_ptr(),
+                                          n_seqs, _v(o8), _v(os), heads, kv_heads, qk_scale,
+                                          _s(stream)))
+
+
 def paged_kv_scatter(k, v, ks, vs, kv: PagedKV, start_token: int, rows: int, kv_dim: int,
                      kv_heads: int, stream=None) -> None:
     check("q3_paged_kv_scatter",

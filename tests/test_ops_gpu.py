@@ -217,7 +217,8 @@ def test_exp_correctly_rounded(ops):
            (rng.standard_normal(1 << 20) * 30).astype(F),
            rng.uniform(-150, 128, 1 << 20).astype(F),
            (rng.standard_normal(1 << 18) * 1e-6).astype(F)]
-    x = np.concatenate(pts).reshape(-1, 64)
+    x = np.concatenate(pts)
+    x = np.concatenate([x, np.zeros((-x.size) % 64, F)]).reshape(-1, 64)
     y = torch.zeros(x.shape, dtype=torch.float32, device="cuda")
     ops.exp2_rows(dev(x), y)
     same_bits(host(y), exp2_cr(x))
@@ -368,3 +369,51 @@ def test_paged_kv_scatter_and_batch(ops):
     hk = host(pk)
     assert np.array_equal(hk[1], K[:32]) and np.array_equal(hk[0, :8], K[32:])
     same_bits(host(pvs)[0, :8], VS[32:])
+
+
+# ---------------------------------------------------------------- decode batch
+@pytest.mark.parametrize("lens", [[1, 31, 32, 33, 100], [2049, 300, 64, 4100, 5],
+                                  [2112] * 8])
+def test_attention_decode_batch(ops, q3, lens):
+    """One decode row per sequence over a shared pool with shuffled per-sequence
+    tables (the TMA kernel; chunks of 2048 keys are crossed by 2049 and 4100)."""
+    rng = np.random.default_rng(sum(lens))
+    heads, kvh, kw = 16, 8, 1024
+    B = len(lens)
+    max_pages = max((n + 31) // 32 for n in lens) + 1
+    pages = B * max_pages + 3
+    perm = rng.permutation(pages)[:B * max_pages].reshape(B, max_pages).astype(np.uint16)
+    pk = rng.integers(-127, 128, (pages, 32, kw)).astype(np.int8)
+    pv = rng.integers(-127, 128, (pages, 32, kw)).astype(np.int8)
+    pks = rng.uniform(1e-3, 1e-2, (pages, 32, kvh)).astype(F)
+    pvs = rng.uniform(1e-3, 1e-2, (pages, 32, kvh)).astype(F)
+    pks[:, 20:] = np.nan          # garbage past the end of a partial page must not leak
+    pvs[:, 20:] = np.inf
+    q8 = rng.integers(-127, 128, (B, heads * 128)).astype(np.int8)
+    qs = rng.uniform(1e-3, 1e-2, (B, heads)).astype(F)
+    for s, n in enumerate(lens):   # the valid part of every page holds finite scales
+        for t in range(n):
+            p, sl = perm[s, t // 32], t % 32
+            pks[p, sl] = rng.uniform(1e-3, 1e-2, kvh)
+            pvs[p, sl] = rng.uniform(1e-3, 1e-2, kvh)
+    d = [dev(a) for a in (pk, pv, pks, pvs)]
+    kv = ops.paged_kv(*d, dev(np.zeros(1, np.int16)), kvh)
+    o8 = torch.zeros(B, heads * 128, dtype=torch.int8, device="cuda")
+    os_ = torch.zeros(B, heads, dtype=torch.float32, device="cuda")
+    qk = float(F(1.0 / np.sqrt(128.0)))
+    ops.attention_decode_batch(dev(q8), dev(qs), kv, pages, dev(perm.view(np.int16)), max_pages,
+                               dev(np.asarray(lens, np.int32)), B, o8, os_, heads, kvh, qk)
+    got8, gots = host(o8), host(os_)
+    assert q3._lib.lib().q3_device_status() == 0
+    for s, n in enumerate(lens):
+        rows = [perm[s, t // 32] for t in range(n)]
+        sl = [t % 32 for t in range(n)]
+        k8 = pk[rows, sl]
+        v8 = pv[rows, sl]
+        ks = pks[rows, sl]
+        vs = pvs[rows, sl]
+        ref = O.attention(q8[s:s + 1], qs[s:s + 1], k8, ks, v8, vs, np.array([n - 1]), heads,
+                          kvh, 128, F(qk))
+        r8, rs = O.quant_groups(ref, 128)
+        same_bits(got8[s:s + 1], r8)
+        same_bits(gots[s:s + 1], rs)
