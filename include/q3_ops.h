@@ -264,9 +264,11 @@ int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream);
 const char *q3_last_cuda_error(void);
 int q3_device_check(void); /* Q3_OK on an sm_100 device, else Q3_ERR_ARCH */
 
-/* Device-side error word of the library's kernels (0 = none; bit 0: a bounded
- * wait on a TMA pipeline barrier timed out and the kernel gave up).  Reading
- * synchronises with the device and clears the word; -1 if it cannot be read. */
+/* Device-side error word of the library's kernels (0 = none; bit 1: a page
+ * index beyond the pool was skipped; bit 2: a sequence needs more pages than
+ * its table holds; bit 16: a bounded wait in a tensor-core GEMM pipeline timed
+ * out and the kernel gave up).  Reading synchronises with the device and clears
+ * the word; -1 if it cannot be read. */
 int q3_device_status(void);
 
 /* Number of kernels this library has launched in this process (all threads). */

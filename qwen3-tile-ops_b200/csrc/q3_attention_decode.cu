@@ -345,9 +345,15 @@ int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const v
 
 }  // namespace q3
 
+namespace q3 {
+int gemm_device_status_take();
+}
+
 extern "C" int q3_device_status(void) {
   unsigned int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, q3::g_device_error, sizeof v) != cudaSuccess) return -1;
   if (v) cudaMemcpyToSymbol(q3::g_device_error, &zero, sizeof zero);
-  return static_cast<int>(v);
+  const int g = q3::gemm_device_status_take();
+  if (g < 0) return -1;
+  return static_cast<int>(v) | g;
 }

@@ -6,6 +6,41 @@
 // one GEMM is bit-identical to running the sequences one by one.
 #include "q3_attention.h"
 #include "q3_common.cuh"
+#include "q3_gemm.h"
+
+namespace q3 {
+struct QkvArgs {
+  const float *part;
+  int G, B, heads, kv_heads;
+  const float *nq, *nk;
+  const float *cos_t, *sin_t;
+  const int32_t *pos;
+  float inv_hd;
+  int8_t *q8;
+  float *qs;
+  char *pk, *pv, *pks, *pvs;
+  const uint16_t *tables;
+  uint32_t max_pages;
+};
+struct AddNormArgs {
+  const float *part;
+  int G, B, H;
+  float *x;
+  const float *w;
+  float inv;
+  int8_t *h8;
+  float *hs;
+};
+struct SwigluArgs {
+  const float *part;
+  int G, B, I;
+  int8_t *s8;
+  float *ss;
+};
+int red_qkv(const QkvArgs &a, cudaStream_t s);
+int red_add_norm(const AddNormArgs &a, cudaStream_t s);
+int red_swiglu(const SwigluArgs &a, cudaStream_t s);
+}  // namespace q3
 
 namespace {
 
@@ -26,6 +61,7 @@ struct DecodeWs {
   int *kv_len;           // [B]
   float *best;           // [B]
   unsigned long long *keys;  // [B]
+  float *part;           // split-K partials (fused path), largest GEMM of a layer
   size_t total;
 };
 
@@ -55,6 +91,14 @@ DecodeWs carve(const q3_layout &L, uint32_t B, char *base) {
   w.kv_len = (int *)take(4 * B);
   w.best = (float *)take(4 * B);
   w.keys = (unsigned long long *)take(8 * B);
+  {
+    const size_t qkv = (size_t)(H / 256) * B * (QW + 2 * KW), o = (size_t)(QW / 128) * B * H;
+    const size_t gu = 2 * (size_t)(H / 256) * B * I, d = (size_t)(I / 256) * B * H;
+    size_t mx = qkv > o ? qkv : o;
+    mx = mx > gu ? mx : gu;
+    mx = mx > d ? mx : d;
+    w.part = (float *)take(4 * mx);
+  }
   w.total = off;
   return w;
 }
@@ -105,6 +149,118 @@ __global__ void k_keys_to_ids(const unsigned long long *keys, int32_t *next_ids,
   if (s < B) next_ids[s] = static_cast<int32_t>(0xffffffffu - static_cast<unsigned>(keys[s] & 0xffffffffu));
 }
 
+// The batched step with split-K tensor-core GEMMs and fused group reductions
+// (9 launches per layer).  Same arithmetic as the operator-by-operator path.
+int decode_fused(char *bl, const q3_layout &L, const q3_kv_pool *pool, const uint16_t *tables,
+                 uint32_t max_pages, const int32_t *ids, const int32_t *pos, uint32_t B,
+                 int32_t *next_ids, const DecodeWs &w, cudaStream_t st) {
+  void *s = st;
+  const int64_t *o = L.off;
+  const uint32_t H = L.hidden, HD = L.head_dim, QW = L.heads * HD, KW = L.kv_heads * HD,
+                 I = L.inter, V = L.vocab;
+  const float inv_h = 1.0f / static_cast<float>(H), inv_hd = 1.0f / static_cast<float>(HD);
+  const q3_view x = v2(w.x, B, H, Q3_DT_F32), h = v2(w.h, B, H, Q3_DT_F32);
+  const q3_view h8 = v2(w.h8, B, H, Q3_DT_I8), hs = v2(w.hs, B, H / 256, Q3_DT_F32);
+  const q3_view q8 = v2(w.q8, B, QW, Q3_DT_I8), qs = v2(w.qs, B, L.heads, Q3_DT_F32);
+  const q3_view idv = v2(const_cast<int32_t *>(ids), B, 1, Q3_DT_I32);
+  const q3_view emb = v2(bl + o[Q3_OFF_EMB], V, H, Q3_DT_I8);
+  const q3_view emb_s = v2(bl + o[Q3_OFF_EMB] + (int64_t)V * H, V, 1, Q3_DT_F32);
+  const q3_view lm = v2(bl + o[Q3_OFF_LM], V, H, Q3_DT_I8);
+  const q3_view lm_s = v2(bl + o[Q3_OFF_LM] + (int64_t)V * H, V, 1, Q3_DT_F32);
+  const float *cos_t = reinterpret_cast<const float *>(bl + o[Q3_OFF_COS]);
+  const float *sin_t = reinterpret_cast<const float *>(bl + o[Q3_OFF_SIN]);
+  {
+    const q3_view n1_0 = v2(bl + o[Q3_OFF_N1], H, 1, Q3_DT_F32);
+    Q3_TRY(q3_embedding_rmsnorm_rows(&emb, &emb_s, &idv, &x, &n1_0, &h, inv_h, s));
+    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+  }
+  for (uint32_t Li = 0; Li < L.layers; ++Li) {
+    char *lw = bl + o[Q3_OFF_LQ] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERW_STRIDE];
+    char *ln = bl + o[Q3_OFF_N1] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERN_STRIDE];
+    auto Wp = [&](int key) { return reinterpret_cast<const int8_t *>(lw + (o[key] - o[Q3_OFF_LQ])); };
+    auto Sp = [&](int key) { return reinterpret_cast<const float *>(lw + (o[key] - o[Q3_OFF_LQ])); };
+    const float *nq = reinterpret_cast<const float *>(ln + (o[Q3_OFF_NQ] - o[Q3_OFF_N1]));
+    const float *nk = reinterpret_cast<const float *>(ln + (o[Q3_OFF_NK] - o[Q3_OFF_N1]));
+    const float *n2 = reinterpret_cast<const float *>(ln + (o[Q3_OFF_N2] - o[Q3_OFF_N1]));
+    const float *next_norm =
+        (Li + 1 < L.layers)
+            ? reinterpret_cast<const float *>(bl + o[Q3_OFF_N1] + static_cast<int64_t>(Li + 1) * o[Q3_OFF_LAYERN_STRIDE])
+            : reinterpret_cast<const float *>(bl + o[Q3_OFF_NF]);
+    char *pk = static_cast<char *>(pool->k) + Li * pool->layer_stride;
+    char *pv = static_cast<char *>(pool->v) + Li * pool->layer_stride;
+    char *pks = static_cast<char *>(pool->ks) + Li * pool->scale_layer_stride;
+    char *pvs = static_cast<char *>(pool->vs) + Li * pool->scale_layer_stride;
+
+    // Q | K | V partials, then norm/rope/quant into q8 and the KV pages
+    {
+      const int8_t *wts[3] = {Wp(Q3_OFF_LQ), Wp(Q3_OFF_LK), Wp(Q3_OFF_LV)};
+      const float *scs[3] = {Sp(Q3_OFF_LQ_SCALE), Sp(Q3_OFF_LK_SCALE), Sp(Q3_OFF_LV_SCALE)};
+      const int rows[3] = {(int)QW, (int)KW, (int)KW};
+      Q3_TRY(q3::gemm_tc_partials(1, 3, wts, scs, rows, w.h8, H, reinterpret_cast<const char *>(w.hs),
+                                  4 * (H / 256), B, H, 256, w.part, st));
+      q3::QkvArgs a{w.part, (int)(H / 256), (int)B, (int)L.heads, (int)L.kv_heads, nq, nk, cos_t,
+                    sin_t, pos, inv_hd, w.q8, w.qs, pk, pv, pks, pvs, tables, max_pages};
+      Q3_TRY(q3::red_qkv(a, st));
+    }
+    // attention
+    {
+      q3::DecodeAttnArgs d{};
+      d.q8 = reinterpret_cast<const char *>(w.q8);
+      d.q_rb = QW;
+      d.qs = reinterpret_cast<const char *>(w.qs);
+      d.qs_rb = 4 * L.heads;
+      d.o8 = reinterpret_cast<char *>(w.o8);
+      d.o_rb = QW;
+      d.os = reinterpret_cast<char *>(w.os);
+      d.os_rb = 4 * L.heads;
+      d.ks = pks;
+      d.vs = pvs;
+      d.table = tables;
+      d.table_stride = max_pages;
+      d.page_bytes = kPT * KW;
+      d.row_bytes = KW;
+      d.scale_page_bytes = kPT * 4 * L.kv_heads;
+      d.scale_row_bytes = 4 * L.kv_heads;
+      d.kv_len = w.kv_len;
+      d.qk_scale = kInvSqrt128;
+      Q3_TRY(q3::attention_decode_launch(d, pk, pv, pool->num_pages, L.kv_heads, B, st));
+    }
+    // O (+ residual) -> x; RMSNorm(n2) + quant -> h8/hs
+    {
+      const int8_t *wts[1] = {Wp(Q3_OFF_LO)};
+      const float *scs[1] = {Sp(Q3_OFF_LO_SCALE)};
+      const int rows[1] = {(int)H};
+      Q3_TRY(q3::gemm_tc_partials(1, 1, wts, scs, rows, w.o8, QW, reinterpret_cast<const char *>(w.os),
+                                  4 * L.heads, B, QW, 128, w.part, st));
+      q3::AddNormArgs a{w.part, (int)(QW / 128), (int)B, (int)H, w.x, n2, inv_h, w.h8, w.hs};
+      Q3_TRY(q3::red_add_norm(a, st));
+    }
+    // gate/up -> SwiGLU + quant -> s8/ss
+    {
+      const int8_t *wts[2] = {Wp(Q3_OFF_LG), Wp(Q3_OFF_LU)};
+      const float *scs[2] = {Sp(Q3_OFF_LG_SCALE), Sp(Q3_OFF_LU_SCALE)};
+      const int rows[2] = {(int)I, (int)I};
+      Q3_TRY(q3::gemm_tc_partials(2, 2, wts, scs, rows, w.h8, H, reinterpret_cast<const char *>(w.hs),
+                                  4 * (H / 256), B, H, 256, w.part, st));
+      q3::SwigluArgs a{w.part, (int)(H / 256), (int)B, (int)I, w.s8, w.ss};
+      Q3_TRY(q3::red_swiglu(a, st));
+    }
+    // down (+ residual) -> x; next layer's RMSNorm (or the final norm) + quant
+    {
+      const int8_t *wts[1] = {Wp(Q3_OFF_LD)};
+      const float *scs[1] = {Sp(Q3_OFF_LD_SCALE)};
+      const int rows[1] = {(int)H};
+      Q3_TRY(q3::gemm_tc_partials(1, 1, wts, scs, rows, w.s8, I, reinterpret_cast<const char *>(w.ss),
+                                  4 * (I / 256), B, I, 256, w.part, st));
+      q3::AddNormArgs a{w.part, (int)(I / 256), (int)B, (int)H, w.x, next_norm, inv_h, w.h8, w.hs};
+      Q3_TRY(q3::red_add_norm(a, st));
+    }
+  }
+  // final norm + quant already in h8/hs: lm_head fused with argmax
+  Q3_TRY(q3_gemm_nt_group_argmax(&h8, &hs, &lm, &lm_s, w.best, next_ids, 256, w.keys, 8 * B, s));
+  return Q3_OK;
+}
+
 }  // namespace
 
 extern "C" size_t q3_decode_workspace_bytes(const q3_layout *L, uint32_t n_seqs) {
@@ -139,6 +295,10 @@ extern "C" int q3_decode_step_batch(void *blob, const q3_layout *layout, const q
                                   reinterpret_cast<const float *>(bl + o[Q3_OFF_SIN]), HALF, w.cos,
                                   w.sin, w.kv_len, w.best, next_ids, B);
   Q3_TRY(q3h::launch_status());
+  // fast path: the Qwen3-0.6B shapes with tensor-core split-K GEMMs
+  if (B <= 64 && H == 1024 && HD == 128 && L.heads == 2 * L.kv_heads && I % 256 == 0 &&
+      QW % 128 == 0 && pool->num_pages > 0)
+    return decode_fused(bl, L, pool, tables, max_pages, ids, pos, B, next_ids, w, st);
 
   const q3_view x = v2(w.x, B, H, Q3_DT_F32), h = v2(w.h, B, H, Q3_DT_F32);
   const q3_view h8 = v2(w.h8, B, H, Q3_DT_I8), hs = v2(w.hs, B, H / 256, Q3_DT_F32);

@@ -43,5 +43,14 @@ struct GemmArgs {
 };
 
 int gemm_simt(const GemmArgs &p, cudaStream_t s);
+int gemm_tc(const GemmArgs &p, cudaStream_t s);
+bool gemm_tc_eligible(const GemmArgs &p);
+int argmax_begin(const GemmArgs &p, cudaStream_t s);
+int argmax_end(const GemmArgs &p, cudaStream_t s);
+
+// split-K partials for decode-sized GEMMs (q3_gemm_tc.cu)
+int gemm_tc_partials(int nacc, int nmaps, const int8_t *const *w, const float *const *ws,
+                     const int *rows, const int8_t *a, long a_rb, const char *a_scale,
+                     long as_rb, int M, int K, int group, float *out, cudaStream_t s);
 
 }  // namespace q3

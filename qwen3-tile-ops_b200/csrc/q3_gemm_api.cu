@@ -155,5 +155,12 @@ extern "C" int q3_gemm_nt_group_argmax(const q3_view *a, const q3_view *a_scale,
 }
 
 namespace q3 {
-int gemm_dispatch(const GemmArgs &p, cudaStream_t s) { return gemm_simt(p, s); }
+// tensor cores where the shape allows, the CUDA-core kernel otherwise (same bits)
+int gemm_dispatch(const GemmArgs &p, cudaStream_t s) {
+  if (p.mode == EPI_ARGMAX) Q3_TRY(argmax_begin(p, s));
+  const int st = gemm_tc_eligible(p) ? gemm_tc(p, s) : gemm_simt(p, s);
+  if (st != Q3_OK) return st;
+  if (p.mode == EPI_ARGMAX) return argmax_end(p, s);
+  return Q3_OK;
+}
 }  // namespace q3

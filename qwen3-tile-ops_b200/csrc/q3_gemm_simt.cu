@@ -227,6 +227,17 @@ static int launch_simt(const GemmArgs &p, cudaStream_t s) {
   return q3h::launch_status();
 }
 
+// the lm_head argmax keys: cleared before the row-max kernel, merged into
+// (best, bidx) after it (whichever GEMM path ran)
+int argmax_begin(const GemmArgs &p, cudaStream_t s) {
+  k_argmax_init<<<(p.M + 127) / 128, 128, 0, s>>>(p.arg_keys, p.M);
+  return q3h::launch_status();
+}
+int argmax_end(const GemmArgs &p, cudaStream_t s) {
+  k_argmax_finish<<<(p.M + 127) / 128, 128, 0, s>>>(p.arg_keys, p.best, p.bidx, p.M);
+  return q3h::launch_status();
+}
+
 int gemm_simt(const GemmArgs &p, cudaStream_t s) {
   switch (p.mode) {
     case EPI_STORE: return launch_simt<128, 8, EPI_STORE>(p, s);
@@ -234,14 +245,7 @@ int gemm_simt(const GemmArgs &p, cudaStream_t s) {
     case EPI_QUANT: return launch_simt<128, 8, EPI_QUANT>(p, s);
     case EPI_NORMROPE: return launch_simt<128, 8, EPI_NORMROPE>(p, s);
     case EPI_SWIGLU: return launch_simt<256, 8, EPI_SWIGLU>(p, s);
-    case EPI_ARGMAX: {
-      const int rows = p.M;
-      k_argmax_init<<<(rows + 127) / 128, 128, 0, s>>>(p.arg_keys, rows);
-      int st = launch_simt<128, 8, EPI_ARGMAX>(p, s);
-      if (st) return st;
-      k_argmax_finish<<<(rows + 127) / 128, 128, 0, s>>>(p.arg_keys, p.best, p.bidx, rows);
-      return q3h::launch_status();
-    }
+    case EPI_ARGMAX: return launch_simt<128, 8, EPI_ARGMAX>(p, s);
   }
   return Q3_ERR_SHAPE;
 }

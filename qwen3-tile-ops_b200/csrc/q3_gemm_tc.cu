@@ -1,0 +1,750 @@
+// Per-K-group w8a8 GEMM on the 5th-generation tensor cores (tcgen05, kind::i8),
+// with the epilogues of kernels/group_gemm.h:27-222, swiglu_quant.h:105-255 and
+// lm_argmax.h:72-182.  Bit-identical to the CUDA-core path (q3_gemm_simt.cu).
+//
+// Orientation: the MMA's M dimension is 128 WEIGHT rows (output features), its
+// N dimension a tile of NTOK tokens (activation rows), K the input features.
+// One TMEM accumulator [128 lanes = features][NTOK columns = tokens] int32 per
+// K-group; two of them alternate, so the epilogue warps dequantise group g
+//     acc[n][m] = acc[n][m] + (f32(part[n][m]) * b_scale[n]) * a_scale[m][g]
+// (the reference's order, ref_qwen3.py:152-157) while the MMA warp runs g+1.
+// A thread of the epilogue owns one feature row, so every per-feature reduction
+// of the reference (head RMSNorm, head/group absmax) is a reduction over lanes.
+//
+// Warps: 0-3 epilogue (TMEM lanes 32w..32w+31), 4 TMA producer, 5 MMA issuer
+// and TMEM owner.  Operands arrive by TMA (no multicast) into 128B-swizzled
+// shared memory, 128 K-bytes per stage.  No warp leaves before the others; every
+// mbarrier wait is bounded (about one second) and a timeout sets bit 16 of the
+// device error word, drains the copies and MMAs in flight and frees TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "q3_common.cuh"
+#include "q3_gemm.h"
+
+namespace q3 {
+
+// device error word of this file's kernels (q3_device_status ORs it in)
+static __device__ unsigned int g_gemm_error = 0;
+
+int gemm_device_status_take() {
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof v) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof zero);
+  return static_cast<int>(v);
+}
+
+namespace tc {
+
+constexpr unsigned kErrGemmTimeout = 1u << 16;
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = (EPI_WARPS + 2) * 32;
+
+template <int NTOK, int MODE>
+struct Cfg {
+  static constexpr int NACC = (MODE == EPI_SWIGLU) ? 2 : 1;           // gate + up
+  static constexpr int TILES = (MODE == EPI_SWIGLU) ? 2 : 1;          // 128-row tiles per CTA
+  static constexpr int A_BYTES = 128 * 128;                           // one weight box
+  static constexpr int B_BYTES = NTOK * 128;                          // one activation box
+  static constexpr int STAGE_BYTES = NACC * A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS_RAW = 2 * NACC * NTOK;
+  static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
+                                   : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
+  static constexpr int XROWS = (MODE == EPI_SWIGLU) ? 256 : (MODE == EPI_NORMROPE || MODE == EPI_QUANT) ? 128 : 1;
+  static constexpr int STAGES = (MODE == EPI_SWIGLU) ? 3 : 4;
+};
+
+template <int NTOK, int MODE>
+struct __align__(1024) Smem {
+  alignas(1024) int8_t stage[Cfg<NTOK, MODE>::STAGES][Cfg<NTOK, MODE>::STAGE_BYTES];
+  // epilogue staging [feature][token], rows padded by one word (conflict-free)
+  float xchg[Cfg<NTOK, MODE>::XROWS][NTOK + 1];
+  float xchg2[MODE == EPI_SWIGLU ? 128 : 1][MODE == EPI_SWIGLU ? NTOK + 1 : 1];
+  float ascale[NTOK * 16];                 // a_scale[m][g] for this token tile (<= 16 groups)
+  unsigned long long full[Cfg<NTOK, MODE>::STAGES], empty[Cfg<NTOK, MODE>::STAGES], tfull[2], tempty[2], done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t su32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long *b, unsigned c) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(c) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long *b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ uint64_t gtime() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// bounded wait for the completion of the phase with parity `par`
+__device__ __forceinline__ bool mbar_wait(unsigned long long *b, uint32_t par, const int *abort) {
+  const uint32_t a = su32(b);
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(a), "r"(par)
+        : "memory");
+    if (ok) return true;
+    if ((it & 127) == 0) {
+      if (abort && *reinterpret_cast<const volatile int *>(abort)) return false;
+      const uint64_t t = gtime();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > 1000000000ull) return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *m, int x, int y,
+                                       unsigned long long *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(su32(bar))
+      : "memory");
+}
+// shared-memory matrix descriptor: K-major, 128B swizzle, 8-row atoms 1024 B apart
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = (saddr & 0x3FFFFu) >> 4;
+  d |= 1ull << 16;                   // leading byte offset (unused for swizzled K-major)
+  d |= (1024ull >> 4) << 32;         // stride byte offset: next 8-row atom
+  d |= 1ull << 46;                   // descriptor version for tcgen05
+  d |= 2ull << 61;                   // 128-byte swizzle
+  return d;
+}
+// instruction descriptor: s32 accumulate, s8 x s8, both K-major, M = 128, N = ntok
+__host__ __device__ constexpr uint32_t idesc_i8(int ntok) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(ntok >> 3) << 17) |
+         ((128u >> 4) << 24);
+}
+__device__ __forceinline__ void mma_i8(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t id,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(dt),
+      "l"(ad), "l"(bd), "r"(id), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(unsigned long long *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15},"
+      " [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+}
+
+struct TcArgs {
+  GemmArgs g;
+  int groups;         // K / group
+  int boxes;          // group / 128
+};
+
+template <int NTOK, int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+              const __grid_constant__ CUtensorMap tmB, const TcArgs args) {
+  using C = Cfg<NTOK, MODE>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  Smem<NTOK, MODE> &sm = *reinterpret_cast<Smem<NTOK, MODE> *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const GemmArgs &p = args.g;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = args.groups, NB = args.boxes;
+  const int row0 = blockIdx.x * 128 * C::TILES;   // first feature row of this CTA
+  const int m0 = blockIdx.y * NTOK;               // first token
+  const int mvalid = min(NTOK, p.M - m0);
+  const int total_it = C::TILES * G * NB;         // producer / MMA k-iterations
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.tfull[i], 1);
+      mbar_init(&sm.tempty[i], EPI_WARPS);
+    }
+    mbar_init(&sm.done, 1);
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == EPI_WARPS + 1) {   // TMEM allocation (whole warp)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(&sm.tmem_base)),
+                 "n"(C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (warp < EPI_WARPS) {        // this token tile's activation scales, all groups
+    for (int i = threadIdx.x; i < NTOK * G; i += EPI_WARPS * 32) {
+      const int m = i / G, g = i % G;
+      sm.ascale[i] = (m < mvalid)
+                         ? *reinterpret_cast<const float *>(p.a_scale + (long)(m0 + m) * p.as_rb + g * 4)
+                         : 0.0f;
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == EPI_WARPS) {
+    // ------------------------------------------------------------ TMA producer
+    int issued = 0;
+    bool ok = true;
+    for (int it = 0; it < total_it && ok; ++it) {
+      const int st = it % STAGES;
+      if (lane == 0) {
+        if (!mbar_wait(&sm.empty[st], ((it / STAGES) & 1) ^ 1, &sm.abort)) ok = false;
+        else {
+          const int t = it / (G * NB), r = it % (G * NB);
+          const int k0 = r * 128;   // (g * NB + box) * 128
+          mbar_expect_tx(&sm.full[st], C::STAGE_BYTES);
+          int8_t *dst = sm.stage[st];
+          tma_2d(dst, &tmA, k0, row0 + t * 128, &sm.full[st]);
+          if (C::NACC == 2) tma_2d(dst + C::A_BYTES, &tmA2, k0, row0 + t * 128, &sm.full[st]);
+          tma_2d(dst + C::NACC * C::A_BYTES, &tmB, k0, m0, &sm.full[st]);
+          ++issued;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    }
+    if (!ok && lane == 0) {
+      atomicOr(&g_gemm_error, kErrGemmTimeout);
+      sm.abort = 1;
+      for (int it = max(0, issued - STAGES); it < issued; ++it)   // let issued copies land
+        mbar_wait(&sm.full[it % STAGES], (it / STAGES) & 1, nullptr);
+    }
+  } else if (warp == EPI_WARPS + 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t ID = idesc_i8(NTOK);
+    bool ok = true;
+    int it = 0;
+    for (int gi = 0; gi < C::TILES * G && ok; ++gi) {
+      const int buf = gi & 1;
+      if (lane == 0 && !mbar_wait(&sm.tempty[buf], ((gi >> 1) & 1) ^ 1, &sm.abort)) ok = false;
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      fence_after();
+      for (int box = 0; box < NB && ok; ++box, ++it) {
+        const int st = it % STAGES;
+        if (lane == 0) {
+          if (!mbar_wait(&sm.full[st], (it / STAGES) & 1, &sm.abort)) ok = false;
+          else {
+            fence_after();
+            const uint32_t sa = su32(sm.stage[st]);
+            const uint32_t sb = sa + C::NACC * C::A_BYTES;
+#pragma unroll
+            for (int a = 0; a < C::NACC; ++a) {
+              const uint32_t dt = tmem + (buf * C::NACC + a) * NTOK;
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                mma_i8(dt, sdesc(sa + a * C::A_BYTES + ks * 32), sdesc(sb + ks * 32), ID,
+                       (box | ks) != 0);
+            }
+            mma_commit(&sm.empty[st]);          // frees the stage when these MMAs finish
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      }
+      if (ok && lane == 0) mma_commit(&sm.tfull[buf]);
+    }
+    if (lane == 0) {                             // every MMA issued has completed
+      mma_commit(&sm.done);
+      mbar_wait(&sm.done, 0, nullptr);
+    }
+    if (!ok && lane == 0) {
+      atomicOr(&g_gemm_error, kErrGemmTimeout);
+      sm.abort = 1;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int tid = threadIdx.x;                 // feature row within the 128-row tile
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    bool ok = true;
+    int gi = 0;
+    for (int t = 0; t < C::TILES && ok; ++t) {
+      const int n = row0 + t * 128 + tid;
+      const float bs = p.b_scale[n];
+      const float bs2 = (C::NACC == 2) ? p.b2_scale[n] : 0.0f;
+      float acc[C::NACC][NTOK];
+#pragma unroll
+      for (int a = 0; a < C::NACC; ++a)
+#pragma unroll
+        for (int m = 0; m < NTOK; ++m) acc[a][m] = 0.0f;
+      for (int g = 0; g < G; ++g, ++gi) {
+        const int buf = gi & 1;
+        if (!mbar_wait(&sm.tfull[buf], (gi >> 1) & 1, &sm.abort)) { ok = false; break; }
+        fence_after();
+#pragma unroll
+        for (int a = 0; a < C::NACC; ++a) {
+          const float b = a ? bs2 : bs;
+#pragma unroll
+          for (int c = 0; c < NTOK; c += 16) {
+            int v[16];
+            tmem_ld16(lane_addr + (buf * C::NACC + a) * NTOK + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float as = sm.ascale[(c + i) * G + g];
+              acc[a][c + i] = __fadd_rn(acc[a][c + i], __fmul_rn(__fmul_rn(i2f_small(v[i]), b), as));
+            }
+          }
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.tempty[buf]);
+      }
+      if (!ok) break;
+
+      // -------------------------------------------------------- epilogues
+      if (MODE == EPI_STORE || MODE == EPI_ADD) {
+#pragma unroll
+        for (int m = 0; m < NTOK; ++m) {
+          if (m < mvalid) {
+            float *row = reinterpret_cast<float *>(p.out + (long)(m0 + m) * p.out_rb);
+            row[n] = (MODE == EPI_ADD) ? __fadd_rn(row[n], acc[0][m]) : acc[0][m];
+          }
+        }
+      } else if (MODE == EPI_ARGMAX) {
+        // (max, first index) per token over the tile's 128 rows -> atomicMax of a
+        // packed key (monotone value << 32 | ~index): largest value, then smallest index
+#pragma unroll
+        for (int m = 0; m < NTOK; ++m) {
+          const float v = __fadd_rn(acc[0][m], 0.0f);   // -0 -> +0: equal maxima compare equal
+          const unsigned b = __float_as_uint(v);
+          const unsigned key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+          unsigned long long k =
+              (static_cast<unsigned long long>(key) << 32) | (0xffffffffu - static_cast<unsigned>(n));
+#pragma unroll
+          for (int o = 16; o; o >>= 1) {
+            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+            k = k2 > k ? k2 : k;
+          }
+          if (lane == 0 && m < mvalid) atomicMax(p.arg_keys + m0 + m, k);
+        }
+      } else {
+        // stage this tile's values [feature][token] in shared memory (padded rows)
+        // and continue with one warp per token (features l, l+32, l+64, l+96 per lane)
+        if (MODE == EPI_SWIGLU) {
+#pragma unroll
+          for (int m = 0; m < NTOK; ++m) {
+            sm.xchg[t * 128 + tid][m] = acc[0][m];
+            sm.xchg2[tid][m] = acc[1][m];
+          }
+          epi_sync();
+          // silu(g)*u (ref_qwen3.py:194-200), element by element (rolled loop)
+          for (int m = 0; m < mvalid; ++m) {
+            const float gt = sm.xchg[t * 128 + tid][m];
+            float e = exp_ref(__fmul_rn(gt, -1.0f));
+            e = __fadd_rn(e, 1.0f);
+            e = __fdiv_rn(1.0f, e);
+            sm.xchg[t * 128 + tid][m] = __fmul_rn(__fmul_rn(gt, e), sm.xchg2[tid][m]);
+          }
+          epi_sync();
+          if (t == C::TILES - 1) {
+            // per-token absmax over the 256-feature group, quantise both tiles
+            for (int m = warp; m < mvalid; m += EPI_WARPS) {
+              float v[8];
+              float mx = 0.0f;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                v[k] = sm.xchg[lane + 32 * k][m];
+                mx = fmaxf(mx, fabsf(v[k]));
+              }
+              mx = warp_tree_max(mx);
+              const float scale = __fmul_rn(mx, kInv127);
+              int8_t *q = reinterpret_cast<int8_t *>(p.q8 + (long)(m0 + m) * p.q8_rb) + row0;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) q[lane + 32 * k] = static_cast<int8_t>(quant1(v[k], scale));
+              if (lane == 0)
+                *reinterpret_cast<float *>(p.qs + (long)(m0 + m) * p.qs_rb + (row0 / 256) * 4) = scale;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int m = 0; m < NTOK; ++m) sm.xchg[tid][m] = acc[0][m];
+          epi_sync();
+          const int r0 = row0 + t * 128;
+          for (int m = warp; m < mvalid; m += EPI_WARPS) {
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = sm.xchg[lane + 32 * k][m];
+            if (MODE == EPI_NORMROPE) {
+              // head RMSNorm: tree over each 32-row block (k), blocks summed in order
+              float ss = 0.0f;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) ss = __fadd_rn(ss, warp_tree_sum(__fmul_rn(v[k], v[k])));
+              ss = __fadd_rn(__fmul_rn(ss, p.inv_hd), kEps);
+              const float r = rsqrt_ref(ss);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], r), p.nw[lane + 32 * k]);
+              // rotate-half RoPE: pairs (l, l+64) and (l+32, l+96) live in this lane
+              const float *cr = reinterpret_cast<const float *>(p.cos + (long)(m0 + m) * p.cos_rb);
+              const float *sr = reinterpret_cast<const float *>(p.sin + (long)(m0 + m) * p.sin_rb);
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                const float cs = cr[lane + 32 * k], sn = sr[lane + 32 * k];
+                const float l = v[k], rr = v[k + 2];
+                v[k] = __fsub_rn(__fmul_rn(l, cs), __fmul_rn(rr, sn));
+                v[k + 2] = __fadd_rn(__fmul_rn(l, sn), __fmul_rn(rr, cs));
+              }
+            }
+            float mx = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) mx = fmaxf(mx, fabsf(v[k]));
+            mx = warp_tree_max(mx);
+            const float scale = __fmul_rn(mx, kInv127);
+            int8_t *q = reinterpret_cast<int8_t *>(p.q8 + (long)(m0 + m) * p.q8_rb) + r0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) q[lane + 32 * k] = static_cast<int8_t>(quant1(v[k], scale));
+            if (lane == 0)
+              *reinterpret_cast<float *>(p.qs + (long)(m0 + m) * p.qs_rb + (r0 / 128) * 4) = scale;
+          }
+        }
+        epi_sync();   // the staging buffer is rewritten by the next tile
+      }
+    }
+    if (!ok && lane == 0) {
+      atomicOr(&g_gemm_error, kErrGemmTimeout);
+      sm.abort = 1;
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == EPI_WARPS + 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "n"(C::TMEM_COLS)
+                 : "memory");
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// int8 [rows][cols] with row stride `stride` bytes; box = 128 bytes x box_rows
+static bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols,
+                     uint64_t stride, uint32_t box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {stride};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NTOK, int MODE>
+static int launch(const GemmArgs &p, cudaStream_t s) {
+  using C = Cfg<NTOK, MODE>;
+  CUtensorMap ta, ta2, tb;
+  const uint64_t K = p.K;
+  if (!make_map(&ta, p.b, p.N, K, p.b_rb, 128)) return Q3_ERR_CUDA;
+  if (!make_map(&ta2, C::NACC == 2 ? p.b2 : p.b, p.N, K, p.b_rb, 128)) return Q3_ERR_CUDA;
+  if (!make_map(&tb, p.a, p.M, K, p.a_rb, NTOK)) return Q3_ERR_CUDA;
+  const size_t smem = sizeof(Smem<NTOK, MODE>) + 1024;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [&] {
+    attr = cudaFuncSetAttribute(k_gemm_tc<NTOK, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)smem);
+  });
+  if (attr != cudaSuccess) {
+    q3h::set_cuda_error(attr);
+    return Q3_ERR_CUDA;
+  }
+  TcArgs a{p, p.K / p.group, p.group / 128};
+  dim3 grid(p.N / (128 * C::TILES), (p.M + NTOK - 1) / NTOK);
+  q3h::timer_begin(q3h::TIMER_GEMM, s);
+  k_gemm_tc<NTOK, MODE><<<grid, THREADS, smem, s>>>(ta, ta2, tb, a);
+  const int st = q3h::launch_status();
+  q3h::timer_end(q3h::TIMER_GEMM, s);
+  return st;
+}
+
+}  // namespace tc
+
+// Shapes the tensor-core path takes: 128-byte K boxes within whole groups,
+// 16-byte aligned operands, at most 16 groups, whole 128-row (256 for SwiGLU) tiles.
+bool gemm_tc_eligible(const GemmArgs &p) {
+  if (p.group % 128 || p.K % p.group || p.K / p.group > 16 || p.group > 256) return false;
+  if (p.a_rb % 16 || p.b_rb % 16 || reinterpret_cast<uintptr_t>(p.a) % 16 ||
+      reinterpret_cast<uintptr_t>(p.b) % 16)
+    return false;
+  if (p.mode == EPI_SWIGLU) {
+    if (p.N % 256 || reinterpret_cast<uintptr_t>(p.b2) % 16) return false;
+  } else if (p.N % 128) {
+    return false;
+  }
+  return true;
+}
+
+int gemm_tc(const GemmArgs &p, cudaStream_t s) {
+  switch (p.mode) {
+    case EPI_STORE: return tc::launch<64, EPI_STORE>(p, s);
+    case EPI_ADD: return tc::launch<64, EPI_ADD>(p, s);
+    case EPI_QUANT: return tc::launch<64, EPI_QUANT>(p, s);
+    case EPI_NORMROPE: return tc::launch<64, EPI_NORMROPE>(p, s);
+    case EPI_SWIGLU: return tc::launch<64, EPI_SWIGLU>(p, s);
+    case EPI_ARGMAX: return tc::launch<64, EPI_ARGMAX>(p, s);
+  }
+  return Q3_ERR_SHAPE;
+}
+
+}  // namespace q3
+
+// ===========================================================================
+// Split-K partials for small token counts (decode): one CTA per (128-row
+// weight tile, K-group).  It writes the group's dequantised partial
+//     part[a][g][m][n] = (f32(int32(A_g . W_g)[m][n]) * w_scale[n]) * a_scale[m][g]
+// (the reference's per-group product, ref_qwen3.py:154-156) to a scratch
+// buffer; the reduce kernels (q3_decode_fused.cu) add the groups in order from
+// 0 and apply the epilogue.  Up to three weight matrices share one launch
+// (Q/K/V): row tiles [0, t1) use map 0, [t1, t2) map 1, the rest map 2; with
+// NACC = 2 (gate/up) maps 0 and 1 are read for the same rows.
+// ===========================================================================
+namespace q3 {
+namespace tc {
+
+struct PartArgs {
+  const int8_t *a;          // activations [M][K]
+  const char *a_scale;      // [M][G] f32
+  long as_rb;
+  const float *ws[3];       // per-map output-row scales
+  int t1, t2;               // row-tile boundaries between maps
+  int M, N, K, group, G;
+  float *out;               // [NACC][G][M][N]
+};
+
+template <int NTOK, int NACC>
+struct PartSmem {
+  alignas(1024) int8_t a[2][NACC][128 * 128];
+  alignas(1024) int8_t b[2][NTOK * 128];
+  unsigned long long full[2], tfull;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int NTOK, int NACC>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_tc_part(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
+                   const __grid_constant__ CUtensorMap tm2, const __grid_constant__ CUtensorMap tmB,
+                   const PartArgs p) {
+  constexpr int TMEM_COLS = (NACC * NTOK) <= 32 ? 32 : (NACC * NTOK) <= 64 ? 64 : (NACC * NTOK) <= 128 ? 128 : 256;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  PartSmem<NTOK, NACC> &sm = *reinterpret_cast<PartSmem<NTOK, NACC> *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, g = blockIdx.y;
+  const int nb = p.group / 128;
+  const int map = NACC == 2 ? 0 : (tile < p.t1 ? 0 : tile < p.t2 ? 1 : 2);
+  const int row_in_map = NACC == 2 ? tile * 128
+                                   : (tile - (map == 0 ? 0 : map == 1 ? p.t1 : p.t2)) * 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.full[0], 1);
+    mbar_init(&sm.full[1], 1);
+    mbar_init(&sm.tfull, 1);
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == EPI_WARPS + 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(&sm.tmem_base)),
+                 "n"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == EPI_WARPS) {
+    if (lane == 0) {
+      const CUtensorMap *ma = map == 0 ? &tm0 : map == 1 ? &tm1 : &tm2;
+      for (int b = 0; b < nb; ++b) {
+        const int k0 = g * p.group + b * 128;
+        mbar_expect_tx(&sm.full[b], NACC * 128 * 128 + NTOK * 128);
+        tma_2d(sm.a[b][0], ma, k0, row_in_map, &sm.full[b]);
+        if (NACC == 2) tma_2d(sm.a[b][NACC - 1], &tm1, k0, row_in_map, &sm.full[b]);
+        tma_2d(sm.b[b], &tmB, k0, 0, &sm.full[b]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == EPI_WARPS + 1) {
+    constexpr uint32_t ID = idesc_i8(NTOK);
+    bool ok = true;
+    if (lane == 0) {
+      for (int b = 0; b < nb && ok; ++b) {
+        if (!mbar_wait(&sm.full[b], 0, &sm.abort)) { ok = false; break; }
+        fence_after();
+        const uint32_t sb = su32(sm.b[b]);
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+          const uint32_t sa = su32(sm.a[b][a]);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma_i8(tmem + a * NTOK, sdesc(sa + ks * 32), sdesc(sb + ks * 32), ID, (b | ks) != 0);
+        }
+      }
+      mma_commit(&sm.tfull);          // completes once every MMA issued has finished
+      if (!ok) {
+        atomicOr(&g_gemm_error, kErrGemmTimeout);
+        sm.abort = 1;
+        mbar_wait(&sm.tfull, 0, nullptr);
+        for (int b = 0; b < nb; ++b) mbar_wait(&sm.full[b], 0, nullptr);   // copies landed
+      }
+    }
+    __syncwarp();
+  } else {
+    const int tid = threadIdx.x;
+    const int n = tile * 128 + tid;                    // output feature (global column)
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    const bool ok = mbar_wait(&sm.tfull, 0, &sm.abort);
+    fence_after();
+    if (ok) {
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) {
+        const float ws = p.ws[NACC == 2 ? a : map][row_in_map + tid];
+        int v[NTOK];
+#pragma unroll
+        for (int c = 0; c < NTOK; c += 16) tmem_ld16(lane_addr + a * NTOK + c, *reinterpret_cast<int(*)[16]>(&v[c]));
+        tmem_wait_ld();
+        float *dst = p.out + ((size_t)(a * p.G + g) * p.M) * p.N + n;
+#pragma unroll
+        for (int m = 0; m < NTOK; ++m) {
+          if (m < p.M) {
+            const float as = *reinterpret_cast<const float *>(p.a_scale + (long)m * p.as_rb + g * 4);
+            dst[(size_t)m * p.N] = __fmul_rn(__fmul_rn(i2f_small(v[m]), ws), as);
+          }
+        }
+      }
+    } else if (lane == 0) {
+      atomicOr(&g_gemm_error, kErrGemmTimeout);
+      sm.abort = 1;
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == EPI_WARPS + 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TMEM_COLS)
+                 : "memory");
+}
+
+template <int NTOK, int NACC>
+static int launch_part(const PartArgs &p, const CUtensorMap (&maps)[3], const CUtensorMap &tb,
+                       int tiles, cudaStream_t s) {
+  const size_t smem = sizeof(PartSmem<NTOK, NACC>) + 1024;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [&] {
+    attr = cudaFuncSetAttribute(k_gemm_tc_part<NTOK, NACC>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  if (attr != cudaSuccess) {
+    q3h::set_cuda_error(attr);
+    return Q3_ERR_CUDA;
+  }
+  dim3 grid(tiles, p.G);
+  q3h::timer_begin(q3h::TIMER_GEMM, s);
+  k_gemm_tc_part<NTOK, NACC><<<grid, THREADS, smem, s>>>(maps[0], maps[1], maps[2], tb, p);
+  const int st = q3h::launch_status();
+  q3h::timer_end(q3h::TIMER_GEMM, s);
+  return st;
+}
+
+}  // namespace tc
+
+// One split-K launch: nmaps weight matrices [rows_i][K] (row strides = K) with
+// scales ws_i stacked along the output dimension (NACC = 1), or gate/up read for
+// the same rows (nacc = 2).  out: [nacc][K/group][M][sum rows] f32, M <= 64.
+int gemm_tc_partials(int nacc, int nmaps, const int8_t *const *w, const float *const *ws,
+                     const int *rows, const int8_t *a, long a_rb, const char *a_scale,
+                     long as_rb, int M, int K, int group, float *out, cudaStream_t s) {
+  if (M < 1 || M > 64 || group % 128 || group > 256 || K % group || a_rb % 16 ||
+      reinterpret_cast<uintptr_t>(a) % 16)
+    return Q3_ERR_SHAPE;
+  tc::PartArgs p{};
+  CUtensorMap maps[3];
+  int tiles = 0;
+  for (int i = 0; i < 3; ++i) {
+    const int j = i < nmaps ? i : nmaps - 1;
+    if (rows[j] % 128 || reinterpret_cast<uintptr_t>(w[j]) % 16) return Q3_ERR_SHAPE;
+    if (!tc::make_map(&maps[i], w[j], rows[j], K, K, 128)) return Q3_ERR_CUDA;
+    p.ws[i] = ws[j];
+  }
+  if (nacc == 2) {
+    tiles = rows[0] / 128;
+    p.t1 = p.t2 = tiles;
+  } else {
+    p.t1 = rows[0] / 128;
+    p.t2 = p.t1 + (nmaps > 1 ? rows[1] / 128 : 0);
+    tiles = p.t2 + (nmaps > 2 ? rows[2] / 128 : 0);
+  }
+  CUtensorMap tb;
+  if (!tc::make_map(&tb, a, M, K, a_rb, 64)) return Q3_ERR_CUDA;
+  p.a = a;
+  p.a_scale = a_scale;
+  p.as_rb = as_rb;
+  p.M = M;
+  p.N = tiles * 128;
+  p.K = K;
+  p.group = group;
+  p.G = K / group;
+  p.out = out;
+  return nacc == 2 ? tc::launch_part<64, 2>(p, maps, tb, tiles, s)
+                   : tc::launch_part<64, 1>(p, maps, tb, tiles, s);
+}
+
+}  // namespace q3
