@@ -36,6 +36,9 @@ REPO = Path(__file__).resolve().parent
 METRIC = "Qwen3-0.6B w8a8 prefill & decode tokens/s at 1/2/4/8 B200; % int8/HBM roofline"
 SEQS, CTX, LAYERS, VOCAB = 64, 2048, 28, 151936
 KV_BYTES_PER_TOKEN_LAYER = 2 * 1024 + 2 * 8 * 4   # K+V int8 rows + f32 per-head scales
+# DRAM bytes (read + write) of one k_attention_decode launch at ctx 2048, 64 seqs, from
+# one ncu capture of this bench (--layers 2 --no-graph); the profile summary gives it
+ATT_TRAFFIC_BYTES = 281348352 + 4959744
 
 
 def parse():
@@ -285,9 +288,11 @@ def run_ours(args) -> None:
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * 4 * B, "d2h_bytes_per_step": 4 * B},
         "gpu_launches": int(launches_per_step) * K,
-        "roofline": {"bound": "hbm", "kernel": "k_attention_paged (decode, one layer, 64 seqs)",
+        "roofline": {"bound": "hbm", "kernel": "k_attention_decode (decode, one layer, 64 seqs)",
                      "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-                     "frac": round(achieved / peak_gbs, 4), "traffic": None,
+                     "frac": round(achieved / peak_gbs, 4), "traffic": ATT_TRAFFIC_BYTES,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
+                                       "launch at ctx 2048 (profiles/attention_decode_config4.md)",
                      "avg_launch_ms": round(att_avg, 4), "bytes_per_launch": att_bytes,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650"},
         "clocks": ck,

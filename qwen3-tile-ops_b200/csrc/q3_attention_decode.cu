@@ -232,8 +232,7 @@ __global__ void __launch_bounds__(THREADS, 4)
             const float pv = (t < kv_len) ? __fmul_rn(pr, vs) : 0.0f;
             const float pm = __fmul_rn(warp_tree_max(fabsf(pv)), kInv127);
             const int q = quant1(pv, pm);
-            // key c stored at (c % 4) * 8 + c / 4: pass 2 lane group kg reads 8 contiguous bytes
-            sm.PQ[h][j * 32 + (lane & 3) * 8 + (lane >> 2)] = static_cast<int8_t>(q);
+            sm.PQ[h][j * 32 + lane] = static_cast<int8_t>(q);   // 4 keys per word for dp4a
             if (lane == 0) {
               sm.corr[h][j] = corr;
               sm.psum[h][j] = ps;
@@ -244,25 +243,33 @@ __global__ void __launch_bounds__(THREADS, 4)
       }
     } else {
       // ---- pass 2: P.V and the in-order recurrences (column-parallel)
-      const int chunk = 2 * warp + (dq >> 2);
+      // lane: column quad dq of this warp's 32 columns, key quads kg and kg + 4;
+      // 4 key rows x 4 columns are transposed with byte permutes so that one
+      // dp4a multiplies 4 keys of one column with their 4 packed P values
+      const int chunk = 2 * warp + (dq >> 2), coff = (dq & 3) << 2;
       for (int q = 0; q < rd.count; ++q) {
         const int j = rd.first + q;
         const int8_t *tile = pages[q];
         int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
-        const int2 pw0 = *reinterpret_cast<const int2 *>(&sm.PQ[0][j * 32 + kg * 8]);
-        const int2 pw1 = *reinterpret_cast<const int2 *>(&sm.PQ[1][j * 32 + kg * 8]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int c = kg + 4 * i;
-          const int vw = *reinterpret_cast<const int *>(tile + c * 128 + ((chunk ^ (c & 7)) << 4) +
-                                                        ((dq & 3) << 2));
-          const int p0 = sx8(i < 4 ? pw0.x : pw0.y, i & 3);
-          const int p1 = sx8(i < 4 ? pw1.x : pw1.y, i & 3);
+        for (int half = 0; half < 2; ++half) {
+          const int kq = kg + 4 * half;
+          int w[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int row = 4 * kq + r;
+            w[r] = *reinterpret_cast<const int *>(tile + row * 128 + ((chunk ^ (row & 7)) << 4) + coff);
+          }
+          const int lo01 = __byte_perm(w[0], w[1], 0x5140), hi01 = __byte_perm(w[0], w[1], 0x7362);
+          const int lo23 = __byte_perm(w[2], w[3], 0x5140), hi23 = __byte_perm(w[2], w[3], 0x7362);
+          const int t[4] = {__byte_perm(lo01, lo23, 0x5410), __byte_perm(lo01, lo23, 0x7632),
+                            __byte_perm(hi01, hi23, 0x5410), __byte_perm(hi01, hi23, 0x7632)};
+          const int p0 = *reinterpret_cast<const int *>(&sm.PQ[0][j * 32 + 4 * kq]);
+          const int p1 = *reinterpret_cast<const int *>(&sm.PQ[1][j * 32 + 4 * kq]);
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
-            const int v = sx8(vw, b);
-            a0[b] += p0 * v;
-            a1[b] += p1 * v;
+            a0[b] = __dp4a(t[b], p0, a0[b]);
+            a1[b] = __dp4a(t[b], p1, a1[b]);
           }
         }
 #pragma unroll

@@ -297,7 +297,7 @@ extern "C" int q3_decode_step_batch(void *blob, const q3_layout *layout, const q
   Q3_TRY(q3h::launch_status());
   // fast path: the Qwen3-0.6B shapes with tensor-core split-K GEMMs
   if (B <= 64 && H == 1024 && HD == 128 && L.heads == 2 * L.kv_heads && I % 256 == 0 &&
-      QW % 128 == 0 && pool->num_pages > 0)
+      QW % 128 == 0 && QW / 128 <= 16 && I / 256 <= 16 && pool->num_pages > 0)
     return decode_fused(bl, L, pool, tables, max_pages, ids, pos, B, next_ids, w, st);
 
   const q3_view x = v2(w.x, B, H, Q3_DT_F32), h = v2(w.h, B, H, Q3_DT_F32);

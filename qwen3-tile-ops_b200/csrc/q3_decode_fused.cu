@@ -18,9 +18,17 @@
 
 namespace q3 {
 
+// every group's partial is loaded first (independent loads in flight
+// together), then the partials are added in group order from 0
+constexpr int kMaxGroups = 16;
 __device__ __forceinline__ float group_sum(const float *part, size_t gstride, int G) {
+  float v[kMaxGroups];
+#pragma unroll
+  for (int g = 0; g < kMaxGroups; ++g) v[g] = g < G ? part[g * gstride] : 0.0f;
   float acc = 0.0f;
-  for (int g = 0; g < G; ++g) acc = __fadd_rn(acc, part[g * gstride]);
+#pragma unroll
+  for (int g = 0; g < kMaxGroups; ++g)
+    if (g < G) acc = __fadd_rn(acc, v[g]);
   return acc;
 }
 
@@ -114,13 +122,18 @@ __global__ void __launch_bounds__(256) k_red_add_norm(AddNormArgs a) {
   __shared__ float rsh;
   const int m = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const size_t gstride = static_cast<size_t>(a.B) * a.H;
-  float xv[4];
+  float xv[4], rv[4];
+  // every load (partials, residual) before the first store: nothing to alias
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int n = t + 256 * k;
-    const float r = group_sum(a.part + static_cast<size_t>(m) * a.H + n, gstride, a.G);
-    xv[k] = __fadd_rn(a.x[static_cast<size_t>(m) * a.H + n], r);
-    a.x[static_cast<size_t>(m) * a.H + n] = xv[k];
+    rv[k] = group_sum(a.part + static_cast<size_t>(m) * a.H + n, gstride, a.G);
+    xv[k] = a.x[static_cast<size_t>(m) * a.H + n];
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    xv[k] = __fadd_rn(xv[k], rv[k]);
+    a.x[static_cast<size_t>(m) * a.H + t + 256 * k] = xv[k];
   }
   if (!a.w) return;
   // 32-column block b = warp + 8k: tree per block, blocks summed in order

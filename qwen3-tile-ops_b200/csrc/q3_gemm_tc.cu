@@ -49,7 +49,9 @@ struct Cfg {
   static constexpr int A_BYTES = 128 * 128;                           // one weight box
   static constexpr int B_BYTES = NTOK * 128;                          // one activation box
   static constexpr int STAGE_BYTES = NACC * A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS_RAW = 2 * NACC * NTOK;
+  // accumulator buffers in flight: as many K-groups as TMEM holds (<= 8)
+  static constexpr int NBUF = (512 / (NACC * NTOK)) >= 8 ? 8 : (512 / (NACC * NTOK));
+  static constexpr int TMEM_COLS_RAW = NBUF * NACC * NTOK;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
                                    : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int XROWS = (MODE == EPI_SWIGLU) ? 256 : (MODE == EPI_NORMROPE || MODE == EPI_QUANT) ? 128 : 1;
@@ -63,7 +65,8 @@ struct __align__(1024) Smem {
   float xchg[Cfg<NTOK, MODE>::XROWS][NTOK + 1];
   float xchg2[MODE == EPI_SWIGLU ? 128 : 1][MODE == EPI_SWIGLU ? NTOK + 1 : 1];
   float ascale[NTOK * 16];                 // a_scale[m][g] for this token tile (<= 16 groups)
-  unsigned long long full[Cfg<NTOK, MODE>::STAGES], empty[Cfg<NTOK, MODE>::STAGES], tfull[2], tempty[2], done;
+  unsigned long long full[Cfg<NTOK, MODE>::STAGES], empty[Cfg<NTOK, MODE>::STAGES];
+  unsigned long long tfull[Cfg<NTOK, MODE>::NBUF], tempty[Cfg<NTOK, MODE>::NBUF], done;
   uint32_t tmem_base;
   int abort;
 };
@@ -192,7 +195,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::NBUF; ++i) {
       mbar_init(&sm.tfull[i], 1);
       mbar_init(&sm.tempty[i], EPI_WARPS);
     }
@@ -253,8 +256,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true;
     int it = 0;
     for (int gi = 0; gi < C::TILES * G && ok; ++gi) {
-      const int buf = gi & 1;
-      if (lane == 0 && !mbar_wait(&sm.tempty[buf], ((gi >> 1) & 1) ^ 1, &sm.abort)) ok = false;
+      const int buf = gi % C::NBUF;
+      if (lane == 0 && !mbar_wait(&sm.tempty[buf], ((gi / C::NBUF) & 1) ^ 1, &sm.abort)) ok = false;
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       fence_after();
@@ -305,8 +308,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int m = 0; m < NTOK; ++m) acc[a][m] = 0.0f;
       for (int g = 0; g < G; ++g, ++gi) {
-        const int buf = gi & 1;
-        if (!mbar_wait(&sm.tfull[buf], (gi >> 1) & 1, &sm.abort)) { ok = false; break; }
+        const int buf = gi % C::NBUF;
+        if (!mbar_wait(&sm.tfull[buf], (gi / C::NBUF) & 1, &sm.abort)) { ok = false; break; }
         fence_after();
 #pragma unroll
         for (int a = 0; a < C::NACC; ++a) {
@@ -569,6 +572,7 @@ template <int NTOK, int NACC>
 struct PartSmem {
   alignas(1024) int8_t a[2][NACC][128 * 128];
   alignas(1024) int8_t b[2][NTOK * 128];
+  float as[NTOK];              // a_scale[m][g] of this CTA's group
   unsigned long long full[2], tfull;
   uint32_t tmem_base;
   int abort;
@@ -604,6 +608,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  if (threadIdx.x < NTOK)   // activation scales of this group, staged while the MMA runs
+    sm.as[threadIdx.x] = threadIdx.x < p.M
+        ? *reinterpret_cast<const float *>(p.a_scale + (long)threadIdx.x * p.as_rb + g * 4) : 0.0f;
   fence_before();
   __syncthreads();
   fence_after();
@@ -653,21 +660,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool ok = mbar_wait(&sm.tfull, 0, &sm.abort);
     fence_after();
     if (ok) {
+      const float *wsp = NACC == 2 ? p.ws[0] : (map == 0 ? p.ws[0] : map == 1 ? p.ws[1] : p.ws[2]);
 #pragma unroll
       for (int a = 0; a < NACC; ++a) {
-        const float ws = p.ws[NACC == 2 ? a : map][row_in_map + tid];
+        const float ws = (NACC == 2 && a) ? p.ws[1][row_in_map + tid] : wsp[row_in_map + tid];
         int v[NTOK];
 #pragma unroll
         for (int c = 0; c < NTOK; c += 16) tmem_ld16(lane_addr + a * NTOK + c, *reinterpret_cast<int(*)[16]>(&v[c]));
         tmem_wait_ld();
         float *dst = p.out + ((size_t)(a * p.G + g) * p.M) * p.N + n;
 #pragma unroll
-        for (int m = 0; m < NTOK; ++m) {
-          if (m < p.M) {
-            const float as = *reinterpret_cast<const float *>(p.a_scale + (long)m * p.as_rb + g * 4);
-            dst[(size_t)m * p.N] = __fmul_rn(__fmul_rn(i2f_small(v[m]), ws), as);
-          }
-        }
+        for (int m = 0; m < NTOK; ++m)
+          if (m < p.M) dst[(size_t)m * p.N] = __fmul_rn(__fmul_rn(i2f_small(v[m]), ws), sm.as[m]);
       }
     } else if (lane == 0) {
       atomicOr(&g_gemm_error, kErrGemmTimeout);
