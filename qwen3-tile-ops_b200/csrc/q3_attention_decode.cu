@@ -1,31 +1,37 @@
 // Decode attention (one query row per sequence) over the paged int8 KV pool.
 // Same arithmetic as kernels/attention_gqa.h:404-547 / tools/ref_qwen3.py:210-266,
-// reorganised:
+// reorganised for the tensor cores:
 //
-// The reference walks 32-key blocks in order, and every step of block j uses
-// the running maximum m_j = max(m_{j-1}, tree_max(s_j)).  m_j depends only on
-// block maxima, so it is a prefix max.  Once the m_j are known, each block's
+// The reference walks 32-key blocks in order; block j uses the running maximum
+// m_j = max(m_{j-1}, tree_max(s_j)), a prefix max of the block maxima, so the
+// block's
 //     corr_j = exp(m_{j-1} - m_j),  p_j = exp(s_j - m_j),  psum_j = tree_sum(p_j),
 //     pq_j = quant(p_j * vs, pmax_j),  part_j = f32(int32(pq_j . V_j)) * pmax_j
-// can be computed independently, and only the two cheap recurrences
+// are known as soon as the maxima of blocks 0..j are, and only the two cheap
+// recurrences
 //     den_j = (den_{j-1} * corr_j) + psum_j,  res_j = (res_{j-1} * corr_j) + part_j
-// must run in block order — with exactly the reference's two roundings each.
+// run in block order, with exactly the reference's two roundings each.
 //
-// CTA = one (sequence, kv head), 4 warps: the two q heads of the GQA group
+// CTA = one (sequence, kv head), 4 warps; the two q heads of the GQA group
 // share every K/V page.  Pages (32 tokens x 128 bytes of this kv head) stream
-// through a double buffer of "rounds" of 4 pages with cp.async (16 bytes per
-// thread, XOR-swizzled rows so that row-wise and column-wise reads are free of
-// bank conflicts): the next round is in flight while the current one is used.
-// Per chunk of up to CH blocks:
-//   pass 1  (K rounds, warp w takes page w)  s = q.k for both heads -> S, block maxima
-//   scan    prefix max of the block maxima
-//   pass 1b (block-parallel)  corr, p, psum, pq, pmax per block
-//   pass 2  (V rounds, column-parallel) each warp owns 32 of the 128 output
-//           columns and runs the recurrence over the blocks in order.
+// through three buffers of "rounds" of 4 pages with cp.async (16 bytes per
+// thread, rows stored in the tensor cores' 128-byte swizzle); rounds alternate
+// K and V over the same 4 blocks, two rounds ahead of the one in use.
+//   K round  one tcgen05.mma chain (M = 128 keys, N = 16, K = 128) gives q.k of
+//            both heads for the 4 pages in TMEM; warp w takes page w: scale,
+//            mask, block max, prefix max, then p / psum / pmax / pq and corr.
+//   V round  per page one tcgen05.mma with A = V read MN-major (M = 128 value
+//            columns, K = 32 keys) and B = the pq rows of both heads, so thread
+//            d of the CTA gets the int32 P.V of column d for both heads and runs
+//            the recurrences over the round's blocks in order.
+// All int32 products are exact, so the tensor cores change no bit.  Thread 0
+// waits for each MMA completion with a bound; the outcome reaches the other
+// threads through the barrier, and a timeout sets a bit of the device error word.
 #include <mutex>
 
 #include "q3_attention.h"
 #include "q3_common.cuh"
+#include "q3_tc.cuh"
 
 namespace q3 {
 
@@ -33,291 +39,256 @@ __device__ unsigned int g_device_error = 0;   // read by q3_device_status()
 
 namespace dec {
 
-constexpr int CH = 48;          // blocks per chunk (1536 keys); a multiple of 4
-constexpr int NW = 4;           // warps
+using namespace tcx;
+
+constexpr int NW = 4;               // warps
 constexpr int THREADS = NW * 32;
-constexpr int RPC = 2 * (CH / 4);   // rounds of a full chunk (K rounds then V rounds)
+constexpr int NBUF = 3;             // round buffers (two rounds in flight)
+constexpr int TMEM_COLS = 64;       // K round: 16 columns; V round: 16 per page
 constexpr unsigned kErrPage = 2u;   // a page index >= num_pages (copy skipped)
 constexpr unsigned kErrTable = 4u;  // kv_len needs more pages than the table holds
+constexpr unsigned kErrMma = 8u;    // a tensor-core completion wait timed out
+constexpr uint32_t ID_QK = idesc_i8(16);          // A = keys (K-major), B = q rows
+constexpr uint32_t ID_PV = idesc_i8(16, true);    // A = V (MN-major), B = pq rows
 
 struct Smem {
-  alignas(128) int8_t buf[2][4][4096];
-  float S[2][CH * 32];
-  int8_t PQ[2][CH * 32];
-  float bmax[2][CH];
-  float mrun[2][CH];
-  float pmax[2][CH];
-  float psum[2][CH];
-  float corr[2][CH];
-  int8_t q[2][128];
-  float qs[2];
+  alignas(1024) int8_t buf[NBUF][4][4096];   // page tiles, 128-byte swizzled rows
+  alignas(1024) int8_t qt[2048];             // B of the K round: rows 0,1 = q heads, rest 0
+  alignas(1024) int8_t pq[4][512];           // B of the V round per page: [row group][k half][8 rows][16 B]
+  float bm[4][2];                            // block maxima of the K round
+  float corr[2][4], psum[2][4], pmax[2][4];  // per head, per page of the round
   float red[NW][2];
+  unsigned long long mbar;
+  uint32_t tmem_base;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src)
                : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_all_but_newest() {
-  asm volatile("cp.async.wait_group 1;" ::: "memory");
+__device__ __forceinline__ void cp_wait_keep2() {
+  asm volatile("cp.async.wait_group 2;" ::: "memory");
 }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // byte offset of 16-byte chunk `i` of row `r` in a swizzled 32x128 page tile
 __device__ __forceinline__ int swz(int r, int i) { return r * 128 + (((i ^ (r & 7))) << 4); }
 
-__device__ __forceinline__ int sx8(int w, int b) { return (w << (24 - 8 * b)) >> 24; }
-
-struct Round {
-  int c0;      // first block of the chunk
-  int nbc;     // blocks in the chunk
-  int v;       // 0: K round, 1: V round
-  int first;   // first block of the round (chunk relative)
-  int count;   // pages in the round (1..4)
-};
-
-__device__ __forceinline__ Round round_of(int r, int nb) {
-  const int nch = (nb + CH - 1) / CH;
-  int k = r / RPC;
-  if (k > nch - 1) k = nch - 1;
-  const int rr = r - k * RPC;
-  Round o;
-  o.c0 = k * CH;
-  o.nbc = min(CH, nb - o.c0);
-  const int nrk = (o.nbc + 3) >> 2;
-  o.v = rr >= nrk;
-  o.first = 4 * (rr - (o.v ? nrk : 0));
-  o.count = min(4, o.nbc - o.first);
-  return o;
-}
-
-__device__ __forceinline__ int rounds_total(int nb) {
-  const int nch = (nb + CH - 1) / CH;
-  const int last = nb - (nch - 1) * CH;
-  return (nch - 1) * RPC + 2 * ((last + 3) >> 2);
-}
-
-// each of the 128 threads copies 2 x 16 bytes of every page of the round
-__device__ __forceinline__ void issue_round(const Round &rd, int8_t (*dst)[4096],
+// each of the 128 threads copies 2 x 16 bytes of every page of round r
+// (rounds: 2g = K pages of blocks 4g..4g+3, 2g+1 = V pages of the same blocks)
+__device__ __forceinline__ void issue_round(int r, int nb, int8_t (*dst)[4096],
                                             const DecodeAttnArgs &p, const char *kpool,
                                             const char *vpool, const uint16_t *table, int kvh) {
   const int t = threadIdx.x;
   const int row = t >> 2, c0 = (t & 3) * 2;
-  const char *pool = rd.v ? vpool : kpool;
-  for (int q = 0; q < rd.count; ++q) {
-    const uint32_t page = table[rd.c0 + rd.first + q];
+  const int first = 4 * (r >> 1), count = min(4, nb - first);
+  const char *pool = (r & 1) ? vpool : kpool;
+  const size_t off = static_cast<size_t>(row) * p.row_bytes + kvh * 128 + c0 * 16;
+  for (int q = 0; q < count; ++q) {
+    const uint32_t page = table[first + q];
     if (page >= p.num_pages) {
       if (t == 0) atomicOr(&g_device_error, kErrPage);
       continue;
     }
-    const char *src = pool + static_cast<size_t>(page) * p.page_bytes +
-                      static_cast<size_t>(row) * p.row_bytes + kvh * 128;
-    cp_async16(dst[q] + swz(row, c0), src + c0 * 16);
-    cp_async16(dst[q] + swz(row, c0 + 1), src + (c0 + 1) * 16);
+    const char *src = pool + static_cast<size_t>(page) * p.page_bytes + off;
+    cp_async16(dst[q] + swz(row, c0), src);
+    cp_async16(dst[q] + swz(row, c0 + 1), src + 16);
   }
 }
 
 __global__ void __launch_bounds__(THREADS, 4)
     k_attention_decode(const char *__restrict__ kpool, const char *__restrict__ vpool,
                        DecodeAttnArgs p) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
   const int kvh = blockIdx.x, seq = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int kv_len = p.kv_len[seq];
   const int nb = (kv_len + 31) >> 5;
   const uint16_t *table = p.table + static_cast<long>(seq) * p.table_stride;
   const float qk_scale = p.qk_scale;
   if (kv_len <= 0 || nb > p.table_stride) {        // uniform for the whole CTA
-    if (threadIdx.x == 0) atomicOr(&g_device_error, kErrTable);
+    if (tid == 0) atomicOr(&g_device_error, kErrTable);
     return;
   }
-
-  if (threadIdx.x < 64) {   // q rows of the two heads (int8) and their scales
-    const int hh = threadIdx.x >> 5;
-    const int h = kvh * 2 + hh;
-    const int *src = reinterpret_cast<const int *>(p.q8 + static_cast<long>(seq) * p.q_rb + h * 128);
-    reinterpret_cast<int *>(sm.q[hh])[lane] = src[lane];
-    if (lane == 0) sm.qs[hh] = *reinterpret_cast<const float *>(p.qs + static_cast<long>(seq) * p.qs_rb + h * 4);
-  }
-
-  float m_carry[2] = {kNegFltMax, kNegFltMax};
-  float den_h[2] = {0.0f, 0.0f};     // every lane keeps both heads' denominators
-  float res[2] = {0.0f, 0.0f};
-  const int dq = lane & 7, kg = lane >> 3;
-  const int my_h = kg >> 1;                       // head of the two columns this lane owns
-  const int my_d0 = warp * 32 + dq * 4 + (kg & 1) * 2;
-
-  const int R = rounds_total(nb);
-  issue_round(round_of(0, nb), sm.buf[0], p, kpool, vpool, table, kvh);
+  const int R = 2 * ((nb + 3) >> 2);               // K and V rounds
+  issue_round(0, nb, sm.buf[0], p, kpool, vpool, table, kvh);
   cp_commit();
+  issue_round(1, nb, sm.buf[1], p, kpool, vpool, table, kvh);   // R >= 2 always
+  cp_commit();
+
+  // operand B of both products: rows 2..15 stay zero
+  for (int i = 256 + tid * 4; i < 2048; i += THREADS * 4) *reinterpret_cast<int *>(sm.qt + i) = 0;
+  for (int i = tid * 4; i < 4 * 512; i += THREADS * 4) *reinterpret_cast<int *>(&sm.pq[0][0] + i) = 0;
+  float qsc[2];
+  {
+    const int hh = tid >> 5;                       // threads 0..63: q rows of the two heads
+    if (hh < 2) {
+      const int h = kvh * 2 + hh;
+      const int v = reinterpret_cast<const int *>(p.q8 + static_cast<long>(seq) * p.q_rb + h * 128)[lane];
+      *reinterpret_cast<int *>(sm.qt + hh * 128 + (((lane >> 2) ^ hh) << 4) + (lane & 3) * 4) = v;
+    }
+    qsc[0] = *reinterpret_cast<const float *>(p.qs + static_cast<long>(seq) * p.qs_rb + kvh * 8);
+    qsc[1] = *reinterpret_cast<const float *>(p.qs + static_cast<long>(seq) * p.qs_rb + kvh * 8 + 4);
+  }
+  if (tid == 0) {
+    mbar_init(&sm.mbar, 1);
+    mbar_init_fence();
+  }
+  if (warp == 0) tmem_alloc<TMEM_COLS>(&sm.tmem_base);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+
+  float carry[2] = {kNegFltMax, kNegFltMax};
+  float den[2] = {0.0f, 0.0f}, res[2] = {0.0f, 0.0f};   // thread = value column tid
+  uint32_t phase = 0;
+  bool mma_ok = true;       // thread 0's view of the last completion wait
+  bool aborted = false;     // uniform
+
   for (int r = 0; r < R; ++r) {
-    if (r + 1 < R) issue_round(round_of(r + 1, nb), sm.buf[(r + 1) & 1], p, kpool, vpool, table, kvh);
+    if (r + 2 < R) issue_round(r + 2, nb, sm.buf[(r + 2) % NBUF], p, kpool, vpool, table, kvh);
     cp_commit();
-    cp_wait_all_but_newest();
+    cp_wait_keep2();
+    fence_proxy_async();      // this thread's copies and B-operand stores -> tensor cores
     __syncthreads();
-    const Round rd = round_of(r, nb);
-    const int c0 = rd.c0, nbc = rd.nbc;
-    int8_t(*pages)[4096] = sm.buf[r & 1];
-    if (!rd.v) {
-      // ---- pass 1: scores (warp w takes page w of the round)
-      if (warp < rd.count) {
-        const int j = rd.first + warp;
-        const int8_t *tile = pages[warp];
-        int acc0 = 0, acc1 = 0;
+    const int first = 4 * (r >> 1), count = min(4, nb - first);
+    int8_t(*pages)[4096] = sm.buf[r % NBUF];
+    if (tid == 0) {
+      fence_after();
+      if (!(r & 1)) {
+        const uint32_t a0 = su32(pages[0]), b0 = su32(sm.qt);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int4 kw = *reinterpret_cast<const int4 *>(tile + swz(lane, i));
-          const int4 q0 = *reinterpret_cast<const int4 *>(&sm.q[0][i * 16]);
-          const int4 q1 = *reinterpret_cast<const int4 *>(&sm.q[1][i * 16]);
-          acc0 = __dp4a(kw.x, q0.x, acc0); acc0 = __dp4a(kw.y, q0.y, acc0);
-          acc0 = __dp4a(kw.z, q0.z, acc0); acc0 = __dp4a(kw.w, q0.w, acc0);
-          acc1 = __dp4a(kw.x, q1.x, acc1); acc1 = __dp4a(kw.y, q1.y, acc1);
-          acc1 = __dp4a(kw.z, q1.z, acc1); acc1 = __dp4a(kw.w, q1.w, acc1);
-        }
-        const int t = (c0 + j) * 32 + lane;
-        const uint32_t page = table[c0 + j];
+        for (int ks = 0; ks < 4; ++ks)
+          mma_i8(tmem, sdesc_sw128(a0 + ks * 32), sdesc_sw128(b0 + ks * 32), ID_QK, ks != 0);
+      } else {
+        for (int q = 0; q < count; ++q)
+          mma_i8(tmem + 16 * q, sdesc_sw128(su32(pages[q])), sdesc_plain(su32(sm.pq[q]), 128, 256),
+                 ID_PV, 0);
+      }
+      mma_commit(&sm.mbar);
+      mma_ok = mbar_wait(&sm.mbar, phase, nullptr);
+      fence_before();
+    }
+    if (__syncthreads_or(!mma_ok)) {               // uniform: all threads leave together
+      if (tid == 0) atomicOr(&g_device_error, kErrMma);
+      aborted = true;
+      break;
+    }
+    phase ^= 1u;
+    fence_after();
+    if (!(r & 1)) {
+      // ---- K round: warp w takes block first + w
+      const int j = first + warp;
+      const int t = j * 32 + lane;
+      float s0 = kNegInf, s1 = kNegInf;
+      uint32_t page = 0;
+      if (warp < count) {
+        int a0, a1;
+        tmem_ld2(lane_base, a0, a1);
+        tmem_wait_ld();
+        page = table[j];
         const float ks = (t < kv_len && page < p.num_pages)
                              ? *reinterpret_cast<const float *>(
                                    p.ks + static_cast<size_t>(page) * p.scale_page_bytes +
                                    static_cast<size_t>(lane) * p.scale_row_bytes + kvh * 4)
                              : 0.0f;
-        float s0 = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(acc0), ks), sm.qs[0]), qk_scale);
-        float s1 = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(acc1), ks), sm.qs[1]), qk_scale);
-        if (t >= kv_len) s0 = s1 = kNegInf;          // decode: the row sees keys 0..kv_len-1
-        sm.S[0][j * 32 + lane] = s0;
-        sm.S[1][j * 32 + lane] = s1;
+        if (t < kv_len) {                          // decode: the row sees keys 0..kv_len-1
+          s0 = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a0), ks), qsc[0]), qk_scale);
+          s1 = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a1), ks), qsc[1]), qk_scale);
+        }
         const float b0 = warp_tree_max(s0), b1 = warp_tree_max(s1);
-        if (lane == 0) { sm.bmax[0][j] = b0; sm.bmax[1][j] = b1; }
+        if (lane == 0) { sm.bm[warp][0] = b0; sm.bm[warp][1] = b1; }
       }
-      if (rd.first + rd.count == nbc) {     // last K round of the chunk
-        __syncthreads();
-        // ---- prefix max of the block maxima (warp h scans head h)
-        if (warp < 2) {
-          const int h = warp;
-          float run = m_carry[h];
-          for (int b0 = 0; b0 < nbc; b0 += 32) {
-            const int j = b0 + lane;
-            float v = j < nbc ? sm.bmax[h][j] : kNegInf;
+      __syncthreads();
+      float mp0 = carry[0], mp1 = carry[1];        // running max before block first + warp
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const float u = __shfl_up_sync(0xffffffffu, v, o);
-              if (lane >= o) v = fmaxf(v, u);
-            }
-            v = fmaxf(v, run);
-            if (j < nbc) sm.mrun[h][j] = v;
-            run = __shfl_sync(0xffffffffu, v, 31);
-          }
+      for (int w = 0; w < 4; ++w) {
+        if (w < warp && w < count) { mp0 = fmaxf(mp0, sm.bm[w][0]); mp1 = fmaxf(mp1, sm.bm[w][1]); }
+      }
+      if (warp < count) {
+        const float mj0 = fmaxf(mp0, sm.bm[warp][0]), mj1 = fmaxf(mp1, sm.bm[warp][1]);
+        // lane 0: corr of head 0, lane 1: corr of head 1
+        const float cx = exp_ref(lane == 1 ? __fsub_rn(mp1, mj1) : __fsub_rn(mp0, mj0));
+        const float vs = (t < kv_len && page < p.num_pages)
+                             ? *reinterpret_cast<const float *>(
+                                   p.vs + static_cast<size_t>(page) * p.scale_page_bytes +
+                                   static_cast<size_t>(lane) * p.scale_row_bytes + kvh * 4)
+                             : 0.0f;
+        const float pr0 = exp_ref(__fsub_rn(s0, mj0)), pr1 = exp_ref(__fsub_rn(s1, mj1));
+        const float ps0 = warp_tree_sum(pr0), ps1 = warp_tree_sum(pr1);
+        const float pv0 = (t < kv_len) ? __fmul_rn(pr0, vs) : 0.0f;
+        const float pv1 = (t < kv_len) ? __fmul_rn(pr1, vs) : 0.0f;
+        const float pm0 = __fmul_rn(warp_tree_max(fabsf(pv0)), kInv127);
+        const float pm1 = __fmul_rn(warp_tree_max(fabsf(pv1)), kInv127);
+        int8_t *dst = sm.pq[warp] + (lane >> 4) * 128 + (lane & 15);
+        dst[0] = static_cast<int8_t>(quant1(pv0, pm0));    // row 0: head 2 kvh
+        dst[16] = static_cast<int8_t>(quant1(pv1, pm1));   // row 1: head 2 kvh + 1
+        if (lane < 2) sm.corr[lane][warp] = cx;
+        if (lane == 0) {
+          sm.psum[0][warp] = ps0; sm.psum[1][warp] = ps1;
+          sm.pmax[0][warp] = pm0; sm.pmax[1][warp] = pm1;
         }
-        __syncthreads();
-        // ---- pass 1b: probabilities, requantised P (block-parallel)
-        for (int j = warp; j < nbc; j += NW) {
-          const int t = (c0 + j) * 32 + lane;
-          const uint32_t page = table[c0 + j];
-          const float vs = (t < kv_len && page < p.num_pages)
-                               ? *reinterpret_cast<const float *>(
-                                     p.vs + static_cast<size_t>(page) * p.scale_page_bytes +
-                                     static_cast<size_t>(lane) * p.scale_row_bytes + kvh * 4)
-                               : 0.0f;
+      }
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float mj = sm.mrun[h][j];
-            const float mp = j ? sm.mrun[h][j - 1] : m_carry[h];
-            const float corr = exp_ref(__fsub_rn(mp, mj));
-            const float pr = exp_ref(__fsub_rn(sm.S[h][j * 32 + lane], mj));
-            const float ps = warp_tree_sum(pr);
-            const float pv = (t < kv_len) ? __fmul_rn(pr, vs) : 0.0f;
-            const float pm = __fmul_rn(warp_tree_max(fabsf(pv)), kInv127);
-            const int q = quant1(pv, pm);
-            sm.PQ[h][j * 32 + lane] = static_cast<int8_t>(q);   // 4 keys per word for dp4a
-            if (lane == 0) {
-              sm.corr[h][j] = corr;
-              sm.psum[h][j] = ps;
-              sm.pmax[h][j] = pm;
-            }
-          }
-        }
+      for (int w = 0; w < 4; ++w) {
+        if (w < count) { carry[0] = fmaxf(carry[0], sm.bm[w][0]); carry[1] = fmaxf(carry[1], sm.bm[w][1]); }
       }
     } else {
-      // ---- pass 2: P.V and the in-order recurrences (column-parallel)
-      // lane: column quad dq of this warp's 32 columns, key quads kg and kg + 4;
-      // 4 key rows x 4 columns are transposed with byte permutes so that one
-      // dp4a multiplies 4 keys of one column with their 4 packed P values
-      const int chunk = 2 * warp + (dq >> 2), coff = (dq & 3) << 2;
-      for (int q = 0; q < rd.count; ++q) {
-        const int j = rd.first + q;
-        const int8_t *tile = pages[q];
-        int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+      // ---- V round: column tid of both heads, blocks in order
+      int v[4][2];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int kq = kg + 4 * half;
-          int w[4];
+      for (int q = 0; q < 4; ++q)
+        if (q < count) tmem_ld2(lane_base + 16 * q, v[q][0], v[q][1]);
+      tmem_wait_ld();
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const int row = 4 * kq + r;
-            w[r] = *reinterpret_cast<const int *>(tile + row * 128 + ((chunk ^ (row & 7)) << 4) + coff);
-          }
-          const int lo01 = __byte_perm(w[0], w[1], 0x5140), hi01 = __byte_perm(w[0], w[1], 0x7362);
-          const int lo23 = __byte_perm(w[2], w[3], 0x5140), hi23 = __byte_perm(w[2], w[3], 0x7362);
-          const int t[4] = {__byte_perm(lo01, lo23, 0x5410), __byte_perm(lo01, lo23, 0x7632),
-                            __byte_perm(hi01, hi23, 0x5410), __byte_perm(hi01, hi23, 0x7632)};
-          const int p0 = *reinterpret_cast<const int *>(&sm.PQ[0][j * 32 + 4 * kq]);
-          const int p1 = *reinterpret_cast<const int *>(&sm.PQ[1][j * 32 + 4 * kq]);
+      for (int q = 0; q < 4; ++q) {
+        if (q < count) {
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            a0[b] = __dp4a(t[b], p0, a0[b]);
-            a1[b] = __dp4a(t[b], p1, a1[b]);
+          for (int h = 0; h < 2; ++h) {
+            const float c = sm.corr[h][q];
+            den[h] = __fadd_rn(__fmul_rn(den[h], c), sm.psum[h][q]);
+            res[h] = __fadd_rn(__fmul_rn(res[h], c), __fmul_rn(i2f_small(v[q][h]), sm.pmax[h][q]));
           }
         }
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-#pragma unroll
-          for (int o = 8; o < 32; o <<= 1) {
-            a0[b] += __shfl_xor_sync(0xffffffffu, a0[b], o);
-            a1[b] += __shfl_xor_sync(0xffffffffu, a1[b], o);
-          }
-        }
-        const int sel = (kg & 1) * 2;
-        const int e0 = my_h ? (sel ? a1[2] : a1[0]) : (sel ? a0[2] : a0[0]);
-        const int e1 = my_h ? (sel ? a1[3] : a1[1]) : (sel ? a0[3] : a0[1]);
-        const float corr = sm.corr[my_h][j], pm = sm.pmax[my_h][j];
-        res[0] = __fadd_rn(__fmul_rn(res[0], corr), __fmul_rn(i2f_small(e0), pm));
-        res[1] = __fadd_rn(__fmul_rn(res[1], corr), __fmul_rn(i2f_small(e1), pm));
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          den_h[h] = __fadd_rn(__fmul_rn(den_h[h], sm.corr[h][j]), sm.psum[h][j]);
-      }
-      if (rd.first + rd.count == nbc) {      // last V round: carry the running max
-        m_carry[0] = sm.mrun[0][nbc - 1];
-        m_carry[1] = sm.mrun[1][nbc - 1];
       }
     }
-    __syncthreads();   // buffer (r & 1) and the chunk arrays are reused afterwards
+    fence_before();   // TMEM reads ordered before the next round's barrier and MMA
   }
+  cp_wait_all();
+  if (aborted && tid == 0) mbar_wait(&sm.mbar, phase, nullptr);   // drain, bounded
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 0) tmem_dealloc<TMEM_COLS>(tmem);
+  if (aborted) return;
 
   // ---- 1/den, per-head output quantisation (attention_gqa.h:522-546)
-  const float rden = __fdiv_rn(1.0f, den_h[my_h]);
-  const float o0 = __fmul_rn(res[0], rden), o1 = __fmul_rn(res[1], rden);
-  float mx = fmaxf(fabsf(o0), fabsf(o1));
-  // lanes of the same head differ in bits 0..3 of the lane id (dq and kg & 1)
+  float o[2], mx[2];
 #pragma unroll
-  for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((lane & 15) == 0) sm.red[warp][lane >> 4] = mx;
+  for (int h = 0; h < 2; ++h) {
+    o[h] = __fmul_rn(res[h], __fdiv_rn(1.0f, den[h]));
+    float m = fabsf(o[h]);
+#pragma unroll
+    for (int k = 1; k < 32; k <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, k));
+    mx[h] = m;
+  }
+  if (lane == 0) { sm.red[warp][0] = mx[0]; sm.red[warp][1] = mx[1]; }
   __syncthreads();
-  float hm = 0.0f;
 #pragma unroll
-  for (int w = 0; w < NW; ++w) hm = fmaxf(hm, sm.red[w][my_h]);
-  const float scale = __fmul_rn(hm, kInv127);
-  const int h = kvh * 2 + my_h;
-  char2 qv;
-  qv.x = static_cast<char>(quant1(o0, scale));
-  qv.y = static_cast<char>(quant1(o1, scale));
-  *reinterpret_cast<char2 *>(p.o8 + static_cast<long>(seq) * p.o_rb + h * 128 + my_d0) = qv;
-  if (warp == 0 && (lane & 15) == 0)
-    *reinterpret_cast<float *>(p.os + static_cast<long>(seq) * p.os_rb + h * 4) = scale;
+  for (int h = 0; h < 2; ++h) {
+    float hm = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) hm = fmaxf(hm, sm.red[w][h]);
+    const float scale = __fmul_rn(hm, kInv127);
+    const int hd = kvh * 2 + h;
+    p.o8[static_cast<long>(seq) * p.o_rb + hd * 128 + tid] = static_cast<char>(quant1(o[h], scale));
+    if (tid == 0) *reinterpret_cast<float *>(p.os + static_cast<long>(seq) * p.os_rb + hd * 4) = scale;
+  }
 }
 
 }  // namespace dec
@@ -328,7 +299,7 @@ int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const v
   if (p.row_bytes % 16 || p.page_bytes % 16 || reinterpret_cast<uintptr_t>(k_pool) % 16 ||
       reinterpret_cast<uintptr_t>(v_pool) % 16)
     return Q3_ERR_ALIGN;
-  const size_t smem = sizeof(dec::Smem);
+  const size_t smem = sizeof(dec::Smem) + 1024;   // + alignment slack
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {

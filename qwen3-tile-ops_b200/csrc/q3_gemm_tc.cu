@@ -23,6 +23,7 @@
 
 #include "q3_common.cuh"
 #include "q3_gemm.h"
+#include "q3_tc.cuh"
 
 namespace q3 {
 
@@ -71,98 +72,8 @@ struct __align__(1024) Smem {
   int abort;
 };
 
-__device__ __forceinline__ uint32_t su32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(unsigned long long *b, unsigned c) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(c) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(unsigned long long *b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(unsigned long long *b, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ uint64_t gtime() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// bounded wait for the completion of the phase with parity `par`
-__device__ __forceinline__ bool mbar_wait(unsigned long long *b, uint32_t par, const int *abort) {
-  const uint32_t a = su32(b);
-  uint64_t t0 = 0;
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(a), "r"(par)
-        : "memory");
-    if (ok) return true;
-    if ((it & 127) == 0) {
-      if (abort && *reinterpret_cast<const volatile int *>(abort)) return false;
-      const uint64_t t = gtime();
-      if (t0 == 0) t0 = t;
-      else if (t - t0 > 1000000000ull) return false;
-    }
-  }
-}
-__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *m, int x, int y,
-                                       unsigned long long *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(su32(dst)),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(su32(bar))
-      : "memory");
-}
-// shared-memory matrix descriptor: K-major, 128B swizzle, 8-row atoms 1024 B apart
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
-  uint64_t d = (saddr & 0x3FFFFu) >> 4;
-  d |= 1ull << 16;                   // leading byte offset (unused for swizzled K-major)
-  d |= (1024ull >> 4) << 32;         // stride byte offset: next 8-row atom
-  d |= 1ull << 46;                   // descriptor version for tcgen05
-  d |= 2ull << 61;                   // 128-byte swizzle
-  return d;
-}
-// instruction descriptor: s32 accumulate, s8 x s8, both K-major, M = 128, N = ntok
-__host__ __device__ constexpr uint32_t idesc_i8(int ntok) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(ntok >> 3) << 17) |
-         ((128u >> 4) << 24);
-}
-__device__ __forceinline__ void mma_i8(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t id,
-                                       uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(dt),
-      "l"(ad), "l"(bd), "r"(id), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(unsigned long long *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15},"
-      " [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-        "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
+using namespace tcx;
+
 __device__ __forceinline__ void epi_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
 }
@@ -274,7 +185,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               const uint32_t dt = tmem + (buf * C::NACC + a) * NTOK;
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
-                mma_i8(dt, sdesc(sa + a * C::A_BYTES + ks * 32), sdesc(sb + ks * 32), ID,
+                mma_i8(dt, sdesc_sw128(sa + a * C::A_BYTES + ks * 32), sdesc_sw128(sb + ks * 32), ID,
                        (box | ks) != 0);
             }
             mma_commit(&sm.empty[st]);          // frees the stage when these MMAs finish
@@ -641,7 +552,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t sa = su32(sm.a[b][a]);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            mma_i8(tmem + a * NTOK, sdesc(sa + ks * 32), sdesc(sb + ks * 32), ID, (b | ks) != 0);
+            mma_i8(tmem + a * NTOK, sdesc_sw128(sa + ks * 32), sdesc_sw128(sb + ks * 32), ID, (b | ks) != 0);
         }
       }
       mma_commit(&sm.tfull);          // completes once every MMA issued has finished
