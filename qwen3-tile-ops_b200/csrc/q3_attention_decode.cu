@@ -12,21 +12,24 @@
 //     den_j = (den_{j-1} * corr_j) + psum_j,  res_j = (res_{j-1} * corr_j) + part_j
 // run in block order, with exactly the reference's two roundings each.
 //
-// CTA = one (sequence, kv head), 4 warps; the two q heads of the GQA group
-// share every K/V page.  Pages (32 tokens x 128 bytes of this kv head) stream
-// through three buffers of "rounds" of 4 pages with cp.async (16 bytes per
-// thread, rows stored in the tensor cores' 128-byte swizzle); rounds alternate
-// K and V over the same 4 blocks, two rounds ahead of the one in use.
-//   K round  one tcgen05.mma chain (M = 128 keys, N = 16, K = 128) gives q.k of
-//            both heads for the 4 pages in TMEM; warp w takes page w: scale,
-//            mask, block max, prefix max, then p / psum / pmax / pq and corr.
-//   V round  per page one tcgen05.mma with A = V read MN-major (M = 128 value
-//            columns, K = 32 keys) and B = the pq rows of both heads, so thread
-//            d of the CTA gets the int32 P.V of column d for both heads and runs
-//            the recurrences over the round's blocks in order.
-// All int32 products are exact, so the tensor cores change no bit.  Thread 0
-// waits for each MMA completion with a bound; the outcome reaches the other
-// threads through the barrier, and a timeout sets a bit of the device error word.
+// CTA = one (sequence, kv head); the two q heads of the GQA group share every
+// K/V page.  Blocks go in groups of 4 pages (128 keys).  Warp roles:
+//   warp 4    producer: cp.async of the K pages (ring of 2 groups) and the V
+//             pages (ring of 1) into shared memory, rows in the tensor cores'
+//             128-byte swizzle; completion is tracked by mbarriers
+//             (cp.async.mbarrier.arrive), so nothing blocks on a copy group.
+//   warp 5    MMA issuer (one lane): QK(g) = K tile (M = 128 keys, K = 128) x
+//             the two q rows (N = 16) into one of two TMEM slots; PV(g) = V tile
+//             read MN-major (M = 128 value columns, K = 128 keys) x pq, where row
+//             2q+h of pq holds block q's requantised probabilities for head h in
+//             block q's 32 keys and zeros elsewhere, so column 2q+h of the result
+//             is block q's int32 P.V.  QK runs one group ahead of PV.
+//   warps 0-3 softmax: warp w takes block w of each group (scale, mask, block
+//             max, prefix max, corr, p, psum, pmax, pq); then, with thread
+//             d = value column d, the recurrences of the previous group in order.
+// All int32 products are exact, so the tensor cores change no bit.  Every
+// wait is bounded (about one second); a timeout sets a bit of the device error
+// word, the roles stop, copies and MMAs in flight are drained and TMEM freed.
 #include <mutex>
 
 #include "q3_attention.h"
@@ -41,59 +44,48 @@ namespace dec {
 
 using namespace tcx;
 
-constexpr int NW = 4;               // warps
-constexpr int THREADS = NW * 32;
-constexpr int NBUF = 3;             // round buffers (two rounds in flight)
-constexpr int TMEM_COLS = 64;       // K round: 16 columns; V round: 16 per page
-constexpr unsigned kErrPage = 2u;   // a page index >= num_pages (copy skipped)
-constexpr unsigned kErrTable = 4u;  // kv_len needs more pages than the table holds
-constexpr unsigned kErrMma = 8u;    // a tensor-core completion wait timed out
+constexpr int NCW = 4;                  // softmax warps
+constexpr int THREADS = (NCW + 2) * 32;
+constexpr int PRODUCER = NCW, MMA_WARP = NCW + 1;
+constexpr int TMEM_COLS = 64;           // QK slots at 0 and 16, PV slots at 32 and 48
+constexpr unsigned kErrPage = 2u;       // a page index >= num_pages (copy skipped)
+constexpr unsigned kErrTable = 4u;      // kv_len needs more pages than the table holds
+constexpr unsigned kErrWait = 8u;       // a pipeline wait timed out
 constexpr uint32_t ID_QK = idesc_i8(16);          // A = keys (K-major), B = q rows
 constexpr uint32_t ID_PV = idesc_i8(16, true);    // A = V (MN-major), B = pq rows
 
 struct Smem {
-  alignas(1024) int8_t buf[NBUF][4][4096];   // page tiles, 128-byte swizzled rows
-  alignas(1024) int8_t qt[2048];             // B of the K round: rows 0,1 = q heads, rest 0
-  alignas(1024) int8_t pq[4][512];           // B of the V round per page: [row group][k half][8 rows][16 B]
-  float bm[4][2];                            // block maxima of the K round
-  float corr[2][4], psum[2][4], pmax[2][4];  // per head, per page of the round
-  float red[NW][2];
-  unsigned long long mbar;
+  alignas(1024) int8_t kbuf[2][4][4096];  // K pages of a group, 128-byte swizzled rows
+  alignas(1024) int8_t vbuf[4][4096];     // V pages of a group
+  // B operands, 8 rows each; rows 8..15 of N = 16 alias rows 0..7 (stride offset 0)
+  alignas(1024) int8_t qt[1024];          // 128-byte swizzled: rows 0,1 = q heads
+  alignas(1024) int8_t pq[2][1024];       // no swizzle: [16-key chunk][8 rows][16 B]
+  float bm[2][NCW][2];                    // block maxima
+  float corr[2][2][4], psum[2][2][4], pmax[2][2][4];   // [slot][head][block]
+  float red[NCW][2];
+  unsigned long long kfull[2], kempty[2], vfull, vempty;
+  unsigned long long qk_done[2], pv_done[2], pq_ready[2], bm_ready[2], mma_final;
   uint32_t tmem_base;
+  int abort;
 };
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src)
                : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_keep2() {
-  asm volatile("cp.async.wait_group 2;" ::: "memory");
+// arrive on `b` once every cp.async this thread issued so far has landed
+__device__ __forceinline__ void cp_arrive(unsigned long long *b) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(su32(b)) : "memory");
 }
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-// byte offset of 16-byte chunk `i` of row `r` in a swizzled 32x128 page tile
-__device__ __forceinline__ int swz(int r, int i) { return r * 128 + (((i ^ (r & 7))) << 4); }
-
-// each of the 128 threads copies 2 x 16 bytes of every page of round r
-// (rounds: 2g = K pages of blocks 4g..4g+3, 2g+1 = V pages of the same blocks)
-__device__ __forceinline__ void issue_round(int r, int nb, int8_t (*dst)[4096],
-                                            const DecodeAttnArgs &p, const char *kpool,
-                                            const char *vpool, const uint16_t *table, int kvh) {
-  const int t = threadIdx.x;
-  const int row = t >> 2, c0 = (t & 3) * 2;
-  const int first = 4 * (r >> 1), count = min(4, nb - first);
-  const char *pool = (r & 1) ? vpool : kpool;
-  const size_t off = static_cast<size_t>(row) * p.row_bytes + kvh * 128 + c0 * 16;
-  for (int q = 0; q < count; ++q) {
-    const uint32_t page = table[first + q];
-    if (page >= p.num_pages) {
-      if (t == 0) atomicOr(&g_device_error, kErrPage);
-      continue;
-    }
-    const char *src = pool + static_cast<size_t>(page) * p.page_bytes + off;
-    cp_async16(dst[q] + swz(row, c0), src);
-    cp_async16(dst[q] + swz(row, c0 + 1), src + 16);
-  }
+__device__ __forceinline__ void softmax_sync() {   // the 4 softmax warps only
+  asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
+}
+__device__ __forceinline__ bool wait_or_abort(unsigned long long *b, uint32_t par, Smem &sm) {
+  if (mbar_wait(b, par, &sm.abort)) return true;
+  if (!*reinterpret_cast<volatile int *>(&sm.abort)) atomicOr(&g_device_error, kErrWait);
+  *reinterpret_cast<volatile int *>(&sm.abort) = 1;
+  return false;
 }
 
 __global__ void __launch_bounds__(THREADS, 4)
@@ -108,164 +100,238 @@ __global__ void __launch_bounds__(THREADS, 4)
   const int kv_len = p.kv_len[seq];
   const int nb = (kv_len + 31) >> 5;
   const uint16_t *table = p.table + static_cast<long>(seq) * p.table_stride;
-  const float qk_scale = p.qk_scale;
   if (kv_len <= 0 || nb > p.table_stride) {        // uniform for the whole CTA
     if (tid == 0) atomicOr(&g_device_error, kErrTable);
     return;
   }
-  const int R = 2 * ((nb + 3) >> 2);               // K and V rounds
-  issue_round(0, nb, sm.buf[0], p, kpool, vpool, table, kvh);
-  cp_commit();
-  issue_round(1, nb, sm.buf[1], p, kpool, vpool, table, kvh);   // R >= 2 always
-  cp_commit();
+  const int G = (nb + 3) >> 2;                     // groups of 4 blocks
 
-  // operand B of both products: rows 2..15 stay zero
-  for (int i = 256 + tid * 4; i < 2048; i += THREADS * 4) *reinterpret_cast<int *>(sm.qt + i) = 0;
-  for (int i = tid * 4; i < 4 * 512; i += THREADS * 4) *reinterpret_cast<int *>(&sm.pq[0][0] + i) = 0;
-  float qsc[2];
-  {
-    const int hh = tid >> 5;                       // threads 0..63: q rows of the two heads
-    if (hh < 2) {
-      const int h = kvh * 2 + hh;
-      const int v = reinterpret_cast<const int *>(p.q8 + static_cast<long>(seq) * p.q_rb + h * 128)[lane];
-      *reinterpret_cast<int *>(sm.qt + hh * 128 + (((lane >> 2) ^ hh) << 4) + (lane & 3) * 4) = v;
-    }
-    qsc[0] = *reinterpret_cast<const float *>(p.qs + static_cast<long>(seq) * p.qs_rb + kvh * 8);
-    qsc[1] = *reinterpret_cast<const float *>(p.qs + static_cast<long>(seq) * p.qs_rb + kvh * 8 + 4);
+  // ---- set-up: B operands (zero except the rows written later), barriers, TMEM
+  for (int i = tid * 4; i < 1024; i += THREADS * 4) {
+    if (i >= 256) *reinterpret_cast<int *>(sm.qt + i) = 0;
+    *reinterpret_cast<int *>(sm.pq[0] + i) = 0;
+    *reinterpret_cast<int *>(sm.pq[1] + i) = 0;
+  }
+  if (tid < 64) {                                  // q rows of the two heads
+    const int hh = tid >> 5, h = kvh * 2 + hh;
+    const int v = reinterpret_cast<const int *>(p.q8 + static_cast<long>(seq) * p.q_rb + h * 128)[lane];
+    *reinterpret_cast<int *>(sm.qt + hh * 128 + (((lane >> 2) ^ hh) << 4) + (lane & 3) * 4) = v;
   }
   if (tid == 0) {
-    mbar_init(&sm.mbar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.kfull[i], 32);
+      mbar_init(&sm.kempty[i], 1);
+      mbar_init(&sm.qk_done[i], 1);
+      mbar_init(&sm.pv_done[i], 1);
+      mbar_init(&sm.pq_ready[i], NCW * 32);
+      mbar_init(&sm.bm_ready[i], NCW);
+    }
+    mbar_init(&sm.vfull, 32);
+    mbar_init(&sm.vempty, 1);
+    mbar_init(&sm.mma_final, 1);
+    sm.abort = 0;
     mbar_init_fence();
   }
+  fence_proxy_async();                             // qt / pq stores -> tensor cores
   if (warp == 0) tmem_alloc<TMEM_COLS>(&sm.tmem_base);
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 
-  float carry[2] = {kNegFltMax, kNegFltMax};
-  float den[2] = {0.0f, 0.0f}, res[2] = {0.0f, 0.0f};   // thread = value column tid
-  uint32_t phase = 0;
-  bool mma_ok = true;       // thread 0's view of the last completion wait
-  bool aborted = false;     // uniform
+  float den[2] = {0.0f, 0.0f}, res[2] = {0.0f, 0.0f};   // softmax threads: value column tid
 
-  for (int r = 0; r < R; ++r) {
-    if (r + 2 < R) issue_round(r + 2, nb, sm.buf[(r + 2) % NBUF], p, kpool, vpool, table, kvh);
-    cp_commit();
-    cp_wait_keep2();
-    fence_proxy_async();      // this thread's copies and B-operand stores -> tensor cores
-    __syncthreads();
-    const int first = 4 * (r >> 1), count = min(4, nb - first);
-    int8_t(*pages)[4096] = sm.buf[r % NBUF];
-    if (tid == 0) {
-      fence_after();
-      if (!(r & 1)) {
-        const uint32_t a0 = su32(pages[0]), b0 = su32(sm.qt);
+  if (warp == PRODUCER) {
+    // ---- producer: K(0), K(1), V(0), K(2), V(1), ..., K(G-1), V(G-2), V(G-1)
+    const int r4 = lane >> 3, c16 = lane & 7;     // lane: 16-byte chunk c16 of rows 4i + r4
+    for (int it = 0; it < 2 * G; ++it) {
+      int g, isv;
+      if (it == 0) { g = 0; isv = 0; }
+      else if (it == 2 * G - 1) { g = G - 1; isv = 1; }
+      else { g = (it + 1) >> 1; isv = !(it & 1); if (isv) g -= 1; }
+      // it odd -> K((it+1)/2), it even (>0) -> V(it/2 - 1)
+      unsigned long long *full;
+      int8_t(*dst)[4096];
+      if (!isv) {
+        const int slot = g & 1;
+        if (g >= 2 && !wait_or_abort(&sm.kempty[slot], ((g >> 1) - 1) & 1, sm)) break;
+        full = &sm.kfull[slot];
+        dst = sm.kbuf[slot];
+      } else {
+        if (g >= 1 && !wait_or_abort(&sm.vempty, (g - 1) & 1, sm)) break;
+        full = &sm.vfull;
+        dst = sm.vbuf;
+      }
+      const char *pool = isv ? vpool : kpool;
+      const int first = 4 * g, count = min(4, nb - first);
+      for (int q = 0; q < count; ++q) {
+        const uint32_t page = table[first + q];
+        if (page >= p.num_pages) {
+          if (lane == 0) atomicOr(&g_device_error, kErrPage);
+          continue;
+        }
+        const char *src = pool + static_cast<size_t>(page) * p.page_bytes + kvh * 128 + c16 * 16;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {              // 4 whole rows per instruction
+          const int row = 4 * i + r4;
+          cp_async16(dst[q] + row * 128 + ((c16 ^ (row & 7)) << 4), src + static_cast<size_t>(row) * p.row_bytes);
+        }
+      }
+      cp_arrive(full);
+    }
+    cp_wait_all();
+  } else if (warp == MMA_WARP) {
+    // ---- MMA issuer: QK(0), then per g: QK(g+1), PV(g)
+    if (lane == 0) {
+      const uint32_t bq = su32(sm.qt);
+      bool ok = true;
+      auto issue_qk = [&](int g) -> bool {
+        const int slot = g & 1;
+        if (!wait_or_abort(&sm.kfull[slot], (g >> 1) & 1, sm)) return false;
+        fence_after();
+        const uint32_t a0 = su32(sm.kbuf[slot][0]);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          mma_i8(tmem, sdesc_sw128(a0 + ks * 32), sdesc_sw128(b0 + ks * 32), ID_QK, ks != 0);
-      } else {
-        for (int q = 0; q < count; ++q)
-          mma_i8(tmem + 16 * q, sdesc_sw128(su32(pages[q])), sdesc_plain(su32(sm.pq[q]), 128, 256),
-                 ID_PV, 0);
+          mma_i8(tmem + 16 * slot, sdesc_sw128(a0 + ks * 32), sdesc_sw128(bq + ks * 32, 0), ID_QK,
+                 ks != 0);
+        mma_commit(&sm.qk_done[slot]);
+        mma_commit(&sm.kempty[slot]);
+        return true;
+      };
+      ok = issue_qk(0);
+      for (int g = 0; g < G && ok; ++g) {
+        if (g + 1 < G && !(ok = issue_qk(g + 1))) break;
+        const int slot = g & 1;
+        if (!(ok = wait_or_abort(&sm.vfull, g & 1, sm))) break;
+        if (!(ok = wait_or_abort(&sm.pq_ready[slot], (g >> 1) & 1, sm))) break;
+        fence_after();
+        const int count = min(4, nb - 4 * g);
+        const uint32_t a0 = su32(sm.vbuf[0]), b0 = su32(sm.pq[slot]);
+        for (int q = 0; q < count; ++q)          // k-step q = block q's 32 keys
+          mma_i8(tmem + 32 + 16 * slot, sdesc_sw128(a0 + q * 4096), sdesc_plain(b0 + q * 256, 128, 0),
+                 ID_PV, q != 0);
+        mma_commit(&sm.pv_done[slot]);
+        mma_commit(&sm.vempty);
       }
-      mma_commit(&sm.mbar);
-      mma_ok = mbar_wait(&sm.mbar, phase, nullptr);
-      fence_before();
+      mma_commit(&sm.mma_final);                   // every MMA issued above has completed
+      mbar_wait(&sm.mma_final, 0, nullptr);        // bounded
     }
-    if (__syncthreads_or(!mma_ok)) {               // uniform: all threads leave together
-      if (tid == 0) atomicOr(&g_device_error, kErrMma);
-      aborted = true;
-      break;
-    }
-    phase ^= 1u;
-    fence_after();
-    if (!(r & 1)) {
-      // ---- K round: warp w takes block first + w
-      const int j = first + warp;
-      const int t = j * 32 + lane;
-      float s0 = kNegInf, s1 = kNegInf;
-      uint32_t page = 0;
-      if (warp < count) {
-        int a0, a1;
-        tmem_ld2(lane_base, a0, a1);
-        tmem_wait_ld();
-        page = table[j];
-        const float ks = (t < kv_len && page < p.num_pages)
-                             ? *reinterpret_cast<const float *>(
-                                   p.ks + static_cast<size_t>(page) * p.scale_page_bytes +
-                                   static_cast<size_t>(lane) * p.scale_row_bytes + kvh * 4)
-                             : 0.0f;
-        if (t < kv_len) {                          // decode: the row sees keys 0..kv_len-1
-          s0 = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a0), ks), qsc[0]), qk_scale);
-          s1 = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a1), ks), qsc[1]), qk_scale);
-        }
-        const float b0 = warp_tree_max(s0), b1 = warp_tree_max(s1);
-        if (lane == 0) { sm.bm[warp][0] = b0; sm.bm[warp][1] = b1; }
-      }
-      __syncthreads();
-      float mp0 = carry[0], mp1 = carry[1];        // running max before block first + warp
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        if (w < warp && w < count) { mp0 = fmaxf(mp0, sm.bm[w][0]); mp1 = fmaxf(mp1, sm.bm[w][1]); }
-      }
-      if (warp < count) {
-        const float mj0 = fmaxf(mp0, sm.bm[warp][0]), mj1 = fmaxf(mp1, sm.bm[warp][1]);
-        // lane 0: corr of head 0, lane 1: corr of head 1
-        const float cx = exp_ref(lane == 1 ? __fsub_rn(mp1, mj1) : __fsub_rn(mp0, mj0));
-        const float vs = (t < kv_len && page < p.num_pages)
-                             ? *reinterpret_cast<const float *>(
-                                   p.vs + static_cast<size_t>(page) * p.scale_page_bytes +
-                                   static_cast<size_t>(lane) * p.scale_row_bytes + kvh * 4)
-                             : 0.0f;
-        const float pr0 = exp_ref(__fsub_rn(s0, mj0)), pr1 = exp_ref(__fsub_rn(s1, mj1));
-        const float ps0 = warp_tree_sum(pr0), ps1 = warp_tree_sum(pr1);
-        const float pv0 = (t < kv_len) ? __fmul_rn(pr0, vs) : 0.0f;
-        const float pv1 = (t < kv_len) ? __fmul_rn(pr1, vs) : 0.0f;
-        const float pm0 = __fmul_rn(warp_tree_max(fabsf(pv0)), kInv127);
-        const float pm1 = __fmul_rn(warp_tree_max(fabsf(pv1)), kInv127);
-        int8_t *dst = sm.pq[warp] + (lane >> 4) * 128 + (lane & 15);
-        dst[0] = static_cast<int8_t>(quant1(pv0, pm0));    // row 0: head 2 kvh
-        dst[16] = static_cast<int8_t>(quant1(pv1, pm1));   // row 1: head 2 kvh + 1
-        if (lane < 2) sm.corr[lane][warp] = cx;
-        if (lane == 0) {
-          sm.psum[0][warp] = ps0; sm.psum[1][warp] = ps1;
-          sm.pmax[0][warp] = pm0; sm.pmax[1][warp] = pm1;
+    __syncwarp();
+  } else {
+    // ---- softmax warps
+    const float qs0 = *reinterpret_cast<const float *>(p.qs + static_cast<long>(seq) * p.qs_rb + kvh * 8);
+    const float qs1 = *reinterpret_cast<const float *>(p.qs + static_cast<long>(seq) * p.qs_rb + kvh * 8 + 4);
+    const float qk_scale = p.qk_scale;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    float carry0 = kNegFltMax, carry1 = kNegFltMax;
+    // scales of block (g, warp), loaded one group ahead
+    auto load_scales = [&](int g, float &ks, float &vs) {
+      const int j = 4 * g + warp, t = j * 32 + lane;
+      ks = vs = 0.0f;
+      if (j < nb && t < kv_len) {
+        const uint32_t page = table[j];
+        if (page < p.num_pages) {
+          const size_t o = static_cast<size_t>(page) * p.scale_page_bytes +
+                           static_cast<size_t>(lane) * p.scale_row_bytes + kvh * 4;
+          ks = *reinterpret_cast<const float *>(p.ks + o);
+          vs = *reinterpret_cast<const float *>(p.vs + o);
         }
       }
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        if (w < count) { carry[0] = fmaxf(carry[0], sm.bm[w][0]); carry[1] = fmaxf(carry[1], sm.bm[w][1]); }
-      }
-    } else {
-      // ---- V round: column tid of both heads, blocks in order
-      int v[4][2];
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (q < count) tmem_ld2(lane_base + 16 * q, v[q][0], v[q][1]);
+    };
+    auto recur = [&](int g) -> bool {
+      const int slot = g & 1, count = min(4, nb - 4 * g);
+      if (!wait_or_abort(&sm.pv_done[slot], (g >> 1) & 1, sm)) return false;
+      fence_after();
+      int v[8];
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                   : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                     "=r"(v[6]), "=r"(v[7])
+                   : "r"(lane_base + 32 + 16 * slot));
       tmem_wait_ld();
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (q < count) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const float c = sm.corr[h][q];
-            den[h] = __fadd_rn(__fmul_rn(den[h], c), sm.psum[h][q]);
-            res[h] = __fadd_rn(__fmul_rn(res[h], c), __fmul_rn(i2f_small(v[q][h]), sm.pmax[h][q]));
+            const float c = sm.corr[slot][h][q];
+            den[h] = __fadd_rn(__fmul_rn(den[h], c), sm.psum[slot][h][q]);
+            res[h] = __fadd_rn(__fmul_rn(res[h], c),
+                               __fmul_rn(i2f_small(v[2 * q + h]), sm.pmax[slot][h][q]));
           }
         }
       }
+      return true;
+    };
+    float ks_n, vs_n;
+    load_scales(0, ks_n, vs_n);
+    bool ok = true;
+    for (int g = 0; g < G && ok; ++g) {
+      const int slot = g & 1, count = min(4, nb - 4 * g);
+      const int j = 4 * g + warp, t = j * 32 + lane;
+      const float ks = ks_n, vs = vs_n;
+      if (g + 1 < G) load_scales(g + 1, ks_n, vs_n);
+      if (!(ok = wait_or_abort(&sm.qk_done[slot], (g >> 1) & 1, sm))) break;
+      fence_after();
+      float s0 = kNegInf, s1 = kNegInf;
+      if (warp < count) {
+        int a0, a1;
+        tmem_ld2(lane_base + 16 * slot, a0, a1);
+        tmem_wait_ld();
+        if (t < kv_len) {                          // decode: the row sees keys 0..kv_len-1
+          s0 = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a0), ks), qs0), qk_scale);
+          s1 = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a1), ks), qs1), qk_scale);
+        }
+        const float b0 = warp_tree_max(s0), b1 = warp_tree_max(s1);
+        if (lane == 0) { sm.bm[slot][warp][0] = b0; sm.bm[slot][warp][1] = b1; }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.bm_ready[slot]);
+      if (!(ok = wait_or_abort(&sm.bm_ready[slot], (g >> 1) & 1, sm))) break;
+      float mp0 = carry0, mp1 = carry1;            // running max before block j
+#pragma unroll
+      for (int w = 0; w < NCW; ++w) {
+        if (w < count) {
+          const float c0 = sm.bm[slot][w][0], c1 = sm.bm[slot][w][1];
+          if (w < warp) { mp0 = fmaxf(mp0, c0); mp1 = fmaxf(mp1, c1); }
+          carry0 = fmaxf(carry0, c0);
+          carry1 = fmaxf(carry1, c1);
+        }
+      }
+      if (warp < count) {
+        const float mj0 = fmaxf(mp0, sm.bm[slot][warp][0]), mj1 = fmaxf(mp1, sm.bm[slot][warp][1]);
+        // lane 0: corr of head 0, lane 1: corr of head 1
+        const float cx = exp_ref(lane == 1 ? __fsub_rn(mp1, mj1) : __fsub_rn(mp0, mj0));
+        const float pr0 = exp_ref(__fsub_rn(s0, mj0)), pr1 = exp_ref(__fsub_rn(s1, mj1));
+        const float ps0 = warp_tree_sum(pr0), ps1 = warp_tree_sum(pr1);
+        const float pv0 = (t < kv_len) ? __fmul_rn(pr0, vs) : 0.0f;
+        const float pv1 = (t < kv_len) ? __fmul_rn(pr1, vs) : 0.0f;
+        const float pm0 = __fmul_rn(warp_tree_max(fabsf(pv0)), kInv127);
+        const float pm1 = __fmul_rn(warp_tree_max(fabsf(pv1)), kInv127);
+        // row 2w+h, keys of block w = 16-key chunks 2w and 2w+1
+        int8_t *dst = sm.pq[slot] + (2 * warp + (lane >> 4)) * 128 + 2 * warp * 16 + (lane & 15);
+        dst[0] = static_cast<int8_t>(quant1(pv0, pm0));
+        dst[16] = static_cast<int8_t>(quant1(pv1, pm1));
+        if (lane < 2) sm.corr[slot][lane][warp] = cx;
+        if (lane == 0) {
+          sm.psum[slot][0][warp] = ps0; sm.psum[slot][1][warp] = ps1;
+          sm.pmax[slot][0][warp] = pm0; sm.pmax[slot][1][warp] = pm1;
+        }
+      }
+      fence_proxy_async();                         // pq stores -> tensor cores
+      fence_before();                              // QK slot reads done
+      mbar_arrive(&sm.pq_ready[slot]);
+      if (g >= 1 && !(ok = recur(g - 1))) break;
+      fence_before();
     }
-    fence_before();   // TMEM reads ordered before the next round's barrier and MMA
+    if (ok) ok = recur(G - 1);
+    fence_before();
   }
-  cp_wait_all();
-  if (aborted && tid == 0) mbar_wait(&sm.mbar, phase, nullptr);   // drain, bounded
+
   fence_before();
   __syncthreads();
   fence_after();
   if (warp == 0) tmem_dealloc<TMEM_COLS>(tmem);
-  if (aborted) return;
+  if (*reinterpret_cast<volatile int *>(&sm.abort) || warp >= NCW) return;
 
   // ---- 1/den, per-head output quantisation (attention_gqa.h:522-546)
   float o[2], mx[2];
@@ -278,12 +344,12 @@ __global__ void __launch_bounds__(THREADS, 4)
     mx[h] = m;
   }
   if (lane == 0) { sm.red[warp][0] = mx[0]; sm.red[warp][1] = mx[1]; }
-  __syncthreads();
+  softmax_sync();
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     float hm = 0.0f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) hm = fmaxf(hm, sm.red[w][h]);
+    for (int w = 0; w < NCW; ++w) hm = fmaxf(hm, sm.red[w][h]);
     const float scale = __fmul_rn(hm, kInv127);
     const int hd = kvh * 2 + h;
     p.o8[static_cast<long>(seq) * p.o_rb + hd * 128 + tid] = static_cast<char>(quant1(o[h], scale));
