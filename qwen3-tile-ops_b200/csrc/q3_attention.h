@@ -48,7 +48,9 @@ struct DecodeAttnArgs {
   uint32_t num_pages;            // pages in the pool (page indices are checked)
 };
 
+// pdl: launched as a programmatic dependent of the kernel before it
 int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const void *v_pool,
-                            uint32_t num_pages, int kv_heads, int n_seqs, cudaStream_t s);
+                            uint32_t num_pages, int kv_heads, int n_seqs, cudaStream_t s,
+                            bool pdl = false);
 
 }  // namespace q3

@@ -47,6 +47,7 @@ using namespace tcx;
 constexpr int NCW = 4;                  // softmax warps
 constexpr int THREADS = (NCW + 2) * 32;
 constexpr int PRODUCER = NCW, MMA_WARP = NCW + 1;
+constexpr int TAB_CACHE = 512;          // page-table entries kept in shared memory
 constexpr int TMEM_COLS = 64;           // QK slots at 0 and 16, PV slots at 32 and 48
 constexpr unsigned kErrPage = 2u;       // a page index >= num_pages (copy skipped)
 constexpr unsigned kErrTable = 4u;      // kv_len needs more pages than the table holds
@@ -60,6 +61,7 @@ struct Smem {
   // B operands, 8 rows each; rows 8..15 of N = 16 alias rows 0..7 (stride offset 0)
   alignas(1024) int8_t qt[1024];          // 128-byte swizzled: rows 0,1 = q heads
   alignas(1024) int8_t pq[2][1024];       // no swizzle: [16-key chunk][8 rows][16 B]
+  uint16_t tab[TAB_CACHE];                // this sequence's page table (first TAB_CACHE entries)
   float bm[2][NCW][2];                    // block maxima
   float corr[2][2][4], psum[2][2][4], pmax[2][2][4];   // [slot][head][block]
   float red[NCW][2];
@@ -88,6 +90,10 @@ __device__ __forceinline__ bool wait_or_abort(unsigned long long *b, uint32_t pa
   return false;
 }
 
+__device__ __forceinline__ uint32_t page_of(const Smem &sm, const uint16_t *table, int j) {
+  return j < TAB_CACHE ? sm.tab[j] : table[j];
+}
+
 __global__ void __launch_bounds__(THREADS, 4)
     k_attention_decode(const char *__restrict__ kpool, const char *__restrict__ vpool,
                        DecodeAttnArgs p) {
@@ -97,6 +103,8 @@ __global__ void __launch_bounds__(THREADS, 4)
 
   const int kvh = blockIdx.x, seq = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  pdl_trigger();
+  pdl_wait();       // q, the new K/V rows and kv_len come from earlier kernels
   const int kv_len = p.kv_len[seq];
   const int nb = (kv_len + 31) >> 5;
   const uint16_t *table = p.table + static_cast<long>(seq) * p.table_stride;
@@ -112,6 +120,7 @@ __global__ void __launch_bounds__(THREADS, 4)
     *reinterpret_cast<int *>(sm.pq[0] + i) = 0;
     *reinterpret_cast<int *>(sm.pq[1] + i) = 0;
   }
+  for (int i = tid; i < nb && i < TAB_CACHE; i += THREADS) sm.tab[i] = table[i];
   if (tid < 64) {                                  // q rows of the two heads
     const int hh = tid >> 5, h = kvh * 2 + hh;
     const int v = reinterpret_cast<const int *>(p.q8 + static_cast<long>(seq) * p.q_rb + h * 128)[lane];
@@ -165,7 +174,7 @@ __global__ void __launch_bounds__(THREADS, 4)
       const char *pool = isv ? vpool : kpool;
       const int first = 4 * g, count = min(4, nb - first);
       for (int q = 0; q < count; ++q) {
-        const uint32_t page = table[first + q];
+        const uint32_t page = page_of(sm, table, first + q);
         if (page >= p.num_pages) {
           if (lane == 0) atomicOr(&g_device_error, kErrPage);
           continue;
@@ -229,7 +238,7 @@ __global__ void __launch_bounds__(THREADS, 4)
       const int j = 4 * g + warp, t = j * 32 + lane;
       ks = vs = 0.0f;
       if (j < nb && t < kv_len) {
-        const uint32_t page = table[j];
+        const uint32_t page = page_of(sm, table, j);
         if (page < p.num_pages) {
           const size_t o = static_cast<size_t>(page) * p.scale_page_bytes +
                            static_cast<size_t>(lane) * p.scale_row_bytes + kvh * 4;
@@ -361,7 +370,7 @@ __global__ void __launch_bounds__(THREADS, 4)
 
 // ---------------------------------------------------------------- host side
 int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const void *v_pool,
-                            uint32_t num_pages, int kv_heads, int n_seqs, cudaStream_t s) {
+                            uint32_t num_pages, int kv_heads, int n_seqs, cudaStream_t s, bool pdl) {
   if (p.row_bytes % 16 || p.page_bytes % 16 || reinterpret_cast<uintptr_t>(k_pool) % 16 ||
       reinterpret_cast<uintptr_t>(v_pool) % 16)
     return Q3_ERR_ALIGN;
@@ -380,9 +389,8 @@ int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const v
   a.num_pages = num_pages;
   dim3 grid(kv_heads, n_seqs);
   q3h::timer_begin(q3h::TIMER_ATTENTION, s);
-  dec::k_attention_decode<<<grid, dec::THREADS, smem, s>>>(
-      static_cast<const char *>(k_pool), static_cast<const char *>(v_pool), a);
-  const int st = q3h::launch_status();
+  const int st = q3h::launch_ex(pdl, dec::k_attention_decode, grid, dim3(dec::THREADS), smem, s,
+                                static_cast<const char *>(k_pool), static_cast<const char *>(v_pool), a);
   q3h::timer_end(q3h::TIMER_ATTENTION, s);
   return st;
 }

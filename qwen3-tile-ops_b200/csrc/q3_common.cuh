@@ -98,6 +98,15 @@ __device__ __forceinline__ float warp_tree_max(float v) {
   return v;
 }
 
+// Programmatic dependent launch: let the next kernel of the stream start its
+// prologue (launch_dependents), and wait until every earlier kernel of the
+// stream has finished and its writes are visible (wait).  Both are no-ops for a
+// kernel launched without the programmatic-serialisation attribute.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // int32 -> float32 for |v| < 2^22 with two full-rate ops (exact).
 __device__ __forceinline__ float i2f_small(int v) {
   return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
@@ -125,6 +134,33 @@ inline int launch_status() {
     return Q3_ERR_CUDA;
   }
   return Q3_OK;
+}
+
+// Launch with programmatic stream serialisation when `pdl` is set: the kernel
+// may start while the previous kernel of the stream is still running, so it
+// must call pdl_wait() before it reads what earlier kernels wrote or writes
+// anything they might still read.
+template <typename... KArgs, typename... Args>
+inline int launch_ex(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    count_launch();
+    cudaGetLastError();
+    set_cuda_error(e);
+    return Q3_ERR_CUDA;
+  }
+  return launch_status();
 }
 
 // Benchmark timing hook (q3_timer_attach): events around launches of a family.

@@ -223,7 +223,7 @@ int decode_fused(char *bl, const q3_layout &L, const q3_kv_pool *pool, const uin
       d.scale_row_bytes = 4 * L.kv_heads;
       d.kv_len = w.kv_len;
       d.qk_scale = kInvSqrt128;
-      Q3_TRY(q3::attention_decode_launch(d, pk, pv, pool->num_pages, L.kv_heads, B, st));
+      Q3_TRY(q3::attention_decode_launch(d, pk, pv, pool->num_pages, L.kv_heads, B, st, true));
     }
     // O (+ residual) -> x; RMSNorm(n2) + quant -> h8/hs
     {

@@ -13,7 +13,9 @@
 //                  the new x for the next GEMM (main_big.cpp:178-181, 258-259)
 //   k_red_swiglu   silu(gate) * up, per-256 quant (swiglu_quant.h:164-255)
 // Warp per (row, head) or (row, 256-group): a lane holds features l + 32k, so
-// the reference's 32-column block trees are warp butterflies.
+// the reference's 32-column block trees are warp butterflies.  The kernels are
+// launched as programmatic dependents of the GEMM before them and wait for it
+// before touching memory.
 #include "q3_common.cuh"
 
 namespace q3 {
@@ -48,6 +50,8 @@ struct QkvArgs {
 
 // grid (heads + 2*kv_heads) / 4 x B, block 128: warp per (row, head)
 __global__ void __launch_bounds__(128) k_red_qkv(QkvArgs a) {
+  pdl_trigger();
+  pdl_wait();     // the partials come from the kernel before
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x * 4 + warp;
   const int m = blockIdx.y;
@@ -117,6 +121,8 @@ struct AddNormArgs {
 
 // CTA per row, 256 threads, H == 1024: thread t owns features t + 256k
 __global__ void __launch_bounds__(256) k_red_add_norm(AddNormArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float blk[32];
   __shared__ float gmax[4][8];
   __shared__ float rsh;
@@ -179,6 +185,8 @@ struct SwigluArgs {
 
 // grid (I/256)/4 x B, block 128: warp per (row, 256-column group)
 __global__ void __launch_bounds__(128) k_red_swiglu(SwigluArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = blockIdx.x * 4 + warp, m = blockIdx.y;
   if (grp * 256 >= a.I) return;
@@ -207,17 +215,14 @@ __global__ void __launch_bounds__(128) k_red_swiglu(SwigluArgs a) {
 
 int red_qkv(const QkvArgs &a, cudaStream_t s) {
   const int nh = a.heads + 2 * a.kv_heads;
-  k_red_qkv<<<dim3((nh + 3) / 4, a.B), 128, 0, s>>>(a);
-  return q3h::launch_status();
+  return q3h::launch_ex(true, k_red_qkv, dim3((nh + 3) / 4, a.B), dim3(128), 0, s, a);
 }
 int red_add_norm(const AddNormArgs &a, cudaStream_t s) {
   if (a.H != 1024) return Q3_ERR_SHAPE;
-  k_red_add_norm<<<a.B, 256, 0, s>>>(a);
-  return q3h::launch_status();
+  return q3h::launch_ex(true, k_red_add_norm, dim3(a.B), dim3(256), 0, s, a);
 }
 int red_swiglu(const SwigluArgs &a, cudaStream_t s) {
-  k_red_swiglu<<<dim3((a.I / 256 + 3) / 4, a.B), 128, 0, s>>>(a);
-  return q3h::launch_status();
+  return q3h::launch_ex(true, k_red_swiglu, dim3((a.I / 256 + 3) / 4, a.B), dim3(128), 0, s, a);
 }
 
 }  // namespace q3

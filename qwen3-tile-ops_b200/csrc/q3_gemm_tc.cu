@@ -519,9 +519,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (threadIdx.x < NTOK)   // activation scales of this group, staged while the MMA runs
-    sm.as[threadIdx.x] = threadIdx.x < p.M
-        ? *reinterpret_cast<const float *>(p.a_scale + (long)threadIdx.x * p.as_rb + g * 4) : 0.0f;
+  pdl_trigger();
   fence_before();
   __syncthreads();
   fence_after();
@@ -529,14 +527,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == EPI_WARPS) {
     if (lane == 0) {
+      // weights first (no earlier kernel writes them), then, once the kernel
+      // before has finished, the activations it produced
       const CUtensorMap *ma = map == 0 ? &tm0 : map == 1 ? &tm1 : &tm2;
       for (int b = 0; b < nb; ++b) {
         const int k0 = g * p.group + b * 128;
         mbar_expect_tx(&sm.full[b], NACC * 128 * 128 + NTOK * 128);
         tma_2d(sm.a[b][0], ma, k0, row_in_map, &sm.full[b]);
         if (NACC == 2) tma_2d(sm.a[b][NACC - 1], &tm1, k0, row_in_map, &sm.full[b]);
-        tma_2d(sm.b[b], &tmB, k0, 0, &sm.full[b]);
       }
+      pdl_wait();
+      for (int b = 0; b < nb; ++b) tma_2d(sm.b[b], &tmB, g * p.group + b * 128, 0, &sm.full[b]);
     }
     __syncwarp();
   } else if (warp == EPI_WARPS + 1) {
@@ -568,6 +569,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int tid = threadIdx.x;
     const int n = tile * 128 + tid;                    // output feature (global column)
     const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    pdl_wait();
+    if (tid < NTOK)   // activation scales of this group, staged while the MMA runs
+      sm.as[tid] = tid < p.M ? *reinterpret_cast<const float *>(p.a_scale + (long)tid * p.as_rb + g * 4)
+                             : 0.0f;
+    epi_sync();
     const bool ok = mbar_wait(&sm.tfull, 0, &sm.abort);
     fence_after();
     if (ok) {
@@ -613,8 +619,8 @@ static int launch_part(const PartArgs &p, const CUtensorMap (&maps)[3], const CU
   }
   dim3 grid(tiles, p.G);
   q3h::timer_begin(q3h::TIMER_GEMM, s);
-  k_gemm_tc_part<NTOK, NACC><<<grid, THREADS, smem, s>>>(maps[0], maps[1], maps[2], tb, p);
-  const int st = q3h::launch_status();
+  const int st = q3h::launch_ex(true, k_gemm_tc_part<NTOK, NACC>, grid, dim3(THREADS), smem, s,
+                                maps[0], maps[1], maps[2], tb, p);
   q3h::timer_end(q3h::TIMER_GEMM, s);
   return st;
 }
