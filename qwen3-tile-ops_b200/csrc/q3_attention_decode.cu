@@ -399,6 +399,7 @@ int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const v
 
 namespace q3 {
 int gemm_device_status_take();
+int dgemm_device_status_take();
 }
 
 extern "C" int q3_device_status(void) {
@@ -407,5 +408,8 @@ extern "C" int q3_device_status(void) {
   if (v) cudaMemcpyToSymbol(q3::g_device_error, &zero, sizeof zero);
   const int g = q3::gemm_device_status_take();
   if (g < 0) return -1;
+  const int dg = q3::dgemm_device_status_take();
+  if (dg < 0) return -1;
+  v |= static_cast<unsigned int>(dg);
   return static_cast<int>(v) | g;
 }

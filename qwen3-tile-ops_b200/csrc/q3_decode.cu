@@ -6,6 +6,7 @@
 // one GEMM is bit-identical to running the sequences one by one.
 #include "q3_attention.h"
 #include "q3_common.cuh"
+#include "q3_decode_gemm.h"
 #include "q3_gemm.h"
 
 namespace q3 {
@@ -37,6 +38,16 @@ struct SwigluArgs {
   int8_t *s8;
   float *ss;
 };
+struct NormQuantArgs {
+  const float *x;
+  const float *bsum;
+  const float *w;
+  float inv;
+  int B, H;
+  int8_t *h8;
+  float *hs;
+};
+int norm_quant(const NormQuantArgs &a, cudaStream_t s);
 int red_qkv(const QkvArgs &a, cudaStream_t s);
 int red_add_norm(const AddNormArgs &a, cudaStream_t s);
 int red_swiglu(const SwigluArgs &a, cudaStream_t s);
@@ -62,6 +73,7 @@ struct DecodeWs {
   float *best;           // [B]
   unsigned long long *keys;  // [B]
   float *part;           // split-K partials (fused path), largest GEMM of a layer
+  float *bsum;           // [B][H/32] tree sums of x^2 per 32-column block
   size_t total;
 };
 
@@ -99,6 +111,7 @@ DecodeWs carve(const q3_layout &L, uint32_t B, char *base) {
     mx = mx > d ? mx : d;
     w.part = (float *)take(4 * mx);
   }
+  w.bsum = (float *)take(4 * B * (H / 32));
   w.total = off;
   return w;
 }
@@ -182,25 +195,45 @@ int decode_fused(char *bl, const q3_layout &L, const q3_kv_pool *pool, const uin
     const float *nq = reinterpret_cast<const float *>(ln + (o[Q3_OFF_NQ] - o[Q3_OFF_N1]));
     const float *nk = reinterpret_cast<const float *>(ln + (o[Q3_OFF_NK] - o[Q3_OFF_N1]));
     const float *n2 = reinterpret_cast<const float *>(ln + (o[Q3_OFF_N2] - o[Q3_OFF_N1]));
-    const float *next_norm =
-        (Li + 1 < L.layers)
-            ? reinterpret_cast<const float *>(bl + o[Q3_OFF_N1] + static_cast<int64_t>(Li + 1) * o[Q3_OFF_LAYERN_STRIDE])
-            : reinterpret_cast<const float *>(bl + o[Q3_OFF_NF]);
     char *pk = static_cast<char *>(pool->k) + Li * pool->layer_stride;
     char *pv = static_cast<char *>(pool->v) + Li * pool->layer_stride;
     char *pks = static_cast<char *>(pool->ks) + Li * pool->scale_layer_stride;
     char *pvs = static_cast<char *>(pool->vs) + Li * pool->scale_layer_stride;
 
-    // Q | K | V partials, then norm/rope/quant into q8 and the KV pages
+    // RMSNorm(n1) + quant of x -> h8/hs (layer 0: the embedding step did it)
+    if (Li > 0) {
+      q3::NormQuantArgs a{w.x, w.bsum, reinterpret_cast<const float *>(ln), inv_h, (int)B, (int)H,
+                          w.h8, w.hs};
+      Q3_TRY(q3::norm_quant(a, st));
+    }
+    // Q | K | V, head norm/rope/quant into q8 and the KV pages
     {
       const int8_t *wts[3] = {Wp(Q3_OFF_LQ), Wp(Q3_OFF_LK), Wp(Q3_OFF_LV)};
-      const float *scs[3] = {Sp(Q3_OFF_LQ_SCALE), Sp(Q3_OFF_LK_SCALE), Sp(Q3_OFF_LV_SCALE)};
       const int rows[3] = {(int)QW, (int)KW, (int)KW};
-      Q3_TRY(q3::gemm_tc_partials(1, 3, wts, scs, rows, w.h8, H, reinterpret_cast<const char *>(w.hs),
-                                  4 * (H / 256), B, H, 256, w.part, st));
-      q3::QkvArgs a{w.part, (int)(H / 256), (int)B, (int)L.heads, (int)L.kv_heads, nq, nk, cos_t,
-                    sin_t, pos, inv_hd, w.q8, w.qs, pk, pv, pks, pvs, tables, max_pages};
-      Q3_TRY(q3::red_qkv(a, st));
+      q3::DgemmArgs a{};
+      a.M = (int)B;
+      a.a_scale = reinterpret_cast<const char *>(w.hs);
+      a.as_rb = 4 * (H / 256);
+      a.ws[0] = Sp(Q3_OFF_LQ_SCALE);
+      a.ws[1] = Sp(Q3_OFF_LK_SCALE);
+      a.ws[2] = Sp(Q3_OFF_LV_SCALE);
+      a.heads = (int)L.heads;
+      a.kv_heads = (int)L.kv_heads;
+      a.nq = nq;
+      a.nk = nk;
+      a.cos_t = cos_t;
+      a.sin_t = sin_t;
+      a.pos = pos;
+      a.inv_hd = inv_hd;
+      a.q8 = w.q8;
+      a.qs = w.qs;
+      a.pk = pk;
+      a.pv = pv;
+      a.pks = pks;
+      a.pvs = pvs;
+      a.tables = tables;
+      a.max_pages = max_pages;
+      Q3_TRY(q3::dgemm_launch(q3::DG_QKV, 3, wts, rows, w.h8, H, (int)H, 256, a, st));
     }
     // attention
     {
@@ -225,38 +258,61 @@ int decode_fused(char *bl, const q3_layout &L, const q3_kv_pool *pool, const uin
       d.qk_scale = kInvSqrt128;
       Q3_TRY(q3::attention_decode_launch(d, pk, pv, pool->num_pages, L.kv_heads, B, st, true));
     }
-    // O (+ residual) -> x; RMSNorm(n2) + quant -> h8/hs
+    // O + residual -> x (and its block sums)
     {
       const int8_t *wts[1] = {Wp(Q3_OFF_LO)};
-      const float *scs[1] = {Sp(Q3_OFF_LO_SCALE)};
       const int rows[1] = {(int)H};
-      Q3_TRY(q3::gemm_tc_partials(1, 1, wts, scs, rows, w.o8, QW, reinterpret_cast<const char *>(w.os),
-                                  4 * L.heads, B, QW, 128, w.part, st));
-      q3::AddNormArgs a{w.part, (int)(QW / 128), (int)B, (int)H, w.x, n2, inv_h, w.h8, w.hs};
-      Q3_TRY(q3::red_add_norm(a, st));
+      q3::DgemmArgs a{};
+      a.M = (int)B;
+      a.a_scale = reinterpret_cast<const char *>(w.os);
+      a.as_rb = 4 * L.heads;
+      a.ws[0] = Sp(Q3_OFF_LO_SCALE);
+      a.x = w.x;
+      a.bsum = w.bsum;
+      a.H = (int)H;
+      Q3_TRY(q3::dgemm_launch(q3::DG_RESID, 1, wts, rows, w.o8, QW, (int)QW, 128, a, st));
+    }
+    // RMSNorm(n2) + quant -> h8/hs
+    {
+      q3::NormQuantArgs a{w.x, w.bsum, n2, inv_h, (int)B, (int)H, w.h8, w.hs};
+      Q3_TRY(q3::norm_quant(a, st));
     }
     // gate/up -> SwiGLU + quant -> s8/ss
     {
       const int8_t *wts[2] = {Wp(Q3_OFF_LG), Wp(Q3_OFF_LU)};
-      const float *scs[2] = {Sp(Q3_OFF_LG_SCALE), Sp(Q3_OFF_LU_SCALE)};
       const int rows[2] = {(int)I, (int)I};
-      Q3_TRY(q3::gemm_tc_partials(2, 2, wts, scs, rows, w.h8, H, reinterpret_cast<const char *>(w.hs),
-                                  4 * (H / 256), B, H, 256, w.part, st));
-      q3::SwigluArgs a{w.part, (int)(H / 256), (int)B, (int)I, w.s8, w.ss};
-      Q3_TRY(q3::red_swiglu(a, st));
+      q3::DgemmArgs a{};
+      a.M = (int)B;
+      a.a_scale = reinterpret_cast<const char *>(w.hs);
+      a.as_rb = 4 * (H / 256);
+      a.ws[0] = Sp(Q3_OFF_LG_SCALE);
+      a.ws[1] = Sp(Q3_OFF_LU_SCALE);
+      a.s8 = w.s8;
+      a.ss = w.ss;
+      a.I = (int)I;
+      Q3_TRY(q3::dgemm_launch(q3::DG_SWIGLU, 2, wts, rows, w.h8, H, (int)H, 256, a, st));
     }
-    // down (+ residual) -> x; next layer's RMSNorm (or the final norm) + quant
+    // down + residual -> x (and its block sums)
     {
       const int8_t *wts[1] = {Wp(Q3_OFF_LD)};
-      const float *scs[1] = {Sp(Q3_OFF_LD_SCALE)};
       const int rows[1] = {(int)H};
-      Q3_TRY(q3::gemm_tc_partials(1, 1, wts, scs, rows, w.s8, I, reinterpret_cast<const char *>(w.ss),
-                                  4 * (I / 256), B, I, 256, w.part, st));
-      q3::AddNormArgs a{w.part, (int)(I / 256), (int)B, (int)H, w.x, next_norm, inv_h, w.h8, w.hs};
-      Q3_TRY(q3::red_add_norm(a, st));
+      q3::DgemmArgs a{};
+      a.M = (int)B;
+      a.a_scale = reinterpret_cast<const char *>(w.ss);
+      a.as_rb = 4 * (I / 256);
+      a.ws[0] = Sp(Q3_OFF_LD_SCALE);
+      a.x = w.x;
+      a.bsum = w.bsum;
+      a.H = (int)H;
+      Q3_TRY(q3::dgemm_launch(q3::DG_RESID, 1, wts, rows, w.s8, I, (int)I, 256, a, st));
     }
   }
-  // final norm + quant already in h8/hs: lm_head fused with argmax
+  // final RMSNorm + quant, then lm_head fused with argmax
+  {
+    q3::NormQuantArgs a{w.x, w.bsum, reinterpret_cast<const float *>(bl + o[Q3_OFF_NF]), inv_h,
+                        (int)B, (int)H, w.h8, w.hs};
+    Q3_TRY(q3::norm_quant(a, st));
+  }
   Q3_TRY(q3_gemm_nt_group_argmax(&h8, &hs, &lm, &lm_s, w.best, next_ids, 256, w.keys, 8 * B, s));
   return Q3_OK;
 }

@@ -1,6 +1,7 @@
 // Internal GEMM interface shared by the SIMT and tensor-core paths.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -47,6 +48,13 @@ int gemm_tc(const GemmArgs &p, cudaStream_t s);
 bool gemm_tc_eligible(const GemmArgs &p);
 int argmax_begin(const GemmArgs &p, cudaStream_t s);
 int argmax_end(const GemmArgs &p, cudaStream_t s);
+
+// TMA map of an int8 [rows][cols] matrix (row stride `stride` bytes), 128-byte
+// swizzle, box = 128 bytes x box_rows (q3_gemm_tc.cu)
+namespace tc {
+bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, uint64_t stride,
+              uint32_t box_rows);
+}
 
 // split-K partials for decode-sized GEMMs (q3_gemm_tc.cu)
 int gemm_tc_partials(int nacc, int nmaps, const int8_t *const *w, const float *const *ws,

@@ -383,8 +383,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // int8 [rows][cols] with row stride `stride` bytes; box = 128 bytes x box_rows
-static bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols,
-                     uint64_t stride, uint32_t box_rows) {
+bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols,
+              uint64_t stride, uint32_t box_rows) {
   auto enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {cols, rows};
