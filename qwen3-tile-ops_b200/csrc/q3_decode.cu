@@ -10,34 +10,6 @@
 #include "q3_gemm.h"
 
 namespace q3 {
-struct QkvArgs {
-  const float *part;
-  int G, B, heads, kv_heads;
-  const float *nq, *nk;
-  const float *cos_t, *sin_t;
-  const int32_t *pos;
-  float inv_hd;
-  int8_t *q8;
-  float *qs;
-  char *pk, *pv, *pks, *pvs;
-  const uint16_t *tables;
-  uint32_t max_pages;
-};
-struct AddNormArgs {
-  const float *part;
-  int G, B, H;
-  float *x;
-  const float *w;
-  float inv;
-  int8_t *h8;
-  float *hs;
-};
-struct SwigluArgs {
-  const float *part;
-  int G, B, I;
-  int8_t *s8;
-  float *ss;
-};
 struct NormQuantArgs {
   const float *x;
   const float *bsum;
@@ -48,9 +20,6 @@ struct NormQuantArgs {
   float *hs;
 };
 int norm_quant(const NormQuantArgs &a, cudaStream_t s);
-int red_qkv(const QkvArgs &a, cudaStream_t s);
-int red_add_norm(const AddNormArgs &a, cudaStream_t s);
-int red_swiglu(const SwigluArgs &a, cudaStream_t s);
 }  // namespace q3
 
 namespace {
@@ -72,7 +41,6 @@ struct DecodeWs {
   int *kv_len;           // [B]
   float *best;           // [B]
   unsigned long long *keys;  // [B]
-  float *part;           // split-K partials (fused path), largest GEMM of a layer
   float *bsum;           // [B][H/32] tree sums of x^2 per 32-column block
   size_t total;
 };
@@ -103,14 +71,6 @@ DecodeWs carve(const q3_layout &L, uint32_t B, char *base) {
   w.kv_len = (int *)take(4 * B);
   w.best = (float *)take(4 * B);
   w.keys = (unsigned long long *)take(8 * B);
-  {
-    const size_t qkv = (size_t)(H / 256) * B * (QW + 2 * KW), o = (size_t)(QW / 128) * B * H;
-    const size_t gu = 2 * (size_t)(H / 256) * B * I, d = (size_t)(I / 256) * B * H;
-    size_t mx = qkv > o ? qkv : o;
-    mx = mx > gu ? mx : gu;
-    mx = mx > d ? mx : d;
-    w.part = (float *)take(4 * mx);
-  }
   w.bsum = (float *)take(4 * B * (H / 32));
   w.total = off;
   return w;
@@ -162,8 +122,10 @@ __global__ void k_keys_to_ids(const unsigned long long *keys, int32_t *next_ids,
   if (s < B) next_ids[s] = static_cast<int32_t>(0xffffffffu - static_cast<unsigned>(keys[s] & 0xffffffffu));
 }
 
-// The batched step with split-K tensor-core GEMMs and fused group reductions
-// (9 launches per layer).  Same arithmetic as the operator-by-operator path.
+// The batched step: per layer RMSNorm+quant, QKV (head norm/rope/quant into the
+// KV pages), attention, O (+ residual), RMSNorm+quant, gate/up (SwiGLU+quant),
+// down (+ residual) -- 7 launches, each a programmatic dependent of the one
+// before.  Same arithmetic as the operator-by-operator path.
 int decode_fused(char *bl, const q3_layout &L, const q3_kv_pool *pool, const uint16_t *tables,
                  uint32_t max_pages, const int32_t *ids, const int32_t *pos, uint32_t B,
                  int32_t *next_ids, const DecodeWs &w, cudaStream_t st) {

@@ -56,9 +56,4 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, ui
               uint32_t box_rows);
 }
 
-// split-K partials for decode-sized GEMMs (q3_gemm_tc.cu)
-int gemm_tc_partials(int nacc, int nmaps, const int8_t *const *w, const float *const *ws,
-                     const int *rows, const int8_t *a, long a_rb, const char *a_scale,
-                     long as_rb, int M, int K, int group, float *out, cudaStream_t s);
-
 }  // namespace q3

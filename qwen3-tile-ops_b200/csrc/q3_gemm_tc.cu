@@ -467,205 +467,4 @@ int gemm_tc(const GemmArgs &p, cudaStream_t s) {
 // NACC = 2 (gate/up) maps 0 and 1 are read for the same rows.
 // ===========================================================================
 namespace q3 {
-namespace tc {
-
-struct PartArgs {
-  const int8_t *a;          // activations [M][K]
-  const char *a_scale;      // [M][G] f32
-  long as_rb;
-  const float *ws[3];       // per-map output-row scales
-  int t1, t2;               // row-tile boundaries between maps
-  int M, N, K, group, G;
-  float *out;               // [NACC][G][M][N]
-};
-
-template <int NTOK, int NACC>
-struct PartSmem {
-  alignas(1024) int8_t a[2][NACC][128 * 128];
-  alignas(1024) int8_t b[2][NTOK * 128];
-  float as[NTOK];              // a_scale[m][g] of this CTA's group
-  unsigned long long full[2], tfull;
-  uint32_t tmem_base;
-  int abort;
-};
-
-template <int NTOK, int NACC>
-__global__ void __launch_bounds__(THREADS, 1)
-    k_gemm_tc_part(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
-                   const __grid_constant__ CUtensorMap tm2, const __grid_constant__ CUtensorMap tmB,
-                   const PartArgs p) {
-  constexpr int TMEM_COLS = (NACC * NTOK) <= 32 ? 32 : (NACC * NTOK) <= 64 ? 64 : (NACC * NTOK) <= 128 ? 128 : 256;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  PartSmem<NTOK, NACC> &sm = *reinterpret_cast<PartSmem<NTOK, NACC> *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, g = blockIdx.y;
-  const int nb = p.group / 128;
-  const int map = NACC == 2 ? 0 : (tile < p.t1 ? 0 : tile < p.t2 ? 1 : 2);
-  const int row_in_map = NACC == 2 ? tile * 128
-                                   : (tile - (map == 0 ? 0 : map == 1 ? p.t1 : p.t2)) * 128;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&sm.full[0], 1);
-    mbar_init(&sm.full[1], 1);
-    mbar_init(&sm.tfull, 1);
-    sm.abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == EPI_WARPS + 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     su32(&sm.tmem_base)),
-                 "n"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  pdl_trigger();
-  fence_before();
-  __syncthreads();
-  fence_after();
-  const uint32_t tmem = sm.tmem_base;
-
-  if (warp == EPI_WARPS) {
-    if (lane == 0) {
-      // weights first (no earlier kernel writes them), then, once the kernel
-      // before has finished, the activations it produced
-      const CUtensorMap *ma = map == 0 ? &tm0 : map == 1 ? &tm1 : &tm2;
-      for (int b = 0; b < nb; ++b) {
-        const int k0 = g * p.group + b * 128;
-        mbar_expect_tx(&sm.full[b], NACC * 128 * 128 + NTOK * 128);
-        tma_2d(sm.a[b][0], ma, k0, row_in_map, &sm.full[b]);
-        if (NACC == 2) tma_2d(sm.a[b][NACC - 1], &tm1, k0, row_in_map, &sm.full[b]);
-      }
-      pdl_wait();
-      for (int b = 0; b < nb; ++b) tma_2d(sm.b[b], &tmB, g * p.group + b * 128, 0, &sm.full[b]);
-    }
-    __syncwarp();
-  } else if (warp == EPI_WARPS + 1) {
-    constexpr uint32_t ID = idesc_i8(NTOK);
-    bool ok = true;
-    if (lane == 0) {
-      for (int b = 0; b < nb && ok; ++b) {
-        if (!mbar_wait(&sm.full[b], 0, &sm.abort)) { ok = false; break; }
-        fence_after();
-        const uint32_t sb = su32(sm.b[b]);
-#pragma unroll
-        for (int a = 0; a < NACC; ++a) {
-          const uint32_t sa = su32(sm.a[b][a]);
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            mma_i8(tmem + a * NTOK, sdesc_sw128(sa + ks * 32), sdesc_sw128(sb + ks * 32), ID, (b | ks) != 0);
-        }
-      }
-      mma_commit(&sm.tfull);          // completes once every MMA issued has finished
-      if (!ok) {
-        atomicOr(&g_gemm_error, kErrGemmTimeout);
-        sm.abort = 1;
-        mbar_wait(&sm.tfull, 0, nullptr);
-        for (int b = 0; b < nb; ++b) mbar_wait(&sm.full[b], 0, nullptr);   // copies landed
-      }
-    }
-    __syncwarp();
-  } else {
-    const int tid = threadIdx.x;
-    const int n = tile * 128 + tid;                    // output feature (global column)
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-    pdl_wait();
-    if (tid < NTOK)   // activation scales of this group, staged while the MMA runs
-      sm.as[tid] = tid < p.M ? *reinterpret_cast<const float *>(p.a_scale + (long)tid * p.as_rb + g * 4)
-                             : 0.0f;
-    epi_sync();
-    const bool ok = mbar_wait(&sm.tfull, 0, &sm.abort);
-    fence_after();
-    if (ok) {
-      const float *wsp = NACC == 2 ? p.ws[0] : (map == 0 ? p.ws[0] : map == 1 ? p.ws[1] : p.ws[2]);
-#pragma unroll
-      for (int a = 0; a < NACC; ++a) {
-        const float ws = (NACC == 2 && a) ? p.ws[1][row_in_map + tid] : wsp[row_in_map + tid];
-        int v[NTOK];
-#pragma unroll
-        for (int c = 0; c < NTOK; c += 16) tmem_ld16(lane_addr + a * NTOK + c, *reinterpret_cast<int(*)[16]>(&v[c]));
-        tmem_wait_ld();
-        float *dst = p.out + ((size_t)(a * p.G + g) * p.M) * p.N + n;
-#pragma unroll
-        for (int m = 0; m < NTOK; ++m)
-          if (m < p.M) dst[(size_t)m * p.N] = __fmul_rn(__fmul_rn(i2f_small(v[m]), ws), sm.as[m]);
-      }
-    } else if (lane == 0) {
-      atomicOr(&g_gemm_error, kErrGemmTimeout);
-      sm.abort = 1;
-    }
-  }
-  fence_before();
-  __syncthreads();
-  fence_after();
-  if (warp == EPI_WARPS + 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TMEM_COLS)
-                 : "memory");
-}
-
-template <int NTOK, int NACC>
-static int launch_part(const PartArgs &p, const CUtensorMap (&maps)[3], const CUtensorMap &tb,
-                       int tiles, cudaStream_t s) {
-  const size_t smem = sizeof(PartSmem<NTOK, NACC>) + 1024;
-  static std::once_flag once;
-  static cudaError_t attr = cudaSuccess;
-  std::call_once(once, [&] {
-    attr = cudaFuncSetAttribute(k_gemm_tc_part<NTOK, NACC>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  });
-  if (attr != cudaSuccess) {
-    q3h::set_cuda_error(attr);
-    return Q3_ERR_CUDA;
-  }
-  dim3 grid(tiles, p.G);
-  q3h::timer_begin(q3h::TIMER_GEMM, s);
-  const int st = q3h::launch_ex(true, k_gemm_tc_part<NTOK, NACC>, grid, dim3(THREADS), smem, s,
-                                maps[0], maps[1], maps[2], tb, p);
-  q3h::timer_end(q3h::TIMER_GEMM, s);
-  return st;
-}
-
-}  // namespace tc
-
-// One split-K launch: nmaps weight matrices [rows_i][K] (row strides = K) with
-// scales ws_i stacked along the output dimension (NACC = 1), or gate/up read for
-// the same rows (nacc = 2).  out: [nacc][K/group][M][sum rows] f32, M <= 64.
-int gemm_tc_partials(int nacc, int nmaps, const int8_t *const *w, const float *const *ws,
-                     const int *rows, const int8_t *a, long a_rb, const char *a_scale,
-                     long as_rb, int M, int K, int group, float *out, cudaStream_t s) {
-  if (M < 1 || M > 64 || group % 128 || group > 256 || K % group || a_rb % 16 ||
-      reinterpret_cast<uintptr_t>(a) % 16)
-    return Q3_ERR_SHAPE;
-  tc::PartArgs p{};
-  CUtensorMap maps[3];
-  int tiles = 0;
-  for (int i = 0; i < 3; ++i) {
-    const int j = i < nmaps ? i : nmaps - 1;
-    if (rows[j] % 128 || reinterpret_cast<uintptr_t>(w[j]) % 16) return Q3_ERR_SHAPE;
-    if (!tc::make_map(&maps[i], w[j], rows[j], K, K, 128)) return Q3_ERR_CUDA;
-    p.ws[i] = ws[j];
-  }
-  if (nacc == 2) {
-    tiles = rows[0] / 128;
-    p.t1 = p.t2 = tiles;
-  } else {
-    p.t1 = rows[0] / 128;
-    p.t2 = p.t1 + (nmaps > 1 ? rows[1] / 128 : 0);
-    tiles = p.t2 + (nmaps > 2 ? rows[2] / 128 : 0);
-  }
-  CUtensorMap tb;
-  if (!tc::make_map(&tb, a, M, K, a_rb, 64)) return Q3_ERR_CUDA;
-  p.a = a;
-  p.a_scale = a_scale;
-  p.as_rb = as_rb;
-  p.M = M;
-  p.N = tiles * 128;
-  p.K = K;
-  p.group = group;
-  p.G = K / group;
-  p.out = out;
-  return nacc == 2 ? tc::launch_part<64, 2>(p, maps, tb, tiles, s)
-                   : tc::launch_part<64, 1>(p, maps, tb, tiles, s);
-}
-
 }  // namespace q3
