@@ -253,6 +253,19 @@ int q3_decode_step_batch(void *blob, const q3_layout *layout,
                          const int32_t *pos, uint32_t n_seqs, int32_t *next_ids,
                          void *workspace, size_t workspace_bytes, void *stream);
 
+/* Prompt prefill for n_seqs independent sequences (extension; the batched form
+ * of src/main_big.cpp:332-348's prompt chunks): ids[s*T + t] is token t of
+ * sequence s, at position t.  Writes every layer's K/V rows 0..T-1 into the
+ * pages tables[s*max_pages ...] (device) of the pool and the greedy next id of
+ * every sequence to next_ids[s] (device).  Same bits as prefilling each
+ * sequence alone in 32-row chunks.  Needs T <= max_seq, ceil(T/32) <= max_pages
+ * and q3_prefill_workspace_bytes(layout, n_seqs, T) bytes of workspace. */
+size_t q3_prefill_workspace_bytes(const q3_layout *layout, uint32_t n_seqs, uint32_t T);
+int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv_pool *pool,
+                     const uint16_t *tables, uint32_t max_pages, const int32_t *ids,
+                     uint32_t n_seqs, uint32_t T, int32_t *next_ids, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
 /* ---- value ops (include/tile.h exp_/exp2 semantics; tests/guest/value_ops.cpp)
  * out[i] = exp(x[i]) as the path computes it: exp2(f32(x * log2e))
  * (tools/ref_qwen3.py:27-29), or out[i] = exp2(x[i]); both correctly rounded

@@ -92,6 +92,10 @@ SIGS = {
     "q3_decode_step_batch": [C.c_void_p, C.POINTER(Layout), C.POINTER(KVPool), C.c_void_p,
                              C.c_uint32, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p,
                              C.c_void_p, C.c_size_t, C.c_void_p],
+    "q3_prefill_workspace_bytes": [C.POINTER(Layout), C.c_uint32, C.c_uint32],
+    "q3_prefill_batch": [C.c_void_p, C.POINTER(Layout), C.POINTER(KVPool), C.c_void_p, C.c_uint32,
+                         C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_size_t,
+                         C.c_void_p],
     "q3_exp_rows": [VP, VP, C.c_void_p],
     "q3_exp2_rows": [VP, VP, C.c_void_p],
     "q3_last_cuda_error": [],
@@ -103,6 +107,7 @@ SIGS = {
 }
 RESTYPE = {"q3_gemm_nt_group_argmax_workspace_bytes": C.c_size_t,
            "q3_forward_workspace_bytes": C.c_size_t, "q3_decode_workspace_bytes": C.c_size_t,
+           "q3_prefill_workspace_bytes": C.c_size_t,
            "q3_last_cuda_error": C.c_char_p, "q3_launch_count": C.c_uint64}
 
 _lib = None

@@ -1,0 +1,252 @@
+// Batched prompt prefill: n_seqs independent sequences, each with a T-token
+// prompt at positions 0..T-1, written into a shared KV page pool under
+// per-sequence page tables (kernels/kv_pages.h:98-131 semantics), and the
+// greedy next token of every sequence.
+//
+// Per row the arithmetic is forward_chunk's (src/main_big.cpp:145-296): rows
+// never interact except through attention, and a prompt processed as one
+// chunk of T rows gives the same bits as the reference's 32-row chunks — every
+// row's K/V is written before attention, which masks each row to the keys at
+// or before its position (tools/ref_qwen3.py:269-289).  The GEMMs run with all
+// n_seqs * T rows stacked (M = n_seqs * T); attention is the causal batched
+// paged kernel over the pool; only each sequence's last row goes through the
+// final norm and the lm_head argmax.
+#include "q3_attention.h"
+#include "q3_common.cuh"
+#include "q3_gemm.h"
+
+namespace {
+
+constexpr uint32_t kPT = 32;   // page tokens
+constexpr float kInvSqrt128 = 0.08838834764831845f;
+
+struct PrefillWs {
+  float *x, *h;          // [M][H]
+  int8_t *h8;            // [M][H]
+  float *hs;             // [M][H/256]
+  int8_t *q8, *o8;       // [M][QW]
+  float *qs, *os;        // [M][heads]
+  int8_t *k8, *v8;       // [M][KW] staging of the new K/V rows
+  float *ks, *vs;        // [M][kv_heads]
+  int8_t *s8;            // [M][I]
+  float *ss;             // [M][I/256]
+  float *cos, *sin;      // [M][64] rows at each row's position
+  float *xl, *hl;        // [B][H] last rows
+  int8_t *h8l;           // [B][H]
+  float *hsl;            // [B][H/256]
+  float *best;           // [B]
+  unsigned long long *keys;  // [B]
+  size_t total;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+PrefillWs carve(const q3_layout &L, size_t M, uint32_t B, char *base) {
+  const size_t H = L.hidden, QW = L.heads * L.head_dim, KW = L.kv_heads * L.head_dim, I = L.inter;
+  PrefillWs w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) { char *p = base ? base + off : nullptr; off += align256(bytes); return p; };
+  w.x = (float *)take(4 * M * H);
+  w.h = (float *)take(4 * M * H);
+  w.h8 = (int8_t *)take(M * H);
+  w.hs = (float *)take(4 * M * (H / 256));
+  w.q8 = (int8_t *)take(M * QW);
+  w.o8 = (int8_t *)take(M * QW);
+  w.qs = (float *)take(4 * M * L.heads);
+  w.os = (float *)take(4 * M * L.heads);
+  w.k8 = (int8_t *)take(M * KW);
+  w.v8 = (int8_t *)take(M * KW);
+  w.ks = (float *)take(4 * M * L.kv_heads);
+  w.vs = (float *)take(4 * M * L.kv_heads);
+  w.s8 = (int8_t *)take(M * I);
+  w.ss = (float *)take(4 * M * (I / 256));
+  w.cos = (float *)take(4 * M * (L.head_dim / 2));
+  w.sin = (float *)take(4 * M * (L.head_dim / 2));
+  w.xl = (float *)take(4 * B * H);
+  w.hl = (float *)take(4 * B * H);
+  w.h8l = (int8_t *)take(B * H);
+  w.hsl = (float *)take(4 * B * (H / 256));
+  w.best = (float *)take(4 * B);
+  w.keys = (unsigned long long *)take(8 * B);
+  w.total = off;
+  return w;
+}
+
+q3_view v2(void *p, uint32_t rows, uint32_t cols, uint8_t dt) {
+  const int es = (dt == Q3_DT_I8 || dt == Q3_DT_U8) ? 1 : 4;
+  return q3_view{p, static_cast<int32_t>(cols * es), es, rows, cols, dt};
+}
+
+// rope rows of row m (position m % T)
+__global__ void k_prefill_rope_rows(const float *cos_t, const float *sin_t, int half, int T,
+                                    float *cos, float *sin) {
+  const int m = blockIdx.x, t = m % T;
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    cos[(size_t)m * half + j] = cos_t[(size_t)t * half + j];
+    sin[(size_t)m * half + j] = sin_t[(size_t)t * half + j];
+  }
+}
+
+// K/V row m = s*T + t -> page tables[s][t/32], slot t%32
+__global__ void k_prefill_scatter(const int8_t *k8, const int8_t *v8, const float *ks,
+                                  const float *vs, const uint16_t *tables, uint32_t max_pages,
+                                  int T, char *pk, char *pv, char *pks, char *pvs, int kw,
+                                  int kvh) {
+  const int m = blockIdx.x, s = m / T, t = m % T;
+  const uint32_t page = tables[static_cast<size_t>(s) * max_pages + t / kPT], slot = t % kPT;
+  const size_t row = static_cast<size_t>(page) * kPT + slot;
+  for (int i = threadIdx.x; i < kw / 16; i += blockDim.x) {
+    reinterpret_cast<int4 *>(pk + row * kw)[i] = reinterpret_cast<const int4 *>(k8 + (size_t)m * kw)[i];
+    reinterpret_cast<int4 *>(pv + row * kw)[i] = reinterpret_cast<const int4 *>(v8 + (size_t)m * kw)[i];
+  }
+  for (int h = threadIdx.x; h < kvh; h += blockDim.x) {
+    reinterpret_cast<float *>(pks + row * kvh * 4)[h] = ks[(size_t)m * kvh + h];
+    reinterpret_cast<float *>(pvs + row * kvh * 4)[h] = vs[(size_t)m * kvh + h];
+  }
+}
+
+// x row s*T + T-1 -> xl[s]; best[s] = -3e38, next_ids[s] = 0 (argmax state)
+__global__ void k_prefill_last_rows(const float *x, int T, int H, float *xl, float *best,
+                                    int32_t *next_ids) {
+  const int s = blockIdx.x;
+  const float *src = x + (static_cast<size_t>(s) * T + T - 1) * H;
+  for (int j = threadIdx.x; j < H; j += blockDim.x) xl[(size_t)s * H + j] = src[j];
+  if (threadIdx.x == 0) {
+    best[s] = -3.0e38f;
+    next_ids[s] = 0;
+  }
+}
+
+}  // namespace
+
+extern "C" size_t q3_prefill_workspace_bytes(const q3_layout *L, uint32_t n_seqs, uint32_t T) {
+  if (!L) return 0;
+  return carve(*L, static_cast<size_t>(n_seqs) * T, n_seqs, nullptr).total;
+}
+
+extern "C" int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv_pool *pool,
+                                const uint16_t *tables, uint32_t max_pages, const int32_t *ids,
+                                uint32_t n_seqs, uint32_t T, int32_t *next_ids, void *workspace,
+                                size_t workspace_bytes, void *stream) {
+  if (!blob || !layout || !pool || !tables || !ids || !next_ids || !workspace) return Q3_ERR_NULL;
+  const q3_layout &L = *layout;
+  if (L.head_dim != 128 || L.hidden % 256 || L.inter % 256 || L.max_seq % kPT) return Q3_ERR_SHAPE;
+  if (n_seqs == 0 || T == 0) return Q3_OK;
+  if (T > L.max_seq || (size_t)(T + kPT - 1) / kPT > max_pages) return Q3_ERR_CAPACITY;
+  if ((size_t)n_seqs * T > 0x7fffffffu / L.inter) return Q3_ERR_CAPACITY;
+  if (workspace_bytes < q3_prefill_workspace_bytes(layout, n_seqs, T)) return Q3_ERR_CAPACITY;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256) return Q3_ERR_ALIGN;
+  if (!pool->k || !pool->v || !pool->ks || !pool->vs) return Q3_ERR_NULL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void *s = st;
+  const int64_t *o = L.off;
+  const uint32_t B = n_seqs, H = L.hidden, HD = L.head_dim, QW = L.heads * HD,
+                 KW = L.kv_heads * HD, I = L.inter, V = L.vocab, HALF = HD / 2;
+  const uint32_t M = B * T;
+  char *bl = static_cast<char *>(blob);
+  PrefillWs w = carve(L, M, B, static_cast<char *>(workspace));
+
+  k_prefill_rope_rows<<<M, 64, 0, st>>>(reinterpret_cast<const float *>(bl + o[Q3_OFF_COS]),
+                                        reinterpret_cast<const float *>(bl + o[Q3_OFF_SIN]), HALF,
+                                        T, w.cos, w.sin);
+  Q3_TRY(q3h::launch_status());
+
+  const q3_view x = v2(w.x, M, H, Q3_DT_F32), h = v2(w.h, M, H, Q3_DT_F32);
+  const q3_view h8 = v2(w.h8, M, H, Q3_DT_I8), hs = v2(w.hs, M, H / 256, Q3_DT_F32);
+  const q3_view q8 = v2(w.q8, M, QW, Q3_DT_I8), qs = v2(w.qs, M, L.heads, Q3_DT_F32);
+  const q3_view o8 = v2(w.o8, M, QW, Q3_DT_I8), os = v2(w.os, M, L.heads, Q3_DT_F32);
+  const q3_view k8 = v2(w.k8, M, KW, Q3_DT_I8), ks = v2(w.ks, M, L.kv_heads, Q3_DT_F32);
+  const q3_view v8 = v2(w.v8, M, KW, Q3_DT_I8), vs = v2(w.vs, M, L.kv_heads, Q3_DT_F32);
+  const q3_view s8 = v2(w.s8, M, I, Q3_DT_I8), ss = v2(w.ss, M, I / 256, Q3_DT_F32);
+  const q3_view cosv = v2(w.cos, M, HALF, Q3_DT_F32), sinv = v2(w.sin, M, HALF, Q3_DT_F32);
+  const q3_view idv = v2(const_cast<int32_t *>(ids), M, 1, Q3_DT_I32);
+  const q3_view emb = v2(bl + o[Q3_OFF_EMB], V, H, Q3_DT_I8);
+  const q3_view emb_s = v2(bl + o[Q3_OFF_EMB] + (int64_t)V * H, V, 1, Q3_DT_F32);
+  const q3_view lm = v2(bl + o[Q3_OFF_LM], V, H, Q3_DT_I8);
+  const q3_view lm_s = v2(bl + o[Q3_OFF_LM] + (int64_t)V * H, V, 1, Q3_DT_F32);
+  const q3_view nf = v2(bl + o[Q3_OFF_NF], H, 1, Q3_DT_F32);
+  const float inv_h = 1.0f / static_cast<float>(H), inv_hd = 1.0f / static_cast<float>(HD);
+
+  {
+    const q3_view n1_0 = v2(bl + o[Q3_OFF_N1], H, 1, Q3_DT_F32);
+    Q3_TRY(q3_embedding_rmsnorm_rows(&emb, &emb_s, &idv, &x, &n1_0, &h, inv_h, s));
+  }
+  for (uint32_t Li = 0; Li < L.layers; ++Li) {
+    char *lw = bl + o[Q3_OFF_LQ] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERW_STRIDE];
+    char *ln = bl + o[Q3_OFF_N1] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERN_STRIDE];
+    auto W = [&](int key, uint32_t r, uint32_t c) { return v2(lw + (o[key] - o[Q3_OFF_LQ]), r, c, Q3_DT_I8); };
+    auto S = [&](int key, uint32_t r) { return v2(lw + (o[key] - o[Q3_OFF_LQ]), r, 1, Q3_DT_F32); };
+    const q3_view wq = W(Q3_OFF_LQ, QW, H), wk = W(Q3_OFF_LK, KW, H), wv = W(Q3_OFF_LV, KW, H);
+    const q3_view wo = W(Q3_OFF_LO, H, QW), wg = W(Q3_OFF_LG, I, H), wu = W(Q3_OFF_LU, I, H);
+    const q3_view wd = W(Q3_OFF_LD, H, I);
+    const q3_view wqs = S(Q3_OFF_LQ_SCALE, QW), wks = S(Q3_OFF_LK_SCALE, KW);
+    const q3_view wvs = S(Q3_OFF_LV_SCALE, KW), wos = S(Q3_OFF_LO_SCALE, H);
+    const q3_view wgs = S(Q3_OFF_LG_SCALE, I), wus = S(Q3_OFF_LU_SCALE, I);
+    const q3_view wds = S(Q3_OFF_LD_SCALE, H);
+    const q3_view n1 = v2(ln, H, 1, Q3_DT_F32);
+    const q3_view nq = v2(ln + (o[Q3_OFF_NQ] - o[Q3_OFF_N1]), HD, 1, Q3_DT_F32);
+    const q3_view nk = v2(ln + (o[Q3_OFF_NK] - o[Q3_OFF_N1]), HD, 1, Q3_DT_F32);
+    const q3_view n2 = v2(ln + (o[Q3_OFF_N2] - o[Q3_OFF_N1]), H, 1, Q3_DT_F32);
+    char *pk = static_cast<char *>(pool->k) + Li * pool->layer_stride;
+    char *pv = static_cast<char *>(pool->v) + Li * pool->layer_stride;
+    char *pks = static_cast<char *>(pool->ks) + Li * pool->scale_layer_stride;
+    char *pvs = static_cast<char *>(pool->vs) + Li * pool->scale_layer_stride;
+
+    if (Li != 0) Q3_TRY(q3_rmsnorm_rows(&x, &n1, &h, inv_h, s));
+    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wv, &wvs, nullptr, 256, nullptr, &v8, &vs, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wk, &wks, nullptr, 256, nullptr, &k8, &ks, &nk,
+                                  &cosv, &sinv, inv_hd, s));
+    k_prefill_scatter<<<M, 64, 0, st>>>(w.k8, w.v8, w.ks, w.vs, tables, max_pages, (int)T, pk, pv,
+                                        pks, pvs, KW, L.kv_heads);
+    Q3_TRY(q3h::launch_status());
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wq, &wqs, nullptr, 256, nullptr, &q8, &qs, &nq, &cosv,
+                                  &sinv, inv_hd, s));
+    {
+      q3::AttnArgs a{};
+      a.q8 = reinterpret_cast<const char *>(w.q8);
+      a.q_rb = QW;
+      a.qs = reinterpret_cast<const char *>(w.qs);
+      a.qs_rb = 4 * L.heads;
+      a.o8 = reinterpret_cast<char *>(w.o8);
+      a.o_rb = QW;
+      a.os = reinterpret_cast<char *>(w.os);
+      a.os_rb = 4 * L.heads;
+      a.k = pk;
+      a.v = pv;
+      a.ks = pks;
+      a.vs = pvs;
+      a.table = tables;
+      a.table_stride = max_pages;
+      a.page_tokens = kPT;
+      a.page_bytes = kPT * KW;
+      a.row_bytes = KW;
+      a.scale_page_bytes = kPT * 4 * L.kv_heads;
+      a.scale_row_bytes = 4 * L.kv_heads;
+      a.heads = L.heads;
+      a.kv_heads = L.kv_heads;
+      a.q_rows = (int)T;
+      a.kv_len = (int)T;
+      a.kv_len_dev = nullptr;
+      a.causal = 1;
+      a.qk_scale = kInvSqrt128;
+      Q3_TRY(q3::attention_launch(a, (int)B, st));
+    }
+    Q3_TRY(q3_gemm_nt_group_store(&o8, &os, &wo, &wos, nullptr, 128, &x, nullptr, nullptr, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+    Q3_TRY(q3_rmsnorm_rows(&x, &n2, &h, inv_h, s));
+    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    Q3_TRY(q3_gemm_gate_up_swiglu_quant(&h8, &hs, &wg, &wgs, &wu, &wus, &s8, &ss, 256, s));
+    Q3_TRY(q3_gemm_nt_group_store(&s8, &ss, &wd, &wds, nullptr, 256, &x, nullptr, nullptr, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+  }
+  // last row of every sequence: final norm + quant, lm_head fused with argmax
+  k_prefill_last_rows<<<B, 256, 0, st>>>(w.x, (int)T, (int)H, w.xl, w.best, next_ids);
+  Q3_TRY(q3h::launch_status());
+  const q3_view xl = v2(w.xl, B, H, Q3_DT_F32), hl = v2(w.hl, B, H, Q3_DT_F32);
+  const q3_view h8l = v2(w.h8l, B, H, Q3_DT_I8), hsl = v2(w.hsl, B, H / 256, Q3_DT_F32);
+  Q3_TRY(q3_rmsnorm_rows(&xl, &nf, &hl, inv_h, s));
+  Q3_TRY(q3_quant_rows_heads(&hl, &h8l, &hsl, 256, s));
+  return q3_gemm_nt_group_argmax(&h8l, &hsl, &lm, &lm_s, w.best, next_ids, 256, w.keys, 8 * B, s);
+}

@@ -183,3 +183,65 @@ def test_decode_step_batch(q3, layers, vocab, lens):
             assert np.array_equal(pool["pv"][L, p, sl], kvs[s].v8[L][n])
             same_bits(pool["pks"][L, p, sl], kvs[s].ks[L][n])
             same_bits(pool["pvs"][L, p, sl], kvs[s].vs[L][n])
+
+
+# ---------------------------------------------------------------- batched prefill
+def _prefill_case(q3, layers, vocab, B, T, seed=0):
+    """Prefill B prompts of T tokens on the oracle (32-row chunks) and in ONE
+    batched GPU prefill into a shared page pool under shuffled page tables."""
+    shape = synth.Shape(layers=layers, vocab=vocab, max_seq=(T + 31) // 32 * 32)
+    w = synth.build_model(shape)
+    rng = np.random.default_rng(seed)
+    max_pages = shape.max_seq // 32
+    total_pages = B * max_pages
+    tables = rng.permutation(total_pages).reshape(B, max_pages).astype(np.uint16)
+    prompts = rng.integers(0, vocab, (B, T))
+    want_ids, want_kv = [], []
+    for s in range(B):
+        kv = O.KV.empty(w, shape.max_seq)
+        pos, lg = 0, None
+        while pos < T:
+            rows = min(32, T - pos)
+            lg = O.forward_chunk(w, [int(v) for v in prompts[s, pos:pos + rows]], kv, pos, rows,
+                                 pos + rows == T)
+            pos += rows
+        want_ids.append(O.argmax_logits(lg))
+        want_kv.append(kv)
+    dims = q3.model.Dims(layers=layers, vocab=vocab, max_seq=shape.max_seq)
+    bm = q3.model.BlobModel(dims).load_weights(w)
+    kw = 8 * 128
+    d = {"pk": torch.zeros((layers, total_pages, 32, kw), dtype=torch.int8, device="cuda"),
+         "pv": torch.zeros((layers, total_pages, 32, kw), dtype=torch.int8, device="cuda"),
+         "pks": torch.zeros((layers, total_pages, 32, 8), dtype=torch.float32, device="cuda"),
+         "pvs": torch.zeros((layers, total_pages, 32, 8), dtype=torch.float32, device="cuda")}
+    pool = q3._lib.KVPool(d["pk"].data_ptr(), d["pv"].data_ptr(), d["pks"].data_ptr(),
+                          d["pvs"].data_ptr(), total_pages * 32 * kw, total_pages * 32 * 8 * 4,
+                          total_pages)
+    tab = torch.from_numpy(tables.view(np.int16)).cuda()
+    ids_d = torch.from_numpy(prompts.astype(np.int32).reshape(-1)).cuda()
+    nxt = torch.full((B,), -1, dtype=torch.int32, device="cuda")
+    lib = q3._lib.lib()
+    wsb = lib.q3_prefill_workspace_bytes(C.byref(bm.L), B, T)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
+        bm.blob.data_ptr(), C.byref(bm.L), C.byref(pool), tab.data_ptr(), max_pages,
+        ids_d.data_ptr(), B, T, nxt.data_ptr(), ws.data_ptr(), wsb,
+        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert q3._lib.lib().q3_device_status() == 0
+    return (nxt.cpu().numpy(), want_ids, {k: v.cpu().numpy() for k, v in d.items()}, tables,
+            want_kv)
+
+
+@pytest.mark.parametrize("layers,vocab,B,T", [(1, 1024, 3, 70), (2, 4096, 2, 128)])
+def test_prefill_batch(q3, layers, vocab, B, T):
+    got, want, pool, tables, kvs = _prefill_case(q3, layers, vocab, B, T)
+    assert list(got) == want
+    for s in range(B):                    # every prompt row of every layer, un-paged
+        for L in range(layers):
+            for t in range(T):
+                p, sl = tables[s, t // 32], t % 32
+                assert np.array_equal(pool["pk"][L, p, sl], kvs[s].k8[L][t])
+                assert np.array_equal(pool["pv"][L, p, sl], kvs[s].v8[L][t])
+                same_bits(pool["pks"][L, p, sl], kvs[s].ks[L][t])
+                same_bits(pool["pvs"][L, p, sl], kvs[s].vs[L][t])
