@@ -51,6 +51,10 @@ def parse():
     ap.add_argument("--seqs", type=int, default=SEQS)
     ap.add_argument("--ctx", type=int, default=CTX)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the config-5 prefill measurement reported under 'prefill'")
+    ap.add_argument("--prefill-seqs", type=int, default=16)
+    ap.add_argument("--prefill-len", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer count (only for small profiling captures; the metric needs 28)")
     return ap.parse_args()
@@ -258,6 +262,11 @@ def run_ours(args) -> None:
         ms, e2e_ms = float(t[0]), float(t[1])
     if graph is not None:
         del graph
+    prefill = None
+    if not args.no_prefill:
+        del pool, ws
+        torch.cuda.empty_cache()
+        prefill = measure_prefill(args, q3, lib, dev, rank, world, dist)
     if dist:
         dist.destroy_process_group()
     if rank != 0:
@@ -293,9 +302,71 @@ def run_ours(args) -> None:
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650"},
         "clocks": ck,
     }
+    if prefill is not None:
+        line["prefill"] = prefill
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(args.ctx)
     print(json.dumps(line), flush=True)
+
+
+# config 5: 16 x 4096-token prompts, causal, 28 layers, vocab 151936
+def prefill_ops(B: int, T: int, layers: int) -> float:
+    """Algorithmic int8 ops of one batched prefill: linear layers for every
+    token, the exact causal triangle of Q.K and P.V, lm_head for the last row."""
+    H, QW, KW, I, V = 1024, 2048, 1024, 3072, VOCAB
+    linear = 2 * (H * (QW + 2 * KW) + QW * H + 2 * H * I + I * H)     # per token per layer
+    attn = 2 * 2 * 16 * 128 * (T * (T + 1) // 2)                      # per layer per sequence
+    return float(B) * (T * layers * linear + layers * attn + 2 * H * V)
+
+
+def measure_prefill(args, q3, lib, dev, rank, world, dist) -> dict:
+    import torch
+    from q3b200 import synthetic
+    from q3b200.model import Dims
+    B, T = args.prefill_seqs, args.prefill_len
+    dims = Dims(layers=args.layers, vocab=VOCAB, max_seq=T)
+    bm = synthetic.random_blob_model(dims, seed=4000 + rank, device=dev)
+    pages = B * (T // 32)
+    pool = synthetic.KVPoolTensors(args.layers, pages, 8, device=dev)
+    g = torch.Generator().manual_seed(5000 + rank)
+    tables = torch.randperm(pages, generator=g).reshape(B, T // 32).to(torch.int16).to(dev)
+    ids = torch.randint(0, VOCAB, (B * T,), generator=g, dtype=torch.int32).to(dev)
+    nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+    wsb = lib.q3_prefill_workspace_bytes(C.byref(bm.L), B, T)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    cpool = pool.c()
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
+            bm.blob.data_ptr(), C.byref(bm.L), C.byref(cpool), tables.data_ptr(), T // 32,
+            ids.data_ptr(), B, T, nxt.data_ptr(), ws.data_ptr(), wsb, stream.cuda_stream))
+
+    with torch.cuda.stream(stream):
+        step()                                   # warm-up
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        step()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    ops = prefill_ops(B, T, args.layers)
+    peak = 4500.0   # nominal dense int8 TOPS per B200 (no measured int8 peak on this pool)
+    return {"metric": "prefill tokens/s (config 5)", "value": round(world * B * T / (ms * 1e-3), 1),
+            "unit": "tokens/s", "ms_per_step": round(ms, 2), "steps": 1, "warmup": 1,
+            "config": {"workload": f"config 5: {B} x {T}-token prompts, causal, {args.layers} layers, "
+                                   f"vocab {VOCAB}, greedy next token", "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "tensor", "achieved": round(ops / (ms * 1e-3) / 1e12, 2),
+                         "peak": peak, "unit": "TOPS (int8)", "frac": round(ops / (ms * 1e-3) / 1e12 / peak, 4),
+                         "ops_per_step": ops, "peak_source": "nominal dense int8 (no measured int8 peak)"}}
 
 
 # ---------------------------------------------------------------------------

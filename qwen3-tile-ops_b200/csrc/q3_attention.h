@@ -49,6 +49,27 @@ struct DecodeAttnArgs {
 };
 
 // pdl: launched as a programmatic dependent of the kernel before it
+// Causal prompt attention on the tensor cores (q3_attention_prefill.cu): query
+// row t of sequence s is row s*T + t of q8/qs/o8/os, at position t; the keys
+// are positions 0..t of the sequence's pages (32 tokens, head_dim 128).
+struct PrefillAttnArgs {
+  const char *qs;      // [n_seqs*T][heads] f32
+  long qs_rb;
+  char *o8;            // [n_seqs*T][heads*128] i8
+  long o_rb;
+  char *os;            // [n_seqs*T][heads] f32
+  long os_rb;
+  const char *ks, *vs;           // per-head scale pools of this layer
+  const uint16_t *table;         // [n_seqs][table_stride]
+  long table_stride;
+  uint32_t scale_page_bytes, scale_row_bytes, num_pages;
+  int heads, kv_heads, T;
+  float qk_scale;
+};
+int attention_prefill_launch(const PrefillAttnArgs &p, const void *q8, long q_rb, int M,
+                             const void *k_pool, const void *v_pool, uint32_t page_bytes,
+                             uint32_t row_bytes, int n_seqs, cudaStream_t s);
+
 int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const void *v_pool,
                             uint32_t num_pages, int kv_heads, int n_seqs, cudaStream_t s,
                             bool pdl = false);

@@ -400,6 +400,7 @@ int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const v
 namespace q3 {
 int gemm_device_status_take();
 int dgemm_device_status_take();
+int pattn_device_status_take();
 }
 
 extern "C" int q3_device_status(void) {
@@ -411,5 +412,8 @@ extern "C" int q3_device_status(void) {
   const int dg = q3::dgemm_device_status_take();
   if (dg < 0) return -1;
   v |= static_cast<unsigned int>(dg);
+  const int pa = q3::pattn_device_status_take();
+  if (pa < 0) return -1;
+  v |= static_cast<unsigned int>(pa);
   return static_cast<int>(v) | g;
 }

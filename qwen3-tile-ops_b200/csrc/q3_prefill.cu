@@ -203,7 +203,27 @@ extern "C" int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv
     Q3_TRY(q3h::launch_status());
     Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wq, &wqs, nullptr, 256, nullptr, &q8, &qs, &nq, &cosv,
                                   &sinv, inv_hd, s));
-    {
+    if (pool->num_pages > 0 && L.heads % L.kv_heads == 0 && (T + kPT - 1) / kPT <= max_pages) {
+      q3::PrefillAttnArgs a{};
+      a.qs = reinterpret_cast<const char *>(w.qs);
+      a.qs_rb = 4 * L.heads;
+      a.o8 = reinterpret_cast<char *>(w.o8);
+      a.o_rb = QW;
+      a.os = reinterpret_cast<char *>(w.os);
+      a.os_rb = 4 * L.heads;
+      a.ks = pks;
+      a.vs = pvs;
+      a.table = tables;
+      a.table_stride = max_pages;
+      a.scale_page_bytes = kPT * 4 * L.kv_heads;
+      a.scale_row_bytes = 4 * L.kv_heads;
+      a.num_pages = pool->num_pages;
+      a.heads = L.heads;
+      a.kv_heads = L.kv_heads;
+      a.T = (int)T;
+      a.qk_scale = kInvSqrt128;
+      Q3_TRY(q3::attention_prefill_launch(a, w.q8, QW, (int)M, pk, pv, kPT * KW, KW, (int)B, st));
+    } else {
       q3::AttnArgs a{};
       a.q8 = reinterpret_cast<const char *>(w.q8);
       a.q_rb = QW;

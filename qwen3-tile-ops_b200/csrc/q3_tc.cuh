@@ -90,10 +90,18 @@ __device__ __forceinline__ uint64_t sdesc_plain(uint32_t saddr, uint32_t lbo, ui
   return d;                                          // layout type 0: no swizzle
 }
 // instruction descriptor, kind::i8: s32 accumulate, s8 x s8, M = 128, N = n;
-// a_mn: A is MN-major (otherwise K-major); B is K-major
-__host__ __device__ constexpr uint32_t idesc_i8(int n, bool a_mn = false) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | (a_mn ? (1u << 15) : 0u) |
+// a_mn / b_mn: that operand is MN-major (otherwise K-major)
+__host__ __device__ constexpr uint32_t idesc_i8(int n, bool a_mn = false, bool b_mn = false) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (a_mn ? (1u << 15) : 0u) | (b_mn ? (1u << 16) : 0u) |
          (static_cast<uint32_t>(n >> 3) << 17) | ((128u >> 4) << 24);
+}
+__device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *m, int x, int y, int z,
+                                       unsigned long long *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
+      : "memory");
 }
 __device__ __forceinline__ void mma_i8(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t id,
                                        uint32_t acc) {

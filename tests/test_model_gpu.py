@@ -233,7 +233,7 @@ def _prefill_case(q3, layers, vocab, B, T, seed=0):
             want_kv)
 
 
-@pytest.mark.parametrize("layers,vocab,B,T", [(1, 1024, 3, 70), (2, 4096, 2, 128)])
+@pytest.mark.parametrize("layers,vocab,B,T", [(1, 1024, 3, 70), (2, 4096, 2, 128), (1, 1024, 2, 300)])
 def test_prefill_batch(q3, layers, vocab, B, T):
     got, want, pool, tables, kvs = _prefill_case(q3, layers, vocab, B, T)
     assert list(got) == want
