@@ -40,12 +40,14 @@ static __device__ __noinline__ float exp2_hard_lookup(float x, float fallback) {
 
 // ---------------------------------------------------------------------------
 // Correctly rounded float32 exp2.
-// y = exp2 in double (CUDA libm, max 1 ulp); RN_f32(y) equals RN_f32(2^x)
-// unless y lies within 2^-47*y of a midpoint between adjacent float32 values;
-// those inputs are in the table made by gen_exp2_table.py (every float32 input
-// whose 2^x is within 2^-46 of a midpoint, resolved at 200 bits).
+//
+// exp2_cr_libm: y = exp2 in double (CUDA libm, max 1 ulp); RN_f32(y) equals
+// RN_f32(2^x) unless y lies within 2^-47*y of a midpoint between adjacent
+// float32 values; those inputs are in the table made by gen_exp2_table.py
+// (every float32 input whose 2^x is within 2^-46 of a midpoint, resolved at
+// 200 bits).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float exp2_cr(float x) {
+__device__ __forceinline__ float exp2_cr_libm(float x) {
   const double y = exp2(static_cast<double>(x));
   const float r = __double2float_rn(y);
   const unsigned rb = __float_as_uint(r);
@@ -56,6 +58,54 @@ __device__ __forceinline__ float exp2_cr(float x) {
   if (fabs(y - mid) <= y * 7.105427357601002e-15 /* 2^-47 */ && y > 0.0)
     return exp2_hard_lookup(x, r);
   return r;
+}
+
+// 2^(i/64), i = 0..63, correctly rounded to double (computed at 300 bits).
+static __device__ const unsigned long long g_exp2_frac64[64] = {
+    0x3ff0000000000000ull, 0x3ff02c9a3e778061ull, 0x3ff059b0d3158574ull, 0x3ff0874518759bc8ull,
+    0x3ff0b5586cf9890full, 0x3ff0e3ec32d3d1a2ull, 0x3ff11301d0125b51ull, 0x3ff1429aaea92de0ull,
+    0x3ff172b83c7d517bull, 0x3ff1a35beb6fcb75ull, 0x3ff1d4873168b9aaull, 0x3ff2063b88628cd6ull,
+    0x3ff2387a6e756238ull, 0x3ff26b4565e27cddull, 0x3ff29e9df51fdee1ull, 0x3ff2d285a6e4030bull,
+    0x3ff306fe0a31b715ull, 0x3ff33c08b26416ffull, 0x3ff371a7373aa9cbull, 0x3ff3a7db34e59ff7ull,
+    0x3ff3dea64c123422ull, 0x3ff4160a21f72e2aull, 0x3ff44e086061892dull, 0x3ff486a2b5c13cd0ull,
+    0x3ff4bfdad5362a27ull, 0x3ff4f9b2769d2ca7ull, 0x3ff5342b569d4f82ull, 0x3ff56f4736b527daull,
+    0x3ff5ab07dd485429ull, 0x3ff5e76f15ad2148ull, 0x3ff6247eb03a5585ull, 0x3ff6623882552225ull,
+    0x3ff6a09e667f3bcdull, 0x3ff6dfb23c651a2full, 0x3ff71f75e8ec5f74ull, 0x3ff75feb564267c9ull,
+    0x3ff7a11473eb0187ull, 0x3ff7e2f336cf4e62ull, 0x3ff82589994cce13ull, 0x3ff868d99b4492edull,
+    0x3ff8ace5422aa0dbull, 0x3ff8f1ae99157736ull, 0x3ff93737b0cdc5e5ull, 0x3ff97d829fde4e50ull,
+    0x3ff9c49182a3f090ull, 0x3ffa0c667b5de565ull, 0x3ffa5503b23e255dull, 0x3ffa9e6b5579fdbfull,
+    0x3ffae89f995ad3adull, 0x3ffb33a2b84f15fbull, 0x3ffb7f76f2fb5e47ull, 0x3ffbcc1e904bc1d2ull,
+    0x3ffc199bdd85529cull, 0x3ffc67f12e57d14bull, 0x3ffcb720dcef9069ull, 0x3ffd072d4a07897cull,
+    0x3ffd5818dcfba487ull, 0x3ffda9e603db3285ull, 0x3ffdfc97337b9b5full, 0x3ffe502ee78b3ff6ull,
+    0x3ffea4afa2a490daull, 0x3ffefa1bee615a27ull, 0x3fff50765b6e4540ull, 0x3fffa7c1819e90d8ull};
+
+// exp2_cr: the same correctly rounded result with a table-driven double
+// evaluation (Tang's method for exp): x = k/64 + r with k = rint(64 x) and
+// |r| <= 1/128 (both exact), 2^x = 2^(k >> 6) * 2^((k & 63)/64) * 2^r, and 2^r
+// by its Taylor series in r ln2 to degree 5 (truncation < 2^-54).  The double
+// result is within about 2^-51 (relative) of 2^x, so when its 29 bits below
+// the float32 precision are more than 64 double ulps away from the midpoint
+// pattern, rounding it to float32 rounds 2^x; otherwise the input is looked up
+// in the hard-case table (every input within 2^-46 of a midpoint).  Results
+// below 2^-125 (float32 subnormals) and non-finite inputs take exp2_cr_libm.
+__device__ __forceinline__ float exp2_cr(float x) {
+  if (!(x >= -125.0f && x < 128.0f)) return x < -151.0f ? 0.0f : exp2_cr_libm(x);
+  const float kf = rintf(__fmul_rn(x, 64.0f));                  // exact
+  const int k = static_cast<int>(kf);
+  const double r = __fma_rn(static_cast<double>(kf), -0.015625, static_cast<double>(x));  // exact
+  double p = 0.0013333558146428443;                              // (ln2)^5 / 5!
+  p = __fma_rn(p, r, 0.009618129107628477);                      // (ln2)^4 / 4!
+  p = __fma_rn(p, r, 0.05550410866482158);                       // (ln2)^3 / 3!
+  p = __fma_rn(p, r, 0.24022650695910072);                       // (ln2)^2 / 2!
+  p = __fma_rn(p, r, 0.6931471805599453);                        // ln2
+  p = __fma_rn(p, r, 1.0);
+  const double t = __longlong_as_double(static_cast<long long>(g_exp2_frac64[k & 63]));
+  const long long yb =
+      __double_as_longlong(__dmul_rn(t, p)) + (static_cast<long long>(k >> 6) << 52);
+  const float res = __double2float_rn(__longlong_as_double(yb));
+  const unsigned low = static_cast<unsigned>(yb) & 0x1FFFFFFFu;  // bits below float32 precision
+  if (low - ((1u << 28) - 64u) <= 128u) return exp2_hard_lookup(x, res);
+  return res;
 }
 
 // exp as amulx(log2e) + aexp2 (ref_qwen3.py:27-29)
