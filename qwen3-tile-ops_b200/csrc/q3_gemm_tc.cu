@@ -5,14 +5,17 @@
 // Orientation: the MMA's M dimension is 128 WEIGHT rows (output features), its
 // N dimension a tile of NTOK tokens (activation rows), K the input features.
 // One TMEM accumulator [128 lanes = features][NTOK columns = tokens] int32 per
-// K-group; two of them alternate, so the epilogue warps dequantise group g
+// K-group; several of them rotate, so the epilogue warps dequantise group g
 //     acc[n][m] = acc[n][m] + (f32(part[n][m]) * b_scale[n]) * a_scale[m][g]
 // (the reference's order, ref_qwen3.py:152-157) while the MMA warp runs g+1.
 // A thread of the epilogue owns one feature row, so every per-feature reduction
 // of the reference (head RMSNorm, head/group absmax) is a reduction over lanes.
 //
-// Warps: 0-3 epilogue (TMEM lanes 32w..32w+31), 4 TMA producer, 5 MMA issuer
-// and TMEM owner.  Operands arrive by TMA (no multicast) into 128B-swizzled
+// Persistent: one CTA per SM walks the (feature tile, token tile) list; the stage
+// ring and the TMEM buffers run on across tiles, so a tile's epilogue overlaps
+// the next tile's copies and MMAs.  Warps: 0-7 epilogue (two per TMEM lane
+// quadrant: warp w reads lanes 32 (w % 4) .. for half w / 4 of the tokens),
+// 8 TMA producer, 9 MMA issuer and TMEM owner.  Operands arrive by TMA (no multicast) into 128B-swizzled
 // shared memory, 128 K-bytes per stage.  No warp leaves before the others; every
 // mbarrier wait is bounded (about one second) and a timeout sets bit 16 of the
 // device error word, drains the copies and MMAs in flight and frees TMEM.
@@ -40,7 +43,7 @@ int gemm_device_status_take() {
 namespace tc {
 
 constexpr unsigned kErrGemmTimeout = 1u << 16;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;   // two per TMEM lane quadrant
 constexpr int THREADS = (EPI_WARPS + 2) * 32;
 
 template <int NTOK, int MODE>
@@ -96,10 +99,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   const GemmArgs &p = args.g;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = args.groups, NB = args.boxes;
-  const int row0 = blockIdx.x * 128 * C::TILES;   // first feature row of this CTA
-  const int m0 = blockIdx.y * NTOK;               // first token
-  const int mvalid = min(NTOK, p.M - m0);
-  const int total_it = C::TILES * G * NB;         // producer / MMA k-iterations
+  const int tiles_x = p.N / (128 * C::TILES);     // feature tiles
+  const int ntiles = tiles_x * ((p.M + NTOK - 1) / NTOK);
+  const int tile_it = C::TILES * G * NB;          // producer / MMA k-iterations per tile
+  // persistent: this CTA takes tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+  // (feature tile fastest, so the CTAs in flight share weights and activations)
+  auto tile_rows = [&](int tile) { return (tile % tiles_x) * 128 * C::TILES; };
+  auto tile_m0 = [&](int tile) { return (tile / tiles_x) * NTOK; };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -121,14 +127,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (warp < EPI_WARPS) {        // this token tile's activation scales, all groups
-    for (int i = threadIdx.x; i < NTOK * G; i += EPI_WARPS * 32) {
-      const int m = i / G, g = i % G;
-      sm.ascale[i] = (m < mvalid)
-                         ? *reinterpret_cast<const float *>(p.a_scale + (long)(m0 + m) * p.as_rb + g * 4)
-                         : 0.0f;
-    }
-  }
   fence_before();
   __syncthreads();
   fence_after();
@@ -138,22 +136,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ TMA producer
     int issued = 0;
     bool ok = true;
-    for (int it = 0; it < total_it && ok; ++it) {
-      const int st = it % STAGES;
-      if (lane == 0) {
-        if (!mbar_wait(&sm.empty[st], ((it / STAGES) & 1) ^ 1, &sm.abort)) ok = false;
-        else {
-          const int t = it / (G * NB), r = it % (G * NB);
-          const int k0 = r * 128;   // (g * NB + box) * 128
-          mbar_expect_tx(&sm.full[st], C::STAGE_BYTES);
-          int8_t *dst = sm.stage[st];
-          tma_2d(dst, &tmA, k0, row0 + t * 128, &sm.full[st]);
-          if (C::NACC == 2) tma_2d(dst + C::A_BYTES, &tmA2, k0, row0 + t * 128, &sm.full[st]);
-          tma_2d(dst + C::NACC * C::A_BYTES, &tmB, k0, m0, &sm.full[st]);
-          ++issued;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      const int row0 = tile_rows(tile), m0 = tile_m0(tile);
+      for (int ti = 0; ti < tile_it && ok; ++ti, ++it) {
+        const int st = it % STAGES;
+        if (lane == 0) {
+          if (!mbar_wait(&sm.empty[st], ((it / STAGES) & 1) ^ 1, &sm.abort)) ok = false;
+          else {
+            const int t = ti / (G * NB), r = ti % (G * NB);
+            const int k0 = r * 128;   // (g * NB + box) * 128
+            mbar_expect_tx(&sm.full[st], C::STAGE_BYTES);
+            int8_t *dst = sm.stage[st];
+            tma_2d(dst, &tmA, k0, row0 + t * 128, &sm.full[st]);
+            if (C::NACC == 2) tma_2d(dst + C::A_BYTES, &tmA2, k0, row0 + t * 128, &sm.full[st]);
+            tma_2d(dst + C::NACC * C::A_BYTES, &tmB, k0, m0, &sm.full[st]);
+            ++issued;
+          }
         }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
     if (!ok && lane == 0) {
       atomicOr(&g_gemm_error, kErrGemmTimeout);
@@ -166,7 +168,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     constexpr uint32_t ID = idesc_i8(NTOK);
     bool ok = true;
     int it = 0;
-    for (int gi = 0; gi < C::TILES * G && ok; ++gi) {
+    const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    for (int gi = 0; gi < my_tiles * C::TILES * G && ok; ++gi) {
       const int buf = gi % C::NBUF;
       if (lane == 0 && !mbar_wait(&sm.tempty[buf], ((gi / C::NBUF) & 1) ^ 1, &sm.abort)) ok = false;
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -205,59 +208,89 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int tid = threadIdx.x;                 // feature row within the 128-row tile
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    // warp w: feature rows 32 (w % 4) + lane of the tile (its TMEM lane
+    // quadrant) and tokens c0 .. c0 + HT - 1 of the token tile, c0 = HT (w / 4)
+    constexpr int HT = NTOK / 2;
+    constexpr int TPW = NTOK / EPI_WARPS;          // tokens per warp in the per-token passes
+    const int f = (warp & 3) * 32 + lane, c0 = (warp >> 2) * HT;
+    const int etid = threadIdx.x;                  // 0 .. EPI_WARPS*32 - 1
+    const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    float nwv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (MODE == EPI_NORMROPE) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) nwv[k] = p.nw[lane + 32 * k];
+    }
     bool ok = true;
     int gi = 0;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+    const int row0 = tile_rows(tile), m0 = tile_m0(tile);
+    const int mvalid = min(NTOK, p.M - m0);
+    epi_sync();                                  // the previous tile's readers are done
+    for (int i = etid; i < NTOK * G; i += EPI_WARPS * 32) {   // this tile's activation scales
+      const int m = i / G, g = i % G;
+      sm.ascale[i] = (m < mvalid)
+                         ? *reinterpret_cast<const float *>(p.a_scale + (long)(m0 + m) * p.as_rb + g * 4)
+                         : 0.0f;
+    }
+    epi_sync();
     for (int t = 0; t < C::TILES && ok; ++t) {
-      const int n = row0 + t * 128 + tid;
+      const int n = row0 + t * 128 + f;
       const float bs = p.b_scale[n];
       const float bs2 = (C::NACC == 2) ? p.b2_scale[n] : 0.0f;
-      float acc[C::NACC][NTOK];
+      float acc[C::NACC][HT];
 #pragma unroll
       for (int a = 0; a < C::NACC; ++a)
 #pragma unroll
-        for (int m = 0; m < NTOK; ++m) acc[a][m] = 0.0f;
+        for (int m = 0; m < HT; ++m) acc[a][m] = 0.0f;
       for (int g = 0; g < G; ++g, ++gi) {
         const int buf = gi % C::NBUF;
         if (!mbar_wait(&sm.tfull[buf], (gi / C::NBUF) & 1, &sm.abort)) { ok = false; break; }
         fence_after();
+        int v[C::NACC][HT];
+#pragma unroll
+        for (int a = 0; a < C::NACC; ++a)
+#pragma unroll
+          for (int c = 0; c < HT; c += 16)
+            tmem_ld16(lane_addr + (buf * C::NACC + a) * NTOK + c0 + c,
+                      *reinterpret_cast<int(*)[16]>(&v[a][c]));
+        tmem_wait_ld();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.tempty[buf]);
 #pragma unroll
         for (int a = 0; a < C::NACC; ++a) {
           const float b = a ? bs2 : bs;
 #pragma unroll
-          for (int c = 0; c < NTOK; c += 16) {
-            int v[16];
-            tmem_ld16(lane_addr + (buf * C::NACC + a) * NTOK + c, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float as = sm.ascale[(c + i) * G + g];
-              acc[a][c + i] = __fadd_rn(acc[a][c + i], __fmul_rn(__fmul_rn(i2f_small(v[i]), b), as));
-            }
-          }
+          for (int i = 0; i < HT; ++i)
+            acc[a][i] = __fadd_rn(acc[a][i],
+                                  __fmul_rn(__fmul_rn(i2f_small(v[a][i]), b), sm.ascale[(c0 + i) * G + g]));
         }
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.tempty[buf]);
       }
       if (!ok) break;
 
       // -------------------------------------------------------- epilogues
       if (MODE == EPI_STORE || MODE == EPI_ADD) {
+        float xv[HT];
+        if (MODE == EPI_ADD) {                     // every load before the first store
 #pragma unroll
-        for (int m = 0; m < NTOK; ++m) {
-          if (m < mvalid) {
-            float *row = reinterpret_cast<float *>(p.out + (long)(m0 + m) * p.out_rb);
-            row[n] = (MODE == EPI_ADD) ? __fadd_rn(row[n], acc[0][m]) : acc[0][m];
+          for (int i = 0; i < HT; ++i)
+            xv[i] = (c0 + i < mvalid)
+                        ? reinterpret_cast<const float *>(p.out + (long)(m0 + c0 + i) * p.out_rb)[n]
+                        : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < HT; ++i) {
+          if (c0 + i < mvalid) {
+            float *row = reinterpret_cast<float *>(p.out + (long)(m0 + c0 + i) * p.out_rb);
+            row[n] = (MODE == EPI_ADD) ? __fadd_rn(xv[i], acc[0][i]) : acc[0][i];
           }
         }
       } else if (MODE == EPI_ARGMAX) {
         // (max, first index) per token over the tile's 128 rows -> atomicMax of a
         // packed key (monotone value << 32 | ~index): largest value, then smallest index
 #pragma unroll
-        for (int m = 0; m < NTOK; ++m) {
-          const float v = __fadd_rn(acc[0][m], 0.0f);   // -0 -> +0: equal maxima compare equal
+        for (int i = 0; i < HT; ++i) {
+          const float v = __fadd_rn(acc[0][i], 0.0f);   // -0 -> +0: equal maxima compare equal
           const unsigned b = __float_as_uint(v);
           const unsigned key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
           unsigned long long k =
@@ -267,25 +300,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
             k = k2 > k ? k2 : k;
           }
-          if (lane == 0 && m < mvalid) atomicMax(p.arg_keys + m0 + m, k);
+          if (lane == 0 && c0 + i < mvalid) atomicMax(p.arg_keys + m0 + c0 + i, k);
         }
       } else {
         // stage this tile's values [feature][token] in shared memory (padded rows)
         // and continue with one warp per token (features l, l+32, l+64, l+96 per lane)
         if (MODE == EPI_SWIGLU) {
+          // silu(g)*u (ref_qwen3.py:194-200), element by element, then staged
 #pragma unroll
-          for (int m = 0; m < NTOK; ++m) {
-            sm.xchg[t * 128 + tid][m] = acc[0][m];
-            sm.xchg2[tid][m] = acc[1][m];
-          }
-          epi_sync();
-          // silu(g)*u (ref_qwen3.py:194-200), element by element (rolled loop)
-          for (int m = 0; m < mvalid; ++m) {
-            const float gt = sm.xchg[t * 128 + tid][m];
-            float e = exp_ref(__fmul_rn(gt, -1.0f));
-            e = __fadd_rn(e, 1.0f);
-            e = __fdiv_rn(1.0f, e);
-            sm.xchg[t * 128 + tid][m] = __fmul_rn(__fmul_rn(gt, e), sm.xchg2[tid][m]);
+          for (int i = 0; i < HT; ++i) {
+            float sw = 0.0f;
+            if (c0 + i < mvalid) {
+              const float gt = acc[0][i];
+              float e = exp_ref(__fmul_rn(gt, -1.0f));
+              e = __fadd_rn(e, 1.0f);
+              e = __fdiv_rn(1.0f, e);
+              sw = __fmul_rn(__fmul_rn(gt, e), acc[1][i]);
+            }
+            sm.xchg[t * 128 + f][c0 + i] = sw;
           }
           epi_sync();
           if (t == C::TILES - 1) {
@@ -309,10 +341,29 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         } else {
 #pragma unroll
-          for (int m = 0; m < NTOK; ++m) sm.xchg[tid][m] = acc[0][m];
+          for (int i = 0; i < HT; ++i) sm.xchg[f][c0 + i] = acc[0][i];
+          // rope rows of this warp's tokens, loaded while the others stage
+          float cs[TPW][2], sn[TPW][2];
+          if (MODE == EPI_NORMROPE) {
+#pragma unroll
+            for (int j = 0; j < TPW; ++j) {
+              const int m = warp + EPI_WARPS * j;
+              const int mm = m < mvalid ? m : 0;
+              const float *cr = reinterpret_cast<const float *>(p.cos + (long)(m0 + mm) * p.cos_rb);
+              const float *sr = reinterpret_cast<const float *>(p.sin + (long)(m0 + mm) * p.sin_rb);
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                cs[j][k] = cr[lane + 32 * k];
+                sn[j][k] = sr[lane + 32 * k];
+              }
+            }
+          }
           epi_sync();
           const int r0 = row0 + t * 128;
-          for (int m = warp; m < mvalid; m += EPI_WARPS) {
+#pragma unroll
+          for (int j = 0; j < TPW; ++j) {
+            const int m = warp + EPI_WARPS * j;
+            if (m >= mvalid) break;
             float v[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) v[k] = sm.xchg[lane + 32 * k][m];
@@ -324,16 +375,13 @@ __global__ void __launch_bounds__(THREADS, 1)
               ss = __fadd_rn(__fmul_rn(ss, p.inv_hd), kEps);
               const float r = rsqrt_ref(ss);
 #pragma unroll
-              for (int k = 0; k < 4; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], r), p.nw[lane + 32 * k]);
+              for (int k = 0; k < 4; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], r), nwv[k]);
               // rotate-half RoPE: pairs (l, l+64) and (l+32, l+96) live in this lane
-              const float *cr = reinterpret_cast<const float *>(p.cos + (long)(m0 + m) * p.cos_rb);
-              const float *sr = reinterpret_cast<const float *>(p.sin + (long)(m0 + m) * p.sin_rb);
 #pragma unroll
               for (int k = 0; k < 2; ++k) {
-                const float cs = cr[lane + 32 * k], sn = sr[lane + 32 * k];
                 const float l = v[k], rr = v[k + 2];
-                v[k] = __fsub_rn(__fmul_rn(l, cs), __fmul_rn(rr, sn));
-                v[k + 2] = __fadd_rn(__fmul_rn(l, sn), __fmul_rn(rr, cs));
+                v[k] = __fsub_rn(__fmul_rn(l, cs[j][k]), __fmul_rn(rr, sn[j][k]));
+                v[k + 2] = __fadd_rn(__fmul_rn(l, sn[j][k]), __fmul_rn(rr, cs[j][k]));
               }
             }
             float mx = 0.0f;
@@ -351,6 +399,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         epi_sync();   // the staging buffer is rewritten by the next tile
       }
     }
+    }                                            // tiles
     if (!ok && lane == 0) {
       atomicOr(&g_gemm_error, kErrGemmTimeout);
       sm.abort = 1;
@@ -417,7 +466,15 @@ static int launch(const GemmArgs &p, cudaStream_t s) {
     return Q3_ERR_CUDA;
   }
   TcArgs a{p, p.K / p.group, p.group / 128};
-  dim3 grid(p.N / (128 * C::TILES), (p.M + NTOK - 1) / NTOK);
+  const int ntiles = (p.N / (128 * C::TILES)) * ((p.M + NTOK - 1) / NTOK);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  dim3 grid(ntiles < sms ? ntiles : sms);       // persistent: one CTA per SM
   q3h::timer_begin(q3h::TIMER_GEMM, s);
   k_gemm_tc<NTOK, MODE><<<grid, THREADS, smem, s>>>(ta, ta2, tb, a);
   const int st = q3h::launch_status();
@@ -454,17 +511,4 @@ int gemm_tc(const GemmArgs &p, cudaStream_t s) {
   return Q3_ERR_SHAPE;
 }
 
-}  // namespace q3
-
-// ===========================================================================
-// Split-K partials for small token counts (decode): one CTA per (128-row
-// weight tile, K-group).  It writes the group's dequantised partial
-//     part[a][g][m][n] = (f32(int32(A_g . W_g)[m][n]) * w_scale[n]) * a_scale[m][g]
-// (the reference's per-group product, ref_qwen3.py:154-156) to a scratch
-// buffer; the reduce kernels (q3_decode_fused.cu) add the groups in order from
-// 0 and apply the epilogue.  Up to three weight matrices share one launch
-// (Q/K/V): row tiles [0, t1) use map 0, [t1, t2) map 1, the rest map 2; with
-// NACC = 2 (gate/up) maps 0 and 1 are read for the same rows.
-// ===========================================================================
-namespace q3 {
 }  // namespace q3
