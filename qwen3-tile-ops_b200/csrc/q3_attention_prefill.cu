@@ -11,17 +11,18 @@
 //
 // CTA = 128 query rows (positions r0..r0+127) of one q head of one sequence;
 // the heaviest row tiles are scheduled first.  Warp roles:
-//   warps 0-7  the rows: warp w owns rows 32 (w % 4) + lane (its TMEM lane
-//              quadrant) and half hf = w / 4 of every block's 32 keys and of the
-//              128 value columns.  The two halves of a row exchange their block
-//              max, tree sums and absmax through shared memory (the reference's
-//              32-key trees split exactly at their top level), so each half
-//              computes corr / pmax itself and runs the res recurrence for its
-//              64 columns in registers.
-//   warp 8     tcgen05 issuer: S_j = Q (M = 128 rows, K = 128) x K_j (N = 32
+//   warps 0-15 the rows: warp w owns rows 32 (w % 4) + lane (its TMEM lane
+//              quadrant) and part pt = w / 4 of every block's 32 keys (8 keys)
+//              and of the 128 value columns (32).  The four parts of a row
+//              exchange their block max, tree sums and absmax through shared
+//              memory (the reference's 32-key trees split exactly at their two
+//              top levels: (s0 + s1) + (s2 + s3)), so each part computes corr /
+//              pmax itself and runs the res recurrence for its 32 columns in
+//              registers.
+//   warp 16    tcgen05 issuer: S_j = Q (M = 128 rows, K = 128) x K_j (N = 32
 //              keys) into one of two TMEM slots, then P.V of block j-1 =
 //              PQ_{j-1} (M = 128, K = 32) x V_{j-1} read MN-major (N = 128).
-//   warp 9     producer: Q once, then per block the K and V page tiles by TMA
+//   warp 17    producer: Q once, then per block the K and V page tiles by TMA
 //              (128-byte swizzle) into a ring of stages, and their scales.
 // The rows overlap block j's softmax with block j-1's P.V on the tensor core.
 // All int32 products are exact; every wait is bounded (about one second), a
@@ -52,9 +53,11 @@ namespace pa {
 using namespace tcx;
 
 constexpr int ROWS = 128;
-constexpr int CW = 8;                      // row warps
-constexpr int MMA_WARP = 8, PRODUCER = 9;
-constexpr int THREADS = 10 * 32;
+constexpr int KP = 4;                      // parts of a block (keys) / of the value columns
+constexpr int CW = 4 * KP;                 // row warps
+constexpr int KPK = 32 / KP, KPC = 128 / KP;   // keys / value columns per part
+constexpr int MMA_WARP = CW, PRODUCER = CW + 1;
+constexpr int THREADS = (CW + 2) * 32;
 constexpr int NST = 4;                     // K/V stages
 constexpr int TMEM_COLS = 256;             // S slots at 0 and 32, P.V at 64..191
 constexpr unsigned kErrWait = 1u << 18;
@@ -68,9 +71,9 @@ struct Smem {
   alignas(1024) int8_t v[NST][32 * 128];
   alignas(1024) int8_t pq[2][2 * ROWS * 16];         // [key half][16 row groups][8 rows][16 B]
   float ks[NST][32], vs[NST][32];
-  float xmax[2][2][ROWS];                            // [block parity][half][row]
-  float xsum[2][2][ROWS], xam[2][2][ROWS];
-  float xout[2][ROWS];
+  float xmax[2][KP][ROWS];                           // [block parity][part][row]
+  float xsum[2][KP][ROWS], xam[2][KP][ROWS];
+  float xout[KP][ROWS];
   unsigned long long q_full, kv_full[NST], kv_empty[NST];
   unsigned long long s_full[2], s_free[2], p_full[2], o_full, o_free, final_done;
   uint32_t tmem_base;
@@ -86,16 +89,20 @@ __device__ __forceinline__ bool wait_or_abort(unsigned long long *b, uint32_t pa
   *reinterpret_cast<volatile int *>(abort) = 1;
   return false;
 }
-// adjacent-pair tree over 16 values (levels of the reference's 32-value tree)
-__device__ __forceinline__ float tree16_sum(const float (&v)[16]) {
-  float t[8];
+// adjacent-pair tree over 8 values (the lower levels of the reference's 32-value tree)
+__device__ __forceinline__ float tree8_sum(const float (&v)[8]) {
+  float t[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) t[i] = __fadd_rn(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) t[i] = __fadd_rn(t[2 * i], t[2 * i + 1]);
+  for (int i = 0; i < 4; ++i) t[i] = __fadd_rn(v[2 * i], v[2 * i + 1]);
 #pragma unroll
   for (int i = 0; i < 2; ++i) t[i] = __fadd_rn(t[2 * i], t[2 * i + 1]);
   return __fadd_rn(t[0], t[1]);
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                 "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -198,30 +205,30 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ rows
-    const int qd = warp & 3, hf = warp >> 2;
+    const int qd = warp & 3, pt = warp >> 2;
     const int r = qd * 32 + lane, pos = r0 + r;
     const bool active = pos < p.T;
     const long grow = static_cast<long>(b) * p.T + pos;     // row of q8/o8
     const float qsc = active ? *reinterpret_cast<const float *>(p.qs + grow * p.qs_rb + h * 4) : 0.0f;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     float m = kNegFltMax, den = 0.0f;
-    float res[64];
+    float res[KPC];
 #pragma unroll
-    for (int d = 0; d < 64; ++d) res[d] = 0.0f;
+    for (int d = 0; d < KPC; ++d) res[d] = 0.0f;
     float corr_prev = 1.0f, pmax_prev = 0.0f;
 
     auto pv_update = [&](int jj, float corr, float pm) {   // res recurrence, block jj
       wait_or_abort(&sm.o_full, jj & 1, &sm.abort);
       fence_after();
-      int o[64];
+      int o[KPC];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld16(lane_base + 64 + 64 * hf + 16 * c, *reinterpret_cast<int(*)[16]>(&o[16 * c]));
+      for (int c = 0; c < KPC / 16; ++c)
+        tmem_ld16(lane_base + 64 + KPC * pt + 16 * c, *reinterpret_cast<int(*)[16]>(&o[16 * c]));
       tmem_wait_ld();
       fence_before();
       mbar_arrive(&sm.o_free);
 #pragma unroll
-      for (int d = 0; d < 64; ++d)
+      for (int d = 0; d < KPC; ++d)
         res[d] = __fadd_rn(__fmul_rn(res[d], corr), __fmul_rn(i2f_small(o[d]), pm));
     };
 
@@ -229,55 +236,64 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int st = j % NST, slot = j & 1;
       wait_or_abort(&sm.s_full[slot], (j >> 1) & 1, &sm.abort);
       fence_after();
-      int a[16];
-      tmem_ld16(lane_base + 32 * slot + 16 * hf, a);
+      int a[KPK];
+      tmem_ld8(lane_base + 32 * slot + KPK * pt, a);
       tmem_wait_ld();
       fence_before();
       mbar_arrive(&sm.s_free[slot]);
       wait_or_abort(&sm.kv_full[st], (j / NST) & 1, &sm.abort);   // the block's scales
-      float s[16];
+      float s[KPK];
       float bm = kNegInf;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int key = 32 * j + 16 * hf + i;
+      for (int i = 0; i < KPK; ++i) {
+        const int key = 32 * j + KPK * pt + i;
         s[i] = (key <= pos)
-                   ? __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a[i]), sm.ks[st][16 * hf + i]), qsc), p.qk_scale)
+                   ? __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a[i]), sm.ks[st][KPK * pt + i]), qsc), p.qk_scale)
                    : kNegInf;
         bm = fmaxf(bm, s[i]);
       }
-      sm.xmax[slot][hf][r] = bm;
+      sm.xmax[slot][pt][r] = bm;
       rows_sync();
-      const float mn = fmaxf(m, fmaxf(sm.xmax[slot][0][r], sm.xmax[slot][1][r]));
+      float bmax = sm.xmax[slot][0][r];
+#pragma unroll
+      for (int q = 1; q < KP; ++q) bmax = fmaxf(bmax, sm.xmax[slot][q][r]);
+      const float mn = fmaxf(m, bmax);
       const float corr = exp_ref(__fsub_rn(m, mn));
-      float pv[16];
+      float pv[KPK];
       float am = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) s[i] = exp_ref(__fsub_rn(s[i], mn));   // p
-      const float ps = tree16_sum(s);
+      for (int i = 0; i < KPK; ++i) s[i] = exp_ref(__fsub_rn(s[i], mn));   // p
+      const float ps = tree8_sum(s);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int key = 32 * j + 16 * hf + i;
-        pv[i] = (key <= pos) ? __fmul_rn(s[i], sm.vs[st][16 * hf + i]) : 0.0f;
+      for (int i = 0; i < KPK; ++i) {
+        const int key = 32 * j + KPK * pt + i;
+        pv[i] = (key <= pos) ? __fmul_rn(s[i], sm.vs[st][KPK * pt + i]) : 0.0f;
         am = fmaxf(am, fabsf(pv[i]));
       }
-      sm.xsum[slot][hf][r] = ps;
-      sm.xam[slot][hf][r] = am;
+      sm.xsum[slot][pt][r] = ps;
+      sm.xam[slot][pt][r] = am;
       rows_sync();
-      const float psum = __fadd_rn(sm.xsum[slot][0][r], sm.xsum[slot][1][r]);
-      const float pm = __fmul_rn(fmaxf(sm.xam[slot][0][r], sm.xam[slot][1][r]), kInv127);
+      // the two top levels of the 32-key tree: (s0 + s1) + (s2 + s3)
+      const float psum = __fadd_rn(__fadd_rn(sm.xsum[slot][0][r], sm.xsum[slot][1][r]),
+                                   __fadd_rn(sm.xsum[slot][2][r], sm.xsum[slot][3][r]));
+      float amx = sm.xam[slot][0][r];
+#pragma unroll
+      for (int q = 1; q < KP; ++q) amx = fmaxf(amx, sm.xam[slot][q][r]);
+      const float pm = __fmul_rn(amx, kInv127);
       den = __fadd_rn(__fmul_rn(den, corr), psum);
       m = mn;
-      uint32_t w4[4];
+      uint32_t w2[2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         const uint32_t b0 = static_cast<uint8_t>(quant1(pv[4 * c + 0], pm));
         const uint32_t b1 = static_cast<uint8_t>(quant1(pv[4 * c + 1], pm));
         const uint32_t b2 = static_cast<uint8_t>(quant1(pv[4 * c + 2], pm));
         const uint32_t b3 = static_cast<uint8_t>(quant1(pv[4 * c + 3], pm));
-        w4[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        w2[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
       }
-      *reinterpret_cast<uint4 *>(sm.pq[slot] + hf * (8 * 2 * ROWS) + (r >> 3) * 128 + (r & 7) * 16) =
-          make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      // keys 8 pt .. : 16-key chunk pt / 2, bytes 8 (pt % 2) .. of the row's 16
+      *reinterpret_cast<uint2 *>(sm.pq[slot] + (pt >> 1) * (8 * 2 * ROWS) + (r >> 3) * 128 +
+                                 (r & 7) * 16 + (pt & 1) * 8) = make_uint2(w2[0], w2[1]);
       fence_proxy_async();
       mbar_arrive(&sm.p_full[slot]);
       if (j >= 1) pv_update(j - 1, corr_prev, pmax_prev);
@@ -290,27 +306,30 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float rden = __fdiv_rn(1.0f, den);
     float mx = 0.0f;
 #pragma unroll
-    for (int d = 0; d < 64; ++d) {
+    for (int d = 0; d < KPC; ++d) {
       res[d] = __fmul_rn(res[d], rden);
       mx = fmaxf(mx, fabsf(res[d]));
     }
-    sm.xout[hf][r] = mx;
+    sm.xout[pt][r] = mx;
     rows_sync();
-    const float scale = __fmul_rn(fmaxf(sm.xout[0][r], sm.xout[1][r]), kInv127);
-    if (active) {
-      uint32_t w4[16];
+    float omx = sm.xout[0][r];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+    for (int q = 1; q < KP; ++q) omx = fmaxf(omx, sm.xout[q][r]);
+    const float scale = __fmul_rn(omx, kInv127);
+    if (active) {
+      uint32_t w4[KPC / 4];
+#pragma unroll
+      for (int c = 0; c < KPC / 4; ++c) {
         const uint32_t b0 = static_cast<uint8_t>(quant1(res[4 * c + 0], scale));
         const uint32_t b1 = static_cast<uint8_t>(quant1(res[4 * c + 1], scale));
         const uint32_t b2 = static_cast<uint8_t>(quant1(res[4 * c + 2], scale));
         const uint32_t b3 = static_cast<uint8_t>(quant1(res[4 * c + 3], scale));
         w4[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
       }
-      uint4 *dst = reinterpret_cast<uint4 *>(p.o8 + grow * p.o_rb + h * 128 + 64 * hf);
+      uint4 *dst = reinterpret_cast<uint4 *>(p.o8 + grow * p.o_rb + h * 128 + KPC * pt);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) dst[c] = make_uint4(w4[4 * c], w4[4 * c + 1], w4[4 * c + 2], w4[4 * c + 3]);
-      if (hf == 0) *reinterpret_cast<float *>(p.os + grow * p.os_rb + h * 4) = scale;
+      for (int c = 0; c < KPC / 16; ++c) dst[c] = make_uint4(w4[4 * c], w4[4 * c + 1], w4[4 * c + 2], w4[4 * c + 3]);
+      if (pt == 0) *reinterpret_cast<float *>(p.os + grow * p.os_rb + h * 4) = scale;
     }
   }
 
