@@ -13,8 +13,11 @@ L2 flush is needed between steps.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-N > 1 runs N independent replicas (one process per GPU, torchrun env), the
-path has no data-path collective in this mode: scaling is weak.
+N > 1 (one process per GPU, torchrun env) runs the SAME 64-sequence step
+tensor-parallel over the KV heads (``q3_tp_decode_step_batch``: heads, MLP
+groups and vocabulary split over the ranks, O/down partials exchanged over
+NVLink inside the GEMM kernels): scaling is strong.  The line also carries a
+``replicas`` object: N independent 64-sequence batches, no collective.
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 oracle port of tools/ref_qwen3.py) on the host cores instead.
 """
@@ -57,6 +60,10 @@ def parse():
     ap.add_argument("--prefill-len", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer count (only for small profiling captures; the metric needs 28)")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+                    help="N > 1: tensor parallel over the KV heads (default) or replicas")
+    ap.add_argument("--no-replicas", action="store_true",
+                    help="N > 1 with tp: skip the replicas comparison measurement")
     return ap.parse_args()
 
 
@@ -115,34 +122,27 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def run_ours(args) -> None:
-    import numpy as np
-    import torch
+def measure_decode(args, q3, lib, dev, rank, world, dist, mode: str) -> dict:
+    """Time K graph-replayed decode steps of config 4.
 
-    rank, local_rank, world = dist_env()
-    torch.cuda.set_device(local_rank)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-    sys.path.insert(0, str(REPO))
-    import __graft_entry__ as ge
-    q3 = ge.load_package()
-    from q3b200 import synthetic
+    mode "single": one GPU, the whole model.  "tp": this rank's tensor-parallel
+    share of the SAME 64-sequence batch (same model, ids and KV on every rank;
+    the rank's pool holds its KV heads).  "replicas": an independent 64-sequence
+    batch per rank (own seeds), no collective."""
+    import torch
+    from q3b200 import synthetic, tp
     from q3b200.model import Dims
-    lib = q3._lib.lib()
-    dev = torch.device("cuda", local_rank)
 
     B, K, W = args.seqs, args.steps, args.warmup
     max_seq = ((args.ctx + W + 2 * K + 2 + 31) // 32) * 32
     dims = Dims(layers=args.layers, vocab=VOCAB, max_seq=max_seq)
-    bm = synthetic.random_blob_model(dims, seed=1000 + rank, device=dev)
+    rseed = rank if mode == "replicas" else 0
+    bm = synthetic.random_blob_model(dims, seed=1000 + rseed, device=dev)
     max_pages = max_seq // 32
-    pool = synthetic.KVPoolTensors(args.layers, B * max_pages, 8, device=dev)
-    pool.fill_random(seed=2000 + rank)
-    g = torch.Generator().manual_seed(3000 + rank)
+    shard = tp.shard_of(bm.L, rank, world) if mode == "tp" else tp.shard_of(bm.L, 0, 1)
+    pool = synthetic.KVPoolTensors(args.layers, B * max_pages, shard.kv_heads, device=dev)
+    pool.fill_random(seed=2000 + rseed, head0=shard.kv_head0, total_heads=8)
+    g = torch.Generator().manual_seed(3000 + rseed)
     tables = torch.randperm(B * max_pages, generator=g).reshape(B, max_pages).to(torch.int16)
     tab_d = tables.to(dev)
     ids_d = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32).to(dev)
@@ -152,17 +152,24 @@ def run_ours(args) -> None:
     ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
     cpool = pool.c()
     stream = torch.cuda.Stream(device=dev)
+    comm = tp.TPComm(bm.L, rank, world, B) if mode == "tp" else None
 
     def step(s):
-        q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
-            bm.blob.data_ptr(), C.byref(bm.L), C.byref(cpool), tab_d.data_ptr(), max_pages,
-            ids_d.data_ptr(), pos_d.data_ptr(), B, nxt_d.data_ptr(), ws.data_ptr(), wsb,
-            s.cuda_stream))
+        if comm is not None:
+            comm.decode_step(bm.blob, bm.L, cpool, tab_d, max_pages, ids_d, pos_d, B, nxt_d,
+                             ws, s)
+        else:
+            q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
+                bm.blob.data_ptr(), C.byref(bm.L), C.byref(cpool), tab_d.data_ptr(), max_pages,
+                ids_d.data_ptr(), pos_d.data_ptr(), B, nxt_d.data_ptr(), ws.data_ptr(), wsb,
+                s.cuda_stream))
 
     def advance():
         ids_d.copy_(nxt_d)
         pos_d.add_(1)
 
+    if dist:
+        dist.barrier()
     with torch.cuda.stream(stream):
         for _ in range(W):
             step(stream)
@@ -189,6 +196,8 @@ def run_ours(args) -> None:
         with torch.cuda.graph(graph, stream=stream):
             step(stream)
         launches_per_step = lib.q3_launch_count() - l0
+        if dist:
+            dist.barrier()
         graph.replay()          # one untimed replay (graph upload)
         torch.cuda.synchronize(dev)
     else:
@@ -198,7 +207,7 @@ def run_ours(args) -> None:
         launches_per_step = lib.q3_launch_count() - l0
 
     vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
-    clocks = ClockSampler(vis[local_rank].strip() if local_rank < len(vis) else local_rank)
+    clocks = ClockSampler(vis[dev.index].strip() if dev.index < len(vis) else dev.index)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
@@ -238,6 +247,8 @@ def run_ours(args) -> None:
     ids_h.copy_(ids_d.cpu())
     pos_h.copy_(pos_d.cpu())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
     torch.cuda.synchronize(dev)
     with torch.cuda.stream(stream):
         e0.record(stream)
@@ -255,16 +266,53 @@ def run_ours(args) -> None:
         e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
+    status = lib.q3_device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} after the {mode} decode measurement")
 
     if dist:
-        t = torch.tensor([ms, e2e_ms], device=dev)
+        t = torch.tensor([ms, e2e_ms, att_avg], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
+        ms, e2e_ms, att_avg = float(t[0]), float(t[1]), float(t[2])
     if graph is not None:
         del graph
+    if comm is not None:
+        comm.close()
+    return {"ms": ms, "e2e_ms": e2e_ms, "att_avg": att_avg, "launches": int(launches_per_step),
+            "clocks": ck, "graph": use_graph, "kv_heads": shard.kv_heads, "q_heads": shard.q_heads}
+
+
+def run_ours(args) -> None:
+    import torch
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    sys.path.insert(0, str(REPO))
+    import __graft_entry__ as ge
+    q3 = ge.load_package()
+    lib = q3._lib.lib()
+    dev = torch.device("cuda", local_rank)
+    B, K, W = args.seqs, args.steps, args.warmup
+
+    mode = "single" if world == 1 else args.parallel
+    dec = measure_decode(args, q3, lib, dev, rank, world, dist, mode)
+    replicas = None
+    if mode == "tp" and not args.no_replicas:
+        torch.cuda.empty_cache()
+        rep = measure_decode(args, q3, lib, dev, rank, world, dist, "replicas")
+        replicas = {"value": round(world * B * K / (rep["ms"] * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(rep["ms"] / K, 4), "scaling": "weak",
+                    "parallelism": f"replicas x{world}",
+                    "note": f"data-parallel comparison: an independent {B}-sequence batch "
+                            "per GPU, no collective"}
     prefill = None
     if not args.no_prefill:
-        del pool, ws
         torch.cuda.empty_cache()
         prefill = measure_prefill(args, q3, lib, dev, rank, world, dist)
     if dist:
@@ -275,33 +323,47 @@ def run_ours(args) -> None:
     peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
         REPO / "MEASURED_PEAKS.json").exists() else {}
     peak_gbs = float(peaks.get("hbm_gbs", 6650.0))
-    # one attention launch = one layer for all sequences at the last timed position
-    ctx_last = args.ctx + W + K + 1          # kv_len of the step the attention is timed on
-    att_bytes = B * ctx_last * KV_BYTES_PER_TOKEN_LAYER + B * (2048 + 2048 + 16 * 4 * 2)
-    achieved = att_bytes / (att_avg * 1e-3) / 1e9
-    tokens = world * B * K
+    # one attention launch = one layer for all sequences (this rank's heads) at
+    # the position the eager attention step ran at
+    kvh, qh = dec["kv_heads"], dec["q_heads"]
+    ctx_last = args.ctx + W + K + 1
+    att_bytes = B * ctx_last * kvh * (2 * 128 + 2 * 4) + B * qh * (2 * 128 + 2 * 4)
+    achieved = att_bytes / (dec["att_avg"] * 1e-3) / 1e9
+    tp = mode == "tp"
+    tokens = (1 if tp else world) * B * K
+    ms, e2e_ms = dec["ms"], dec["e2e_ms"]
     line = {
         "metric": METRIC, "value": round(tokens / (ms * 1e-3), 1), "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "dtype": "int8/f32",
         "data": "synthetic (random-init w8a8 weights, seeded int8 KV prefixes)",
         "config": {"workload": "config 4: batched paged greedy decode, 64 seqs x 2048-token "
                                "prefix, 28 layers, vocab 151936 (decode tokens/s)",
-                   "seqs_per_gpu": B, "context": args.ctx, "page_tokens": 32,
-                   "cuda_graph": use_graph, "l2": "inputs larger than L2 (~8.6 GB KV read per step)",
-                   "parallelism": f"replicas x{world}"},
+                   "seqs": B, "context": args.ctx, "page_tokens": 32,
+                   "cuda_graph": dec["graph"],
+                   "l2": "inputs larger than L2 (~8.6 GB KV read per step on one GPU)",
+                   "parallelism": (f"tp{world}: KV heads {kvh}/rank, vocab-parallel argmax, "
+                                   "ordered partial exchange over NVLink") if tp
+                   else ("single GPU" if world == 1 else f"replicas x{world}")},
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * 4 * B, "d2h_bytes_per_step": 4 * B},
-        "gpu_launches": int(launches_per_step) * K,
-        "roofline": {"bound": "hbm", "kernel": "k_attention_decode (decode, one layer, 64 seqs)",
+        "gpu_launches": dec["launches"] * K,
+        "roofline": {"bound": "hbm",
+                     "kernel": f"k_attention_decode (one layer, {B} seqs, {kvh} KV heads)",
                      "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-                     "frac": round(achieved / peak_gbs, 4), "traffic": ATT_TRAFFIC_BYTES,
+                     "frac": round(achieved / peak_gbs, 4),
+                     "traffic": int(ATT_TRAFFIC_BYTES * kvh / 8),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
-                                       "launch at ctx 2048 (profiles/attention_decode_config4.md)",
-                     "avg_launch_ms": round(att_avg, 4), "bytes_per_launch": att_bytes,
+                                       "launch at ctx 2048, 8 KV heads "
+                                       "(profiles/attention_decode_config4.md)"
+                                       + ("" if kvh == 8 else f", scaled by {kvh}/8 heads"),
+                     "avg_launch_ms": round(dec["att_avg"], 4), "bytes_per_launch": att_bytes,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650"},
-        "clocks": ck,
+        "clocks": dec["clocks"],
     }
+    if replicas is not None:
+        line["replicas"] = replicas
     if prefill is not None:
         line["prefill"] = prefill
     if world == 1 and not args.no_cpu_baseline:

@@ -266,6 +266,60 @@ int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv_pool *pool
                      uint32_t n_seqs, uint32_t T, int32_t *next_ids, void *workspace,
                      size_t workspace_bytes, void *stream);
 
+/* ---- tensor-parallel batched decode (extension) ---------------------------
+ * The batched decode step split over `world` GPUs of one node, one process per
+ * GPU.  The reference runs one hart and has no such split; this follows its
+ * arithmetic exactly (src/main_big.cpp:173-262 per layer):
+ *   - Q/K/V, head norm/rope/quant, the KV pages and attention: by KV head (a
+ *     rank owns kv_heads/world KV heads and their 2 Q heads each);
+ *   - gate/up + SwiGLU + quant: by 256-wide quant group;
+ *   - O and down: every rank computes the dequantised partials of its own K
+ *     groups and stores them into every rank's receive buffer over NVLink;
+ *     each rank then adds all groups in group order (group_gemm.h:194-214 /
+ *     ref_qwen3.py:151-157 order), so x stays bit-identical on every rank;
+ *   - lm_head: by vocabulary rows; the (max, first index) pairs of the ranks
+ *     are exchanged and the largest value, then the smallest index, wins.
+ * The rank's pool holds only its own KV heads: row width kv_heads*128 of the
+ * shard.  next_ids comes out identical on every rank and identical to
+ * q3_decode_step_batch on one GPU. */
+typedef struct q3_tp_shard {
+  int32_t rank, world;
+  uint32_t q_head0, q_heads;        /* Q heads [q_head0, q_head0 + q_heads)        */
+  uint32_t kv_head0, kv_heads;      /* KV heads                                    */
+  uint32_t mlp_group0, mlp_groups;  /* 256-wide intermediate groups                */
+  uint32_t vocab0, vocab_rows;      /* lm_head rows, whole 128-row tiles           */
+} q3_tp_shard;
+
+/* Host only.  Q3_ERR_SHAPE unless world divides kv_heads, heads = 2*kv_heads,
+ * and every rank gets at least one MLP group and one 128-row vocabulary tile. */
+int q3_tp_shard_of(const q3_layout *layout, int32_t rank, int32_t world, q3_tp_shard *out);
+
+/* Bytes of the opaque handle q3_tp_comm_create writes (a CUDA IPC handle). */
+size_t q3_tp_handle_bytes(void);
+
+/* Communicator of one rank on the current device: allocates the rank's
+ * exchange region (receive buffers for up to max_seqs <= 64 sequences and the
+ * signal counters) and writes its handle.  The caller gathers every rank's
+ * handle (rank order) by any means and passes them to q3_tp_comm_connect,
+ * which maps the peers' regions.  reset zeroes this rank's counters (all ranks
+ * reset between the same two host barriers, with no step in flight); after a
+ * timed-out wait (device status bit 20) the counters disagree until reset. */
+int q3_tp_comm_create(const q3_layout *layout, int32_t rank, int32_t world,
+                      uint32_t max_seqs, void **comm, void *handle);
+int q3_tp_comm_connect(void *comm, const void *handles);
+int q3_tp_comm_reset(void *comm, void *stream);
+int q3_tp_comm_destroy(void *comm);
+
+/* One decode step of this rank (same arguments as q3_decode_step_batch; the
+ * workspace size is q3_decode_workspace_bytes).  Every rank calls it with the
+ * same ids, pos and tables; the kernels wait for the peers' partials on the
+ * device (bounded, about two seconds). */
+int q3_tp_decode_step_batch(void *comm, void *blob, const q3_layout *layout,
+                            const q3_kv_pool *pool, const uint16_t *tables,
+                            uint32_t max_pages, const int32_t *ids, const int32_t *pos,
+                            uint32_t n_seqs, int32_t *next_ids, void *workspace,
+                            size_t workspace_bytes, void *stream);
+
 /* ---- value ops (include/tile.h exp_/exp2 semantics; tests/guest/value_ops.cpp)
  * out[i] = exp(x[i]) as the path computes it: exp2(f32(x * log2e))
  * (tools/ref_qwen3.py:27-29), or out[i] = exp2(x[i]); both correctly rounded
@@ -279,8 +333,10 @@ int q3_device_check(void); /* Q3_OK on an sm_100 device, else Q3_ERR_ARCH */
 
 /* Device-side error word of the library's kernels (0 = none; bit 1: a page
  * index beyond the pool was skipped; bit 2: a sequence needs more pages than
- * its table holds; bit 16: a bounded wait in a tensor-core GEMM pipeline timed
- * out and the kernel gave up).  Reading synchronises with the device and clears
+ * its table holds; bit 3 and bits 16-19: a bounded wait in a tensor-core GEMM or
+ * attention pipeline timed out and the kernel gave up; bit 20: a
+ * tensor-parallel exchange wait for another rank timed out).  Reading
+ * synchronises with the device and clears
  * the word; -1 if it cannot be read. */
 int q3_device_status(void);
 

@@ -401,6 +401,7 @@ namespace q3 {
 int gemm_device_status_take();
 int dgemm_device_status_take();
 int pattn_device_status_take();
+int tp_device_status_take();
 }
 
 extern "C" int q3_device_status(void) {
@@ -415,5 +416,8 @@ extern "C" int q3_device_status(void) {
   const int pa = q3::pattn_device_status_take();
   if (pa < 0) return -1;
   v |= static_cast<unsigned int>(pa);
+  const int tp = q3::tp_device_status_take();
+  if (tp < 0) return -1;
+  v |= static_cast<unsigned int>(tp);
   return static_cast<int>(v) | g;
 }

@@ -8,6 +8,7 @@
 #include "q3_common.cuh"
 #include "q3_decode_gemm.h"
 #include "q3_gemm.h"
+#include "q3_tp.h"
 
 namespace q3 {
 struct NormQuantArgs {
@@ -42,6 +43,7 @@ struct DecodeWs {
   float *best;           // [B]
   unsigned long long *keys;  // [B]
   float *bsum;           // [B][H/32] tree sums of x^2 per 32-column block
+  int32_t *lidx;         // [B] argmax index within this rank's vocabulary slice
   size_t total;
 };
 
@@ -72,6 +74,7 @@ DecodeWs carve(const q3_layout &L, uint32_t B, char *base) {
   w.best = (float *)take(4 * B);
   w.keys = (unsigned long long *)take(8 * B);
   w.bsum = (float *)take(4 * B * (H / 32));
+  w.lidx = (int32_t *)take(4 * B);
   w.total = off;
   return w;
 }
@@ -279,7 +282,213 @@ int decode_fused(char *bl, const q3_layout &L, const q3_kv_pool *pool, const uin
   return Q3_OK;
 }
 
+// One rank's share of the batched step under tensor parallelism (the shard of
+// q3_tp_shard_of): Q/K/V, the head epilogues and attention for its heads only,
+// O and down as per-group partials stored to every rank (PART GEMM mode) and
+// summed in group order by the reduce kernel, which also adds the residual and
+// runs the next RMSNorm + quant; gate/up for its 256-wide groups; lm_head for
+// its vocabulary rows, then the exchange of the (max, index) keys.
+int tp_decode(const q3::TpComm &c, char *bl, const q3_layout &L, const q3_kv_pool *pool,
+              const uint16_t *tables, uint32_t max_pages, const int32_t *ids, const int32_t *pos,
+              uint32_t B, int32_t *next_ids, const DecodeWs &w, cudaStream_t st) {
+  void *s = st;
+  const int64_t *o = L.off;
+  const q3_tp_shard &sh = c.shard[c.rank];
+  const uint32_t H = L.hidden, HD = L.head_dim, QW = L.heads * HD, I = L.inter, V = L.vocab;
+  const uint32_t QH = sh.q_heads, KVH = sh.kv_heads, QWl = QH * HD, KWl = KVH * HD;
+  const uint32_t Gl = sh.mlp_groups, Il = Gl * 256;
+  const float inv_h = 1.0f / static_cast<float>(H), inv_hd = 1.0f / static_cast<float>(HD);
+  const q3_view x = v2(w.x, B, H, Q3_DT_F32), h = v2(w.h, B, H, Q3_DT_F32);
+  const q3_view h8 = v2(w.h8, B, H, Q3_DT_I8), hs = v2(w.hs, B, H / 256, Q3_DT_F32);
+  const q3_view idv = v2(const_cast<int32_t *>(ids), B, 1, Q3_DT_I32);
+  const q3_view emb = v2(bl + o[Q3_OFF_EMB], V, H, Q3_DT_I8);
+  const q3_view emb_s = v2(bl + o[Q3_OFF_EMB] + (int64_t)V * H, V, 1, Q3_DT_F32);
+  const float *cos_t = reinterpret_cast<const float *>(bl + o[Q3_OFF_COS]);
+  const float *sin_t = reinterpret_cast<const float *>(bl + o[Q3_OFF_SIN]);
+  {
+    const q3_view n1_0 = v2(bl + o[Q3_OFF_N1], H, 1, Q3_DT_F32);
+    Q3_TRY(q3_embedding_rmsnorm_rows(&emb, &emb_s, &idv, &x, &n1_0, &h, inv_h, s));
+    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+  }
+  for (uint32_t Li = 0; Li < L.layers; ++Li) {
+    char *lw = bl + o[Q3_OFF_LQ] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERW_STRIDE];
+    char *ln = bl + o[Q3_OFF_N1] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERN_STRIDE];
+    auto Wp = [&](int key) { return reinterpret_cast<const int8_t *>(lw + (o[key] - o[Q3_OFF_LQ])); };
+    auto Sp = [&](int key) { return reinterpret_cast<const float *>(lw + (o[key] - o[Q3_OFF_LQ])); };
+    const float *nq = reinterpret_cast<const float *>(ln + (o[Q3_OFF_NQ] - o[Q3_OFF_N1]));
+    const float *nk = reinterpret_cast<const float *>(ln + (o[Q3_OFF_NK] - o[Q3_OFF_N1]));
+    const float *n2 = reinterpret_cast<const float *>(ln + (o[Q3_OFF_N2] - o[Q3_OFF_N1]));
+    const float *n_next = Li + 1 < L.layers
+                              ? reinterpret_cast<const float *>(ln + o[Q3_OFF_LAYERN_STRIDE])
+                              : reinterpret_cast<const float *>(bl + o[Q3_OFF_NF]);
+    char *pk = static_cast<char *>(pool->k) + Li * pool->layer_stride;
+    char *pv = static_cast<char *>(pool->v) + Li * pool->layer_stride;
+    char *pks = static_cast<char *>(pool->ks) + Li * pool->scale_layer_stride;
+    char *pvs = static_cast<char *>(pool->vs) + Li * pool->scale_layer_stride;
+
+    // this rank's Q | K | V heads, head norm/rope/quant into q8 and its KV pages
+    {
+      const int8_t *wts[3] = {Wp(Q3_OFF_LQ) + (size_t)sh.q_head0 * HD * H,
+                              Wp(Q3_OFF_LK) + (size_t)sh.kv_head0 * HD * H,
+                              Wp(Q3_OFF_LV) + (size_t)sh.kv_head0 * HD * H};
+      const int rows[3] = {(int)QWl, (int)KWl, (int)KWl};
+      q3::DgemmArgs a{};
+      a.M = (int)B;
+      a.a_scale = reinterpret_cast<const char *>(w.hs);
+      a.as_rb = 4 * (H / 256);
+      a.ws[0] = Sp(Q3_OFF_LQ_SCALE) + sh.q_head0 * HD;
+      a.ws[1] = Sp(Q3_OFF_LK_SCALE) + sh.kv_head0 * HD;
+      a.ws[2] = Sp(Q3_OFF_LV_SCALE) + sh.kv_head0 * HD;
+      a.heads = (int)QH;
+      a.kv_heads = (int)KVH;
+      a.nq = nq;
+      a.nk = nk;
+      a.cos_t = cos_t;
+      a.sin_t = sin_t;
+      a.pos = pos;
+      a.inv_hd = inv_hd;
+      a.q8 = w.q8;
+      a.qs = w.qs;
+      a.pk = pk;
+      a.pv = pv;
+      a.pks = pks;
+      a.pvs = pvs;
+      a.tables = tables;
+      a.max_pages = max_pages;
+      Q3_TRY(q3::dgemm_launch(q3::DG_QKV, 3, wts, rows, w.h8, H, (int)H, 256, a, st));
+    }
+    {
+      q3::DecodeAttnArgs d{};
+      d.q8 = reinterpret_cast<const char *>(w.q8);
+      d.q_rb = QWl;
+      d.qs = reinterpret_cast<const char *>(w.qs);
+      d.qs_rb = 4 * QH;
+      d.o8 = reinterpret_cast<char *>(w.o8);
+      d.o_rb = QWl;
+      d.os = reinterpret_cast<char *>(w.os);
+      d.os_rb = 4 * QH;
+      d.ks = pks;
+      d.vs = pvs;
+      d.table = tables;
+      d.table_stride = max_pages;
+      d.page_bytes = kPT * KWl;
+      d.row_bytes = KWl;
+      d.scale_page_bytes = kPT * 4 * KVH;
+      d.scale_row_bytes = 4 * KVH;
+      d.kv_len = w.kv_len;
+      d.qk_scale = kInvSqrt128;
+      Q3_TRY(q3::attention_decode_launch(d, pk, pv, pool->num_pages, KVH, B, st, true));
+    }
+    auto part_args = [&](int buf, const float *a_scale, long as_rb, const float *wscale,
+                         int slot0) {
+      q3::DgemmArgs a{};
+      a.M = (int)B;
+      a.a_scale = reinterpret_cast<const char *>(a_scale);
+      a.as_rb = as_rb;
+      a.ws[0] = wscale;
+      a.H = (int)H;
+      a.ndst = c.world;
+      a.slot0 = slot0;
+      a.expect = q3::tp_expect(c, buf);
+      for (int q = 0; q < c.world; ++q) {
+        a.dst[q] = reinterpret_cast<float *>(c.peer[q] + (buf == q3::TP_O ? c.off_orecv : c.off_drecv));
+        a.sig[q] = q3::tp_sig(c, q, buf, c.rank);
+        a.inc[q] = q3::dgemm_part_ctas((int)H, (int)(buf == q3::TP_O ? c.shard[q].q_heads
+                                                                      : c.shard[q].mlp_groups));
+      }
+      return a;
+    };
+    auto reduce = [&](int buf, int slots, const float *nw) {
+      q3::TpReduceArgs r{};
+      r.recv = reinterpret_cast<const float *>(c.local + (buf == q3::TP_O ? c.off_orecv : c.off_drecv));
+      r.slots = slots;
+      r.sig = q3::tp_sig(c, c.rank, buf, 0);
+      r.expect = q3::tp_expect(c, buf);
+      r.world = c.world;
+      r.x = w.x;
+      r.w = nw;
+      r.inv = inv_h;
+      r.B = (int)B;
+      r.H = (int)H;
+      r.h8 = w.h8;
+      r.hs = w.hs;
+      return q3::tp_reduce_norm(r, st);
+    };
+    // O: partials of this rank's heads (one 128-wide K group each) -> every rank
+    {
+      const int8_t *wts[1] = {Wp(Q3_OFF_LO) + sh.q_head0 * HD};
+      const int rows[1] = {(int)H};
+      const q3::DgemmArgs a = part_args(q3::TP_O, w.os, 4 * QH, Sp(Q3_OFF_LO_SCALE), (int)sh.q_head0);
+      Q3_TRY(q3::dgemm_launch(q3::DG_PART, 1, wts, rows, w.o8, QWl, (int)QWl, 128, a, st, QW));
+    }
+    Q3_TRY(reduce(q3::TP_O, (int)L.heads, n2));
+    // gate/up for this rank's 256-wide groups -> SwiGLU + quant
+    {
+      const int8_t *wts[2] = {Wp(Q3_OFF_LG) + (size_t)sh.mlp_group0 * 256 * H,
+                              Wp(Q3_OFF_LU) + (size_t)sh.mlp_group0 * 256 * H};
+      const int rows[2] = {(int)Il, (int)Il};
+      q3::DgemmArgs a{};
+      a.M = (int)B;
+      a.a_scale = reinterpret_cast<const char *>(w.hs);
+      a.as_rb = 4 * (H / 256);
+      a.ws[0] = Sp(Q3_OFF_LG_SCALE) + sh.mlp_group0 * 256;
+      a.ws[1] = Sp(Q3_OFF_LU_SCALE) + sh.mlp_group0 * 256;
+      a.s8 = w.s8;
+      a.ss = w.ss;
+      a.I = (int)Il;
+      Q3_TRY(q3::dgemm_launch(q3::DG_SWIGLU, 2, wts, rows, w.h8, H, (int)H, 256, a, st));
+    }
+    // down: partials of this rank's groups -> every rank
+    {
+      const int8_t *wts[1] = {Wp(Q3_OFF_LD) + sh.mlp_group0 * 256};
+      const int rows[1] = {(int)H};
+      const q3::DgemmArgs a =
+          part_args(q3::TP_DOWN, w.ss, 4 * Gl, Sp(Q3_OFF_LD_SCALE), (int)sh.mlp_group0);
+      Q3_TRY(q3::dgemm_launch(q3::DG_PART, 1, wts, rows, w.s8, Il, (int)Il, 256, a, st, I));
+    }
+    Q3_TRY(reduce(q3::TP_DOWN, (int)(I / 256), n_next));
+  }
+  // lm_head over this rank's vocabulary rows, then the key exchange
+  {
+    const q3_view lm = v2(bl + o[Q3_OFF_LM] + (int64_t)sh.vocab0 * H, sh.vocab_rows, H, Q3_DT_I8);
+    const q3_view lm_s = v2(bl + o[Q3_OFF_LM] + (int64_t)V * H + (int64_t)sh.vocab0 * 4,
+                            sh.vocab_rows, 1, Q3_DT_F32);
+    Q3_TRY(q3_gemm_nt_group_argmax(&h8, &hs, &lm, &lm_s, w.best, w.lidx, 256, w.keys, 8 * B, s));
+  }
+  return q3::tp_argmax_exchange(c, w.best, w.lidx, sh.vocab0, (int)B, next_ids, st);
+}
+
 }  // namespace
+
+extern "C" int q3_tp_decode_step_batch(void *comm, void *blob, const q3_layout *layout,
+                                       const q3_kv_pool *pool, const uint16_t *tables,
+                                       uint32_t max_pages, const int32_t *ids, const int32_t *pos,
+                                       uint32_t n_seqs, int32_t *next_ids, void *workspace,
+                                       size_t workspace_bytes, void *stream) {
+  if (!comm || !blob || !layout || !pool || !tables || !ids || !pos || !next_ids || !workspace)
+    return Q3_ERR_NULL;
+  const q3::TpComm &c = *static_cast<const q3::TpComm *>(comm);
+  const q3_layout &L = *layout;
+  if (L.head_dim != 128 || L.hidden != 1024 || L.inter % 256 || L.max_seq % kPT ||
+      L.heads != c.heads || L.inter / 256 != c.mlp_groups || L.hidden != c.hidden)
+    return Q3_ERR_SHAPE;
+  if (n_seqs == 0) return Q3_OK;
+  if (n_seqs > c.max_seqs || n_seqs > 64) return Q3_ERR_CAPACITY;
+  if (workspace_bytes < q3_decode_workspace_bytes(layout, n_seqs)) return Q3_ERR_CAPACITY;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256) return Q3_ERR_ALIGN;
+  if (!pool->k || !pool->v || !pool->ks || !pool->vs || pool->num_pages == 0) return Q3_ERR_NULL;
+  for (int q = 0; q < c.world; ++q)
+    if (!c.peer[q]) return Q3_ERR_NULL;   // not connected
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char *bl = static_cast<char *>(blob);
+  DecodeWs w = carve(L, n_seqs, static_cast<char *>(workspace));
+  k_decode_prep<<<n_seqs, 64, 0, st>>>(pos, reinterpret_cast<const float *>(bl + L.off[Q3_OFF_COS]),
+                                       reinterpret_cast<const float *>(bl + L.off[Q3_OFF_SIN]),
+                                       L.head_dim / 2, w.cos, w.sin, w.kv_len, w.best, next_ids,
+                                       n_seqs);
+  Q3_TRY(q3h::launch_status());
+  return tp_decode(c, bl, L, pool, tables, max_pages, ids, pos, n_seqs, next_ids, w, st);
+}
 
 extern "C" size_t q3_decode_workspace_bytes(const q3_layout *L, uint32_t n_seqs) {
   if (!L) return 0;

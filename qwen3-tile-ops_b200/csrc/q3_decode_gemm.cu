@@ -101,6 +101,12 @@ __device__ __forceinline__ void push_to_peer(uint32_t dst_cluster, uint32_t src_
       : "memory");
 }
 
+// +1 on a counter that another GPU may poll (system scope, release: every write
+// this thread made, or saw through a barrier, is visible before the count)
+__device__ __forceinline__ void sys_signal(unsigned *ctr) {
+  asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+
 template <int MODE, int NACC, int GPC, int GROUP, int TPCL, int GT>
 __global__ void __launch_bounds__(THREADS, 1)
     k_dgemm(const __grid_constant__ CUtensorMap w0, const __grid_constant__ CUtensorMap w1,
@@ -225,6 +231,34 @@ __global__ void __launch_bounds__(THREADS, 1)
       sm.abort = 1;
     }
     __syncwarp();
+  }
+
+  if constexpr (MODE == DG_PART) {
+    // ---------------------------------------------- tensor-parallel partials -> every rank
+    // Token m of this CTA's partial (512 contiguous bytes of features) goes to
+    // row m of slot slot0 + gs of each rank's receive buffer; a CTA whose MMAs
+    // timed out still signals (its data is void, the error bit says so), so no
+    // rank waits on it for long.
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (warp < EPI_WARPS && !sm.abort) {
+      const float *part = reinterpret_cast<const float *>(sm.region);
+      for (int m = warp; m < p.M; m += EPI_WARPS) {
+        const float4 v = reinterpret_cast<const float4 *>(part + static_cast<size_t>(m) * 128)[lane];
+        const size_t off = (static_cast<size_t>(p.slot0 + gs) * p.M + m) * p.H + tile * 128;
+        for (int q = 0; q < p.ndst; ++q) reinterpret_cast<float4 *>(p.dst[q] + off)[lane] = v;
+      }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+      for (int q = 0; q < p.ndst; ++q) sys_signal(p.sig[q]);
+      if (tile == 0 && gs == 0)
+        for (int q = 0; q < p.ndst; ++q) p.expect[q] += static_cast<unsigned>(p.inc[q]);
+    }
+    if (warp == EPI_WARPS) tmem_dealloc<C::TMEM_COLS>(tmem);
+    return;
   }
 
   // ---------------------------------------------- every partial of the cluster is in smem
@@ -413,7 +447,7 @@ static int launch(const CUtensorMap (&wm)[3], const CUtensorMap &am, const Dgemm
   }
   static_assert(GT % GPC == 0 && TPCL * (GT / GPC) <= 8 && NTOK % (TPCL * (GT / GPC)) == 0,
                 "cluster shape");
-  if (p.G != GT || tiles % TPCL) return Q3_ERR_SHAPE;
+  if ((MODE != DG_PART && p.G != GT) || tiles % TPCL) return Q3_ERR_SHAPE;
   static_assert(C::TMEM_RAW <= 256, "TMEM columns");
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(tiles, p.G / GPC);
@@ -423,7 +457,7 @@ static int launch(const CUtensorMap (&wm)[3], const CUtensorMap &am, const Dgemm
   cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = TPCL;
-  at[0].val.clusterDim.y = p.G / GPC;
+  at[0].val.clusterDim.y = MODE == DG_PART ? 1 : p.G / GPC;
   at[0].val.clusterDim.z = 1;
   at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[1].val.programmaticStreamSerializationAllowed = 1;
@@ -447,9 +481,10 @@ static int launch(const CUtensorMap (&wm)[3], const CUtensorMap &am, const Dgemm
 }  // namespace dg
 
 int dgemm_launch(int mode, int nmaps, const int8_t *const *w, const int *rows, const int8_t *a,
-                 long a_rb, int K, int group, const DgemmArgs &args, cudaStream_t s) {
+                 long a_rb, int K, int group, const DgemmArgs &args, cudaStream_t s, long w_rb) {
   DgemmArgs p = args;
-  if (p.M < 1 || p.M > dg::NTOK || K % group || a_rb % 16 ||
+  if (w_rb == 0) w_rb = K;
+  if (p.M < 1 || p.M > dg::NTOK || K % group || a_rb % 16 || w_rb % 16 || w_rb < K ||
       reinterpret_cast<uintptr_t>(a) % 16)
     return Q3_ERR_SHAPE;
   p.K = K;
@@ -459,7 +494,7 @@ int dgemm_launch(int mode, int nmaps, const int8_t *const *w, const int *rows, c
   for (int i = 0; i < 3; ++i) {
     const int j = i < nmaps ? i : nmaps - 1;
     if (rows[j] % 128 || reinterpret_cast<uintptr_t>(w[j]) % 16) return Q3_ERR_SHAPE;
-    if (!tc::make_map(&wm[i], w[j], rows[j], K, K, 128)) return Q3_ERR_CUDA;
+    if (!tc::make_map(&wm[i], w[j], rows[j], K, w_rb, 128)) return Q3_ERR_CUDA;
   }
   if (mode == DG_SWIGLU) {
     tiles = rows[0] / 128;
@@ -479,6 +514,15 @@ int dgemm_launch(int mode, int nmaps, const int8_t *const *w, const int *rows, c
     return dg::launch<DG_RESID, 1, 3, 256, 1, 12>(wm, am, p, tiles, s);
   if (mode == DG_SWIGLU && group == 256 && p.G == 4)
     return dg::launch<DG_SWIGLU, 2, 1, 256, 2, 4>(wm, am, p, tiles, s);
+  if (mode == DG_PART) {
+    if (p.ndst < 1 || p.ndst > kTpMaxRanks || !p.expect || rows[0] != p.H) return Q3_ERR_SHAPE;
+    for (int q = 0; q < p.ndst; ++q) {
+      if (!p.dst[q] || !p.sig[q]) return Q3_ERR_NULL;
+      if (reinterpret_cast<uintptr_t>(p.dst[q]) % 16) return Q3_ERR_ALIGN;
+    }
+    if (group == 128) return dg::launch<DG_PART, 1, 1, 128, 1, 1>(wm, am, p, tiles, s);
+    if (group == 256) return dg::launch<DG_PART, 1, 1, 256, 1, 1>(wm, am, p, tiles, s);
+  }
   return Q3_ERR_SHAPE;
 }
 

@@ -7,7 +7,9 @@
 
 namespace q3 {
 
-enum DgemmMode { DG_QKV = 0, DG_RESID = 1, DG_SWIGLU = 2 };
+enum DgemmMode { DG_QKV = 0, DG_RESID = 1, DG_SWIGLU = 2, DG_PART = 3 };
+
+constexpr int kTpMaxRanks = 8;
 
 struct DgemmArgs {
   int M;                       // rows (sequences), <= 64
@@ -35,14 +37,27 @@ struct DgemmArgs {
   int8_t *s8;                  // [M][I]
   float *ss;                   // [M][I / 256]
   int I;
+  // PART epilogue (tensor-parallel O / down): the dequantised partial of every
+  // K group goes, unsummed, to slot slot0 + g of every rank's receive buffer
+  // [slots][M][H] (peer pointers), after which each CTA adds 1 to its signal
+  // counter at every rank
+  float *dst[kTpMaxRanks];
+  unsigned *sig[kTpMaxRanks];  // per rank: this rank's counter for this buffer
+  unsigned *expect;            // this rank's expected counts [ranks] for this buffer
+  int inc[kTpMaxRanks];        // CTAs each rank's producer launches per use
+  int ndst, slot0;
 };
 
 // mode QKV: nmaps = 3 (Q, K, V weights), group 256; RESID: nmaps = 1, group 128
-// or 256; SWIGLU: nmaps = 2 (gate, up), group 256.  w[i]: [rows[i]][K] int8,
-// row stride K; a: [M][K] int8 (row stride a_rb).  Launched as a programmatic
-// dependent of the kernel before it.
+// or 256; SWIGLU: nmaps = 2 (gate, up), group 256; PART: nmaps = 1, group 128 or
+// 256, any number of groups.  w[i]: [rows[i]][K] int8, row stride w_rb (0: K);
+// a: [M][K] int8 (row stride a_rb).  Launched as a programmatic dependent of
+// the kernel before it.
 int dgemm_launch(int mode, int nmaps, const int8_t *const *w, const int *rows, const int8_t *a,
-                 long a_rb, int K, int group, const DgemmArgs &args, cudaStream_t s);
+                 long a_rb, int K, int group, const DgemmArgs &args, cudaStream_t s,
+                 long w_rb = 0);
+// number of CTAs a PART launch of `rows` output features and `groups` K groups uses
+inline int dgemm_part_ctas(int rows, int groups) { return (rows / 128) * groups; }
 int dgemm_device_status_take();
 
 }  // namespace q3

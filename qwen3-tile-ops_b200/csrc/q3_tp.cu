@@ -1,0 +1,318 @@
+// Tensor-parallel decode: shard plan, communicator (exchange regions mapped
+// between the ranks' processes with CUDA IPC) and the kernels that consume the
+// exchanged data.  The producers are the PART mode of the decode GEMM
+// (q3_decode_gemm.cu), which stores each rank's dequantised K-group partials
+// straight into every rank's receive buffer, and the argmax exchange below.
+//
+// Ordering protocol (no host collective on the data path).  Region of every
+// rank: sig[buf][producer] counters, expect[buf][producer] (local only), the
+// receive buffers.  A producer CTA stores its data to every rank, fences at
+// system scope, and adds 1 (release, system scope) to sig[buf][me] at every
+// rank.  The consumer of `buf` on a rank waits until sig[buf][q] has reached
+// expect[buf][q] for every q (acquire, system scope; bounded at ~2 s), the
+// expected count having been advanced by this rank's own producer kernel of the
+// buffer, which runs just before the consumer in stream order.  A rank can
+// reuse a buffer only after every rank has consumed its previous contents:
+// the next write into `buf` comes after the writer waited for data that each
+// reader produces only after its own consumer of `buf` finished (stream order).
+#include <string.h>
+
+#include <new>
+
+#include "q3_common.cuh"
+#include "q3_tc.cuh"
+#include "q3_tp.h"
+
+namespace q3 {
+
+static __device__ unsigned int g_tp_error = 0;
+constexpr unsigned kErrTpWait = 1u << 20;
+
+int tp_device_status_take() {
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tp_error, sizeof v) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(g_tp_error, &zero, sizeof zero);
+  return static_cast<int>(v);
+}
+
+namespace {
+
+// wait (bounded, ~2 s) until the counter has reached `target` (wrap-safe)
+__device__ bool wait_count(const unsigned *ctr, unsigned target) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (static_cast<int>(v - target) >= 0) return true;
+    if ((it & 63) == 0) {
+      const uint64_t t = tcx::gtime();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > 2000000000ull) return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void sys_signal(unsigned *ctr) {
+  asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+
+// CTA per row, 256 threads, H == 1024: thread t owns features t + 256k, so
+// warp w holds the 32-column blocks 8k + w (lane = column in the block)
+__global__ void __launch_bounds__(256) k_tp_reduce_norm(TpReduceArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float bsum[32];
+  __shared__ float gmax[4][8];
+  const int m = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  if (t < a.world && !wait_count(a.sig + t, a.expect[t])) atomicOr(&g_tp_error, kErrTpWait);
+  __syncthreads();
+  // group-ordered sum of the partials (ref_qwen3.py:151-157), 4 slots in flight
+  const float *base = a.recv + static_cast<size_t>(m) * a.H + t;
+  const size_t sstride = static_cast<size_t>(a.B) * a.H;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int s = 0;
+  for (; s + 4 <= a.slots; s += 4) {
+    float v[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[j][k] = __ldcg(base + (s + j) * sstride + 256 * k);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[k] = __fadd_rn(acc[k], v[j][k]);
+  }
+  for (; s < a.slots; ++s)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] = __fadd_rn(acc[k], __ldcg(base + s * sstride + 256 * k));
+  // x += sum; tree sums of x^2 per 32-column block (rmsnorm.h:34-81)
+  float *xr = a.x + static_cast<size_t>(m) * a.H;
+  float xv[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) xv[k] = __fadd_rn(xr[t + 256 * k], acc[k]);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float b = warp_tree_sum(__fmul_rn(xv[k], xv[k]));
+    if (lane == 0) bsum[8 * k + warp] = b;
+    xr[t + 256 * k] = xv[k];
+  }
+  __syncthreads();
+  float ss = 0.0f;
+  for (int b = 0; b < 32; ++b) ss = __fadd_rn(ss, bsum[b]);
+  ss = __fadd_rn(__fmul_rn(ss, a.inv), kEps);
+  const float r = rsqrt_ref(ss);
+  float hv[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    hv[k] = __fmul_rn(__fmul_rn(xv[k], r), a.w[t + 256 * k]);
+    const float mx = warp_tree_max(fabsf(hv[k]));
+    if (lane == 0) gmax[k][warp] = mx;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {   // quant group k = features [256k, 256k + 256)
+    float mx = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) mx = fmaxf(mx, gmax[k][w]);
+    const float scale = __fmul_rn(mx, kInv127);
+    a.h8[static_cast<size_t>(m) * a.H + t + 256 * k] = static_cast<int8_t>(quant1(hv[k], scale));
+    if (t == 0) a.hs[static_cast<size_t>(m) * (a.H / 256) + k] = scale;
+  }
+}
+
+struct TpArgmaxArgs {
+  const float *best;
+  const int32_t *bidx;
+  uint32_t v0;
+  int B, world, me, max_seqs;
+  unsigned long long *keys_dst[kTpMaxRanks];   // rank q's key buffer [ranks][max_seqs]
+  unsigned *sig_dst[kTpMaxRanks];              // rank q's sig[TP_KEYS][me]
+  const unsigned long long *keys;              // this rank's key buffer
+  const unsigned *sig;                         // this rank's sig[TP_KEYS][.]
+  unsigned *expect;                            // this rank's expect[TP_KEYS][.]
+  int32_t *next_ids;
+};
+
+// (max, first index) of every rank's slice as one key (monotone value << 32 |
+// ~global index): the largest key is the largest value, then the smallest
+// index -- the first maximum of the whole row, as np.argmax picks it
+// (ref_qwen3.py:447-464).  One CTA, thread i = sequence i.
+__global__ void __launch_bounds__(64) k_tp_argmax_exchange(TpArgmaxArgs a) {
+  const int i = threadIdx.x;
+  if (i < a.B) {
+    const float v = __fadd_rn(a.best[i], 0.0f);
+    const unsigned b = __float_as_uint(v);
+    const unsigned key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    const unsigned long long k = (static_cast<unsigned long long>(key) << 32) |
+                                 (0xffffffffu - (static_cast<unsigned>(a.bidx[i]) + a.v0));
+    for (int q = 0; q < a.world; ++q) a.keys_dst[q][a.me * a.max_seqs + i] = k;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (i == 0)
+    for (int q = 0; q < a.world; ++q) sys_signal(a.sig_dst[q]);
+  if (i < a.world) {
+    const unsigned target = a.expect[i] + 1u;
+    if (!wait_count(a.sig + i, target)) atomicOr(&g_tp_error, kErrTpWait);
+    a.expect[i] = target;
+  }
+  __syncthreads();
+  if (i < a.B) {
+    unsigned long long best = 0ull;
+    for (int q = 0; q < a.world; ++q) {
+      const unsigned long long k = __ldcg(a.keys + q * a.max_seqs + i);
+      best = k > best ? k : best;
+    }
+    a.next_ids[i] = static_cast<int32_t>(0xffffffffu - static_cast<unsigned>(best & 0xffffffffu));
+  }
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+int tp_reduce_norm(const TpReduceArgs &a, cudaStream_t s) {
+  if (a.H != 1024 || a.B < 1 || a.slots < 1 || a.world < 1 || a.world > kTpMaxRanks)
+    return Q3_ERR_SHAPE;
+  return q3h::launch_ex(true, k_tp_reduce_norm, dim3(a.B), dim3(256), 0, s, a);
+}
+
+int tp_argmax_exchange(const TpComm &c, const float *best, const int32_t *bidx, uint32_t v0,
+                       int B, int32_t *next_ids, cudaStream_t s) {
+  if (B < 1 || B > 64 || static_cast<uint32_t>(B) > c.max_seqs) return Q3_ERR_SHAPE;
+  TpArgmaxArgs a{};
+  a.best = best;
+  a.bidx = bidx;
+  a.v0 = v0;
+  a.B = B;
+  a.world = c.world;
+  a.me = c.rank;
+  a.max_seqs = static_cast<int>(c.max_seqs);
+  for (int q = 0; q < c.world; ++q) {
+    a.keys_dst[q] = reinterpret_cast<unsigned long long *>(c.peer[q] + c.off_keys);
+    a.sig_dst[q] = tp_sig(c, q, TP_KEYS, c.rank);
+  }
+  a.keys = reinterpret_cast<const unsigned long long *>(c.local + c.off_keys);
+  a.sig = tp_sig(c, c.rank, TP_KEYS, 0);
+  a.expect = tp_expect(c, TP_KEYS);
+  a.next_ids = next_ids;
+  k_tp_argmax_exchange<<<1, 64, 0, s>>>(a);
+  return q3h::launch_status();
+}
+
+}  // namespace q3
+
+using q3::TpComm;
+
+extern "C" int q3_tp_shard_of(const q3_layout *L, int32_t rank, int32_t world, q3_tp_shard *out) {
+  if (!L || !out) return Q3_ERR_NULL;
+  if (world < 1 || world > q3::kTpMaxRanks || rank < 0 || rank >= world) return Q3_ERR_SHAPE;
+  if (L->kv_heads == 0 || L->kv_heads % world || L->heads != 2 * L->kv_heads || L->inter % 256 ||
+      L->vocab % 128)
+    return Q3_ERR_SHAPE;
+  const uint32_t G = L->inter / 256, T = L->vocab / 128, w = static_cast<uint32_t>(world),
+                 r = static_cast<uint32_t>(rank);
+  if (G < w || T < w) return Q3_ERR_SHAPE;
+  q3_tp_shard s{};
+  s.rank = rank;
+  s.world = world;
+  s.kv_heads = L->kv_heads / w;
+  s.kv_head0 = r * s.kv_heads;
+  s.q_heads = 2 * s.kv_heads;
+  s.q_head0 = 2 * s.kv_head0;
+  s.mlp_group0 = r * G / w;
+  s.mlp_groups = (r + 1) * G / w - s.mlp_group0;
+  const uint32_t t0 = r * T / w, t1 = (r + 1) * T / w;
+  s.vocab0 = t0 * 128;
+  s.vocab_rows = (t1 - t0) * 128;
+  *out = s;
+  return Q3_OK;
+}
+
+extern "C" size_t q3_tp_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int q3_tp_comm_create(const q3_layout *L, int32_t rank, int32_t world,
+                                 uint32_t max_seqs, void **comm, void *handle) {
+  if (!L || !comm || !handle) return Q3_ERR_NULL;
+  *comm = nullptr;
+  if (max_seqs < 1 || max_seqs > 64 || L->hidden != 1024 || L->head_dim != 128)
+    return Q3_ERR_SHAPE;
+  TpComm *c = new (std::nothrow) TpComm{};
+  if (!c) return Q3_ERR_CAPACITY;
+  for (int q = 0; q < world && q < q3::kTpMaxRanks; ++q) {
+    const int st = q3_tp_shard_of(L, q, world, &c->shard[q]);
+    if (st != Q3_OK) {
+      delete c;
+      return st;
+    }
+  }
+  if (world < 1 || world > q3::kTpMaxRanks || rank < 0 || rank >= world) {
+    delete c;
+    return Q3_ERR_SHAPE;
+  }
+  c->rank = rank;
+  c->world = world;
+  c->max_seqs = max_seqs;
+  c->hidden = L->hidden;
+  c->heads = L->heads;
+  c->mlp_groups = L->inter / 256;
+  const size_t slot = static_cast<size_t>(max_seqs) * L->hidden * 4;
+  c->off_sig = 0;
+  c->off_expect = 256;
+  c->off_orecv = 512;
+  c->off_drecv = q3::align256(c->off_orecv + c->heads * slot);
+  c->off_keys = q3::align256(c->off_drecv + c->mlp_groups * slot);
+  c->bytes = q3::align256(c->off_keys + static_cast<size_t>(q3::kTpMaxRanks) * max_seqs * 8);
+  cudaError_t e = cudaMalloc(&c->local, c->bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t *>(handle), c->local);
+  if (e != cudaSuccess) {
+    if (c->local) cudaFree(c->local);
+    delete c;
+    q3h::set_cuda_error(e);
+    return Q3_ERR_CUDA;
+  }
+  c->peer[rank] = c->local;
+  *comm = c;
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_comm_connect(void *comm, const void *handles) {
+  if (!comm || !handles) return Q3_ERR_NULL;
+  TpComm *c = static_cast<TpComm *>(comm);
+  const cudaIpcMemHandle_t *h = static_cast<const cudaIpcMemHandle_t *>(handles);
+  for (int q = 0; q < c->world; ++q) {
+    if (q == c->rank || c->opened[q]) continue;
+    void *p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h[q], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      q3h::set_cuda_error(e);
+      return Q3_ERR_CUDA;
+    }
+    c->peer[q] = static_cast<char *>(p);
+    c->opened[q] = true;
+  }
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_comm_reset(void *comm, void *stream) {
+  if (!comm) return Q3_ERR_NULL;
+  TpComm *c = static_cast<TpComm *>(comm);
+  const cudaError_t e = cudaMemsetAsync(c->local, 0, c->off_orecv, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    q3h::set_cuda_error(e);
+    return Q3_ERR_CUDA;
+  }
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_comm_destroy(void *comm) {
+  if (!comm) return Q3_OK;
+  TpComm *c = static_cast<TpComm *>(comm);
+  for (int q = 0; q < c->world; ++q)
+    if (c->opened[q]) cudaIpcCloseMemHandle(c->peer[q]);
+  if (c->local) cudaFree(c->local);
+  delete c;
+  return Q3_OK;
+}

@@ -1,0 +1,59 @@
+// Tensor-parallel decode across the GPUs of one node (q3_tp.cu): the shard of
+// the model each rank owns, the exchange region every rank maps from every
+// other rank (CUDA IPC over NVLink), and the kernels that consume it.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "q3_decode_gemm.h"
+#include "q3_ops.h"
+
+namespace q3 {
+
+// exchange buffers of the region
+enum TpBuf { TP_O = 0, TP_DOWN = 1, TP_KEYS = 2, TP_NBUF = 3 };
+
+struct TpComm {
+  int rank, world;
+  uint32_t max_seqs, hidden, heads, mlp_groups;
+  char *local;                    // this rank's region (cudaMalloc)
+  char *peer[kTpMaxRanks];        // every rank's region as mapped here (peer[rank] = local)
+  bool opened[kTpMaxRanks];       // peer[q] came from cudaIpcOpenMemHandle
+  size_t bytes;
+  size_t off_sig, off_expect, off_orecv, off_drecv, off_keys;
+  q3_tp_shard shard[kTpMaxRanks];
+};
+
+// per-buffer counters of a region: sig[buf][producer rank], expect[buf][producer rank]
+inline unsigned *tp_sig(const TpComm &c, int q, int buf, int producer) {
+  return reinterpret_cast<unsigned *>(c.peer[q] + c.off_sig) + buf * kTpMaxRanks + producer;
+}
+inline unsigned *tp_expect(const TpComm &c, int buf) {
+  return reinterpret_cast<unsigned *>(c.local + c.off_expect) + buf * kTpMaxRanks;
+}
+
+// x += (((0 + p_0) + p_1) + ... + p_{slots-1}) row by row once every rank's
+// producer has signalled, then RMSNorm(w) + per-256 quant of x -> h8/hs
+struct TpReduceArgs {
+  const float *recv;              // [slots][B][H] this rank's receive buffer
+  int slots;
+  const unsigned *sig;            // this rank's counters of the buffer [ranks]
+  const unsigned *expect;         // [ranks]
+  int world;
+  float *x;                       // [B][H]
+  const float *w;                 // [H]
+  float inv;
+  int B, H;
+  int8_t *h8;                     // [B][H]
+  float *hs;                      // [B][H/256]
+};
+int tp_reduce_norm(const TpReduceArgs &a, cudaStream_t s);
+
+// every rank's (best, first index) of its vocabulary slice -> the greedy id
+int tp_argmax_exchange(const TpComm &c, const float *best, const int32_t *bidx, uint32_t v0,
+                       int B, int32_t *next_ids, cudaStream_t s);
+
+int tp_device_status_take();
+
+}  // namespace q3

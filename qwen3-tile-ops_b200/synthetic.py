@@ -79,16 +79,27 @@ class KVPoolTensors:
         self.ks = torch.zeros((layers, pages, 32, kv_heads), dtype=torch.float32, device=device)
         self.vs = torch.zeros_like(self.ks)
 
-    def fill_random(self, seed: int = 1) -> None:
-        """Seeded int8 K/V uniform in [-127, 127] and scales U[1e-3, 1e-2]."""
+    def fill_random(self, seed: int = 1, head0: int = 0, total_heads: int | None = None) -> None:
+        """Seeded int8 K/V uniform in [-127, 127] and scales U[1e-3, 1e-2].
+
+        With ``total_heads``, this pool holds KV heads ``head0 ..`` of a pool of
+        ``total_heads`` heads filled with the same seed (a tensor-parallel
+        rank's share): the values are drawn at full width and sliced."""
+        total = total_heads or self.kv_heads
+        c0, c1 = head0 * 128, (head0 + self.kv_heads) * 128
         g = torch.Generator(device=self.k.device)
         g.manual_seed(seed)
         for t in (self.k, self.v):
             for layer in t:              # per layer: bounded temporary memory
-                layer.copy_(torch.randint(-127, 128, layer.shape, generator=g, device=t.device,
-                                          dtype=torch.int16).to(torch.int8))
+                full = torch.randint(-127, 128, (self.pages, 32, total * 128), generator=g,
+                                     device=t.device, dtype=torch.int16)
+                layer.copy_(full[..., c0:c1].to(torch.int8))
+                del full
         for t in (self.ks, self.vs):
-            t.uniform_(1e-3, 1e-2, generator=g)
+            full = torch.empty((self.layers, self.pages, 32, total), device=t.device)
+            full.uniform_(1e-3, 1e-2, generator=g)
+            t.copy_(full[..., head0:head0 + self.kv_heads])
+            del full
 
     def c(self):
         from ._lib import KVPool

@@ -112,10 +112,12 @@ def test_config3_full_shape_generate(q3):
 
 
 # ---------------------------------------------------------------- batched decode
-def _decode_case(q3, layers, vocab, lens, seed=0):
+def _decode_case(q3, layers, vocab, lens, seed=0, tp_world1=False):
     """Prefill each sequence on the oracle, load its KV into a shared page
     pool under a shuffled page table, run ONE batched decode step on the GPU
-    and the oracle per sequence; return both."""
+    and the oracle per sequence; return both.  ``tp_world1``: the step runs
+    through the tensor-parallel entry point with a one-rank communicator (the
+    partial-GEMM, ordered-reduce and key-exchange kernels, no peers)."""
     shape = synth.Shape(layers=layers, vocab=vocab, max_seq=(max(lens) + 64 + 31) // 32 * 32)
     w = synth.build_model(shape)
     rng = np.random.default_rng(seed)
@@ -162,19 +164,29 @@ def _decode_case(q3, layers, vocab, lens, seed=0):
     lib = q3._lib.lib()
     wsb = lib.q3_decode_workspace_bytes(C.byref(bm.L), B)
     ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
-    q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
-        bm.blob.data_ptr(), C.byref(bm.L), C.byref(pool), tab.data_ptr(), max_pages,
-        ids_d.data_ptr(), pos_d.data_ptr(), B, nxt.data_ptr(), ws.data_ptr(), wsb,
-        torch.cuda.current_stream().cuda_stream))
-    torch.cuda.synchronize()
+    if tp_world1:
+        from q3b200 import tp
+        comm = tp.TPComm(bm.L, 0, 1, B)
+        comm.decode_step(bm.blob, bm.L, pool, tab, max_pages, ids_d, pos_d, B, nxt, ws,
+                         torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        comm.close()
+    else:
+        q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
+            bm.blob.data_ptr(), C.byref(bm.L), C.byref(pool), tab.data_ptr(), max_pages,
+            ids_d.data_ptr(), pos_d.data_ptr(), B, nxt.data_ptr(), ws.data_ptr(), wsb,
+            torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+    assert lib.q3_device_status() == 0
     return (nxt.cpu().numpy(), want_ids, {k: v.cpu().numpy() for k, v in d.items()}, tables,
             want_kv)
 
 
+@pytest.mark.parametrize("tp_world1", [False, True], ids=["single", "tp1"])
 @pytest.mark.parametrize("layers,vocab,lens", [(1, 1024, [5, 40, 64, 33]),
                                                (2, 4096, [100, 1, 31, 32, 250])])
-def test_decode_step_batch(q3, layers, vocab, lens):
-    got, want, pool, tables, kvs = _decode_case(q3, layers, vocab, lens)
+def test_decode_step_batch(q3, layers, vocab, lens, tp_world1):
+    got, want, pool, tables, kvs = _decode_case(q3, layers, vocab, lens, tp_world1=tp_world1)
     assert list(got) == want
     for s, n in enumerate(lens):          # the new K/V row of every layer
         p, sl = tables[s, n // 32], n % 32

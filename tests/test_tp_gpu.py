@@ -1,0 +1,146 @@
+"""Tensor-parallel batched decode on 2+ GPUs against the single-GPU step.
+
+Each rank is its own process on its own GPU (spawned; ``gloo`` carries only
+the communicators' IPC handles).  Every rank builds the same random model and
+its share of the same seeded KV pool (its KV heads), runs several greedy
+decode steps through ``q3_tp_decode_step_batch``, and records the ids and the
+residual stream; rank 0 then replays the steps with ``q3_decode_step_batch``
+on the whole pool (itself checked against the oracle in test_model_gpu.py).
+Ids, residual stream and the new K/V rows must be bit-identical.
+
+Skipped on boxes with fewer GPUs than ranks: ranks whose kernels wait on each
+other are never run as several processes on one GPU.
+"""
+
+from __future__ import annotations
+
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+B, CTX, STEPS = 48, 300, 4
+
+
+def _run_rank(rank, world, port, out_dir, layers):
+    import ctypes as C
+    import datetime
+    import os
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(repo))
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    comm = None
+    try:
+        import __graft_entry__ as ge
+        q3 = ge.load_package()
+        from q3b200 import synthetic, tp
+        from q3b200.model import Dims
+        lib = q3._lib.lib()
+        dev = torch.device("cuda", rank)
+        max_seq = ((CTX + STEPS + 31) // 32) * 32
+        dims = Dims(layers=layers, vocab=151936, max_seq=max_seq)
+        bm = synthetic.random_blob_model(dims, seed=21, device=dev)
+        sh = tp.shard_of(bm.L, rank, world)
+        max_pages = max_seq // 32
+        pool = synthetic.KVPoolTensors(layers, B * max_pages, sh.kv_heads, device=dev)
+        pool.fill_random(seed=22, head0=sh.kv_head0, total_heads=8)
+        g = torch.Generator().manual_seed(23)
+        tables = torch.randperm(B * max_pages, generator=g).reshape(B, max_pages).to(torch.int16)
+        tab = tables.to(dev)
+        ids0 = torch.randint(0, 151936, (B,), generator=g, dtype=torch.int32)
+        lens = torch.randint(CTX - 200, CTX, (B,), generator=g, dtype=torch.int32)
+        wsb = lib.q3_decode_workspace_bytes(C.byref(bm.L), B)
+        stream = torch.cuda.Stream(device=dev)
+
+        def run(step_fn, cpool):
+            ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+            ids, pos = ids0.to(dev), lens.to(dev)
+            nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+            out = []
+            for _ in range(STEPS):
+                with torch.cuda.stream(stream):
+                    step_fn(cpool, ids, pos, nxt, ws)
+                torch.cuda.synchronize(dev)
+                out.append(nxt.cpu().numpy().copy())
+                ids.copy_(nxt)
+                pos.add_(1)
+            x = ws[:B * 1024 * 4].cpu().numpy().view(np.float32).reshape(B, 1024).copy()
+            return np.stack(out), x
+
+        comm = tp.TPComm(bm.L, rank, world, B)
+
+        def tp_step(cpool, ids, pos, nxt, ws):
+            comm.decode_step(bm.blob, bm.L, cpool, tab, max_pages, ids, pos, B, nxt, ws, stream)
+
+        dist.barrier()
+        got_ids, got_x = run(tp_step, pool.c())
+        status = lib.q3_device_status()
+        # the new K/V rows of this rank's heads, every layer
+        kv_rows = []
+        for s in range(B):
+            for t in range(int(lens[s]), int(lens[s]) + STEPS):
+                p = int(tables[s, t // 32]) & 0xFFFF
+                kv_rows.append(pool.k[:, p, t % 32].cpu().numpy())
+                kv_rows.append(pool.v[:, p, t % 32].cpu().numpy())
+        res = {"ids": got_ids, "x": got_x, "status": np.asarray(status),
+               "kv": np.stack(kv_rows)}
+        dist.barrier()
+        comm.close()
+        comm = None
+        if rank == 0:
+            del pool
+            full = synthetic.KVPoolTensors(layers, B * max_pages, 8, device=dev)
+            full.fill_random(seed=22)
+
+            def one_gpu(cpool, ids, pos, nxt, ws):
+                q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
+                    bm.blob.data_ptr(), C.byref(bm.L), C.byref(cpool), tab.data_ptr(), max_pages,
+                    ids.data_ptr(), pos.data_ptr(), B, nxt.data_ptr(), ws.data_ptr(), wsb,
+                    stream.cuda_stream))
+
+            ref_ids, ref_x = run(one_gpu, full.c())
+            ref_kv = []
+            for s in range(B):
+                for t in range(int(lens[s]), int(lens[s]) + STEPS):
+                    p = int(tables[s, t // 32]) & 0xFFFF
+                    ref_kv.append(full.k[:, p, t % 32].cpu().numpy())
+                    ref_kv.append(full.v[:, p, t % 32].cpu().numpy())
+            res.update(ref_ids=ref_ids, ref_x=ref_x, ref_kv=np.stack(ref_kv))
+        np.savez(Path(out_dir) / f"rank{rank}.npz", **res)
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_decode_matches_single_gpu(q3, tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    layers = 3
+    mp.start_processes(_run_rank, args=(world, port, str(tmp_path), layers), nprocs=world,
+                       join=True, start_method="spawn")
+    r0 = np.load(tmp_path / "rank0.npz")
+    ref_ids, ref_x, ref_kv = r0["ref_ids"], r0["ref_x"], r0["ref_kv"]
+    kvh = 8 // world
+    for r in range(world):
+        d = np.load(tmp_path / f"rank{r}.npz")
+        assert int(d["status"]) == 0, f"rank {r}: device status {int(d['status'])}"
+        np.testing.assert_array_equal(d["ids"], ref_ids)
+        np.testing.assert_array_equal(d["x"].view(np.uint32), ref_x.view(np.uint32))
+        np.testing.assert_array_equal(d["kv"], ref_kv[..., r * kvh * 128:(r + 1) * kvh * 128])
