@@ -60,8 +60,9 @@ def parse():
     ap.add_argument("--prefill-len", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer count (only for small profiling captures; the metric needs 28)")
-    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
-                    help="N > 1: tensor parallel over the KV heads (default) or replicas")
+    ap.add_argument("--parallel", default=None, choices=["tp", "replicas"],
+                    help="N > 1: tensor parallel over the KV heads (default) or replicas; "
+                         "'tp' at N = 1 runs the tensor-parallel kernels with one rank")
     ap.add_argument("--no-replicas", action="store_true",
                     help="N > 1 with tp: skip the replicas comparison measurement")
     return ap.parse_args()
@@ -300,10 +301,12 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local_rank)
     B, K, W = args.seqs, args.steps, args.warmup
 
-    mode = "single" if world == 1 else args.parallel
+    mode = args.parallel or ("single" if world == 1 else "tp")
+    if world == 1 and mode == "replicas":
+        mode = "single"
     dec = measure_decode(args, q3, lib, dev, rank, world, dist, mode)
     replicas = None
-    if mode == "tp" and not args.no_replicas:
+    if mode == "tp" and world > 1 and not args.no_replicas:
         torch.cuda.empty_cache()
         rep = measure_decode(args, q3, lib, dev, rank, world, dist, "replicas")
         replicas = {"value": round(world * B * K / (rep["ms"] * 1e-3), 1), "unit": "tokens/s",

@@ -344,7 +344,8 @@ int q3_device_status(void);
 uint64_t q3_launch_count(void);
 
 /* Kernel timing hook for benchmarks: while attached, the i-th launch of the
- * named kernel family ("attention", "gemm") records cudaEvent_t start[i]
+ * named kernel family ("attention", "gemm", "exchange": the tensor-parallel
+ * reduce and key-exchange kernels) records cudaEvent_t start[i]
  * before it and stop[i] after it on its own stream, for i < capacity.
  * q3_timer_detach() returns how many launches were recorded. */
 int q3_timer_attach(const char *family, void *const *start_events,

@@ -214,7 +214,7 @@ inline int launch_ex(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, 
 }
 
 // Benchmark timing hook (q3_timer_attach): events around launches of a family.
-enum TimerFamily { TIMER_NONE = 0, TIMER_ATTENTION = 1, TIMER_GEMM = 2 };
+enum TimerFamily { TIMER_NONE = 0, TIMER_ATTENTION = 1, TIMER_GEMM = 2, TIMER_EXCHANGE = 3 };
 void timer_begin(int family, cudaStream_t s);
 void timer_end(int family, cudaStream_t s);
 

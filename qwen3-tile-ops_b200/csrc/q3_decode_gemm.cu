@@ -250,7 +250,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int q = 0; q < p.ndst; ++q) reinterpret_cast<float4 *>(p.dst[q] + off)[lane] = v;
       }
     }
-    __threadfence_system();
+    // the barrier orders every thread's stores before thread 0's release at
+    // system scope (release is cumulative), which the consumers acquire
     __syncthreads();
     if (tid == 0) {
       for (int q = 0; q < p.ndst; ++q) sys_signal(p.sig[q]);

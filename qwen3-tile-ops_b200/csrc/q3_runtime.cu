@@ -60,6 +60,7 @@ extern "C" int q3_timer_attach(const char *family, void *const *start_events,
   int fam = q3h::TIMER_NONE;
   if (!strcmp(family, "attention")) fam = q3h::TIMER_ATTENTION;
   else if (!strcmp(family, "gemm")) fam = q3h::TIMER_GEMM;
+  else if (!strcmp(family, "exchange")) fam = q3h::TIMER_EXCHANGE;
   else return Q3_ERR_SHAPE;
   std::lock_guard<std::mutex> lk(g_timer.mu);
   g_timer.family = fam;

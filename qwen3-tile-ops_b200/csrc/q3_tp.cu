@@ -6,9 +6,9 @@
 //
 // Ordering protocol (no host collective on the data path).  Region of every
 // rank: sig[buf][producer] counters, expect[buf][producer] (local only), the
-// receive buffers.  A producer CTA stores its data to every rank, fences at
-// system scope, and adds 1 (release, system scope) to sig[buf][me] at every
-// rank.  The consumer of `buf` on a rank waits until sig[buf][q] has reached
+// receive buffers.  A producer CTA stores its data to every rank, passes a
+// CTA barrier, and one thread adds 1 (release, system scope: cumulative over
+// the stores the barrier ordered before it) to sig[buf][me] at every rank.  The consumer of `buf` on a rank waits until sig[buf][q] has reached
 // expect[buf][q] for every q (acquire, system scope; bounded at ~2 s), the
 // expected count having been advanced by this rank's own producer kernel of the
 // buffer, which runs just before the consumer in stream order.  A rank can
@@ -56,68 +56,49 @@ __device__ __forceinline__ void sys_signal(unsigned *ctr) {
   asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
 }
 
-// CTA per row, 256 threads, H == 1024: thread t owns features t + 256k, so
-// warp w holds the 32-column blocks 8k + w (lane = column in the block)
-__global__ void __launch_bounds__(256) k_tp_reduce_norm(TpReduceArgs a) {
+// CTA per row, 1024 threads, H == 1024: thread t owns feature t, so warp w is
+// the 32-column block w (lane = column in the block) and warps 8g..8g+7 the
+// quant group g; all the partials of a thread are loaded before the first add
+__global__ void __launch_bounds__(1024) k_tp_reduce_norm(TpReduceArgs a) {
   pdl_trigger();
   pdl_wait();
   __shared__ float bsum[32];
-  __shared__ float gmax[4][8];
+  __shared__ float gmax[32];
   const int m = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
   if (t < a.world && !wait_count(a.sig + t, a.expect[t])) atomicOr(&g_tp_error, kErrTpWait);
   __syncthreads();
-  // group-ordered sum of the partials (ref_qwen3.py:151-157), 4 slots in flight
+  // group-ordered sum of the partials (ref_qwen3.py:151-157)
   const float *base = a.recv + static_cast<size_t>(m) * a.H + t;
   const size_t sstride = static_cast<size_t>(a.B) * a.H;
-  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  int s = 0;
-  for (; s + 4 <= a.slots; s += 4) {
-    float v[4][4];
+  float v[kTpMaxSlots];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+  for (int s = 0; s < kTpMaxSlots; ++s) v[s] = s < a.slots ? __ldcg(base + s * sstride) : 0.0f;
+  float acc = 0.0f;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) v[j][k] = __ldcg(base + (s + j) * sstride + 256 * k);
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) acc[k] = __fadd_rn(acc[k], v[j][k]);
-  }
-  for (; s < a.slots; ++s)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc[k] = __fadd_rn(acc[k], __ldcg(base + s * sstride + 256 * k));
-  // x += sum; tree sums of x^2 per 32-column block (rmsnorm.h:34-81)
+  for (int s = 0; s < kTpMaxSlots; ++s)
+    if (s < a.slots) acc = __fadd_rn(acc, v[s]);
+  // x += sum; tree sum of x^2 over this warp's 32-column block (rmsnorm.h:34-81)
   float *xr = a.x + static_cast<size_t>(m) * a.H;
-  float xv[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) xv[k] = __fadd_rn(xr[t + 256 * k], acc[k]);
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float b = warp_tree_sum(__fmul_rn(xv[k], xv[k]));
-    if (lane == 0) bsum[8 * k + warp] = b;
-    xr[t + 256 * k] = xv[k];
-  }
+  const float xv = __fadd_rn(xr[t], acc);
+  xr[t] = xv;
+  const float b = warp_tree_sum(__fmul_rn(xv, xv));
+  if (lane == 0) bsum[warp] = b;
   __syncthreads();
   float ss = 0.0f;
-  for (int b = 0; b < 32; ++b) ss = __fadd_rn(ss, bsum[b]);
+  for (int k = 0; k < 32; ++k) ss = __fadd_rn(ss, bsum[k]);   // block order
   ss = __fadd_rn(__fmul_rn(ss, a.inv), kEps);
   const float r = rsqrt_ref(ss);
-  float hv[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    hv[k] = __fmul_rn(__fmul_rn(xv[k], r), a.w[t + 256 * k]);
-    const float mx = warp_tree_max(fabsf(hv[k]));
-    if (lane == 0) gmax[k][warp] = mx;
-  }
+  const float hv = __fmul_rn(__fmul_rn(xv, r), a.w[t]);
+  const float mx = warp_tree_max(fabsf(hv));
+  if (lane == 0) gmax[warp] = mx;
   __syncthreads();
+  const int g = warp >> 3;                // quant group = features [256g, 256g + 256)
+  float gm = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {   // quant group k = features [256k, 256k + 256)
-    float mx = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) mx = fmaxf(mx, gmax[k][w]);
-    const float scale = __fmul_rn(mx, kInv127);
-    a.h8[static_cast<size_t>(m) * a.H + t + 256 * k] = static_cast<int8_t>(quant1(hv[k], scale));
-    if (t == 0) a.hs[static_cast<size_t>(m) * (a.H / 256) + k] = scale;
-  }
+  for (int w = 0; w < 8; ++w) gm = fmaxf(gm, gmax[8 * g + w]);
+  const float scale = __fmul_rn(gm, kInv127);
+  a.h8[static_cast<size_t>(m) * a.H + t] = static_cast<int8_t>(quant1(hv, scale));
+  if ((t & 255) == 0) a.hs[static_cast<size_t>(m) * (a.H / 256) + g] = scale;
 }
 
 struct TpArgmaxArgs {
@@ -147,8 +128,7 @@ __global__ void __launch_bounds__(64) k_tp_argmax_exchange(TpArgmaxArgs a) {
                                  (0xffffffffu - (static_cast<unsigned>(a.bidx[i]) + a.v0));
     for (int q = 0; q < a.world; ++q) a.keys_dst[q][a.me * a.max_seqs + i] = k;
   }
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();   // every store before thread 0's system-scope release
   if (i == 0)
     for (int q = 0; q < a.world; ++q) sys_signal(a.sig_dst[q]);
   if (i < a.world) {
@@ -172,9 +152,13 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 }  // namespace
 
 int tp_reduce_norm(const TpReduceArgs &a, cudaStream_t s) {
-  if (a.H != 1024 || a.B < 1 || a.slots < 1 || a.world < 1 || a.world > kTpMaxRanks)
+  if (a.H != 1024 || a.B < 1 || a.slots < 1 || a.slots > kTpMaxSlots || a.world < 1 ||
+      a.world > kTpMaxRanks)
     return Q3_ERR_SHAPE;
-  return q3h::launch_ex(true, k_tp_reduce_norm, dim3(a.B), dim3(256), 0, s, a);
+  q3h::timer_begin(q3h::TIMER_EXCHANGE, s);
+  const int st = q3h::launch_ex(true, k_tp_reduce_norm, dim3(a.B), dim3(1024), 0, s, a);
+  q3h::timer_end(q3h::TIMER_EXCHANGE, s);
+  return st;
 }
 
 int tp_argmax_exchange(const TpComm &c, const float *best, const int32_t *bidx, uint32_t v0,
@@ -196,8 +180,11 @@ int tp_argmax_exchange(const TpComm &c, const float *best, const int32_t *bidx, 
   a.sig = tp_sig(c, c.rank, TP_KEYS, 0);
   a.expect = tp_expect(c, TP_KEYS);
   a.next_ids = next_ids;
+  q3h::timer_begin(q3h::TIMER_EXCHANGE, s);
   k_tp_argmax_exchange<<<1, 64, 0, s>>>(a);
-  return q3h::launch_status();
+  const int st = q3h::launch_status();
+  q3h::timer_end(q3h::TIMER_EXCHANGE, s);
+  return st;
 }
 
 }  // namespace q3
@@ -235,7 +222,9 @@ extern "C" int q3_tp_comm_create(const q3_layout *L, int32_t rank, int32_t world
                                  uint32_t max_seqs, void **comm, void *handle) {
   if (!L || !comm || !handle) return Q3_ERR_NULL;
   *comm = nullptr;
-  if (max_seqs < 1 || max_seqs > 64 || L->hidden != 1024 || L->head_dim != 128)
+  if (max_seqs < 1 || max_seqs > 64 || L->hidden != 1024 || L->head_dim != 128 ||
+      L->heads > static_cast<uint32_t>(q3::kTpMaxSlots) ||
+      L->inter / 256 > static_cast<uint32_t>(q3::kTpMaxSlots))
     return Q3_ERR_SHAPE;
   TpComm *c = new (std::nothrow) TpComm{};
   if (!c) return Q3_ERR_CAPACITY;

@@ -11,6 +11,8 @@
 
 namespace q3 {
 
+constexpr int kTpMaxSlots = 16;   // K groups of O (heads) and down (I / 256)
+
 // exchange buffers of the region
 enum TpBuf { TP_O = 0, TP_DOWN = 1, TP_KEYS = 2, TP_NBUF = 3 };
 
