@@ -11,12 +11,20 @@
 // A thread of the epilogue owns one feature row, so every per-feature reduction
 // of the reference (head RMSNorm, head/group absmax) is a reduction over lanes.
 //
+// The dequantisation is the epilogue's inner loop (3 rounded float ops per
+// output and group), so it is kept lean: each accumulator starts at the bit
+// pattern of 1.5 * 2^23 (written back by the epilogue after it reads a
+// buffer), so the int32 group sum converts to float with one exact
+// subtraction.  (Packed f32x2 arithmetic is not used: ptxas may contract a
+// packed multiply and add into one fused operation, which changes the bits.)
+//
 // Persistent: one CTA per SM walks the (feature tile, token tile) list; the stage
 // ring and the TMEM buffers run on across tiles, so a tile's epilogue overlaps
-// the next tile's copies and MMAs.  Warps: 0-7 epilogue (two per TMEM lane
-// quadrant: warp w reads lanes 32 (w % 4) .. for half w / 4 of the tokens),
-// 8 TMA producer, 9 MMA issuer and TMEM owner.  Operands arrive by TMA (no multicast) into 128B-swizzled
-// shared memory, 128 K-bytes per stage.  No warp leaves before the others; every
+// the next tile's copies and MMAs.  Warps: 0 .. EPI_WARPS-1 epilogue (EPI_WARPS/4
+// per TMEM lane quadrant: warp w reads lanes 32 (w % 4) .. for one slice of the
+// tokens), then the TMA producer, then the MMA issuer and TMEM owner.  Operands
+// arrive by TMA (no multicast) into 128B-swizzled shared memory, 128 K-bytes
+// per stage.  No warp leaves before the others; every
 // mbarrier wait is bounded (about one second) and a timeout sets bit 16 of the
 // device error word, drains the copies and MMAs in flight and frees TMEM.
 #include <cuda.h>
@@ -43,8 +51,19 @@ int gemm_device_status_take() {
 namespace tc {
 
 constexpr unsigned kErrGemmTimeout = 1u << 16;
-constexpr int EPI_WARPS = 8;   // two per TMEM lane quadrant
+#ifndef Q3_GEMM_EPI_WARPS
+#define Q3_GEMM_EPI_WARPS 16
+#endif
+#ifndef Q3_GEMM_NTOK_BIG
+#define Q3_GEMM_NTOK_BIG 128
+#endif
+constexpr int EPI_WARPS = Q3_GEMM_EPI_WARPS;   // a multiple of 4 (TMEM lane quadrants)
 constexpr int THREADS = (EPI_WARPS + 2) * 32;
+// Accumulators start at the bit pattern of 1.5 * 2^23: the int32 sum of a
+// K-group (|sum| <= 256 * 127 * 127 < 2^22) then reads as the float
+// 12582912 + sum exactly, so f32(sum) is one exact subtraction.
+constexpr uint32_t kAccBias = 0x4B400000u;
+constexpr float kAccBiasF = 12582912.0f;
 
 template <int NTOK, int MODE>
 struct Cfg {
@@ -60,6 +79,7 @@ struct Cfg {
                                    : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int XROWS = (MODE == EPI_SWIGLU) ? 256 : (MODE == EPI_NORMROPE || MODE == EPI_QUANT) ? 128 : 1;
   static constexpr int STAGES = (MODE == EPI_SWIGLU) ? 3 : 4;
+  static constexpr int HT = NTOK / (EPI_WARPS / 4);                    // tokens per epilogue warp
 };
 
 template <int NTOK, int MODE>
@@ -67,8 +87,7 @@ struct __align__(1024) Smem {
   alignas(1024) int8_t stage[Cfg<NTOK, MODE>::STAGES][Cfg<NTOK, MODE>::STAGE_BYTES];
   // epilogue staging [feature][token], rows padded by one word (conflict-free)
   float xchg[Cfg<NTOK, MODE>::XROWS][NTOK + 1];
-  float xchg2[MODE == EPI_SWIGLU ? 128 : 1][MODE == EPI_SWIGLU ? NTOK + 1 : 1];
-  float ascale[NTOK * 16];                 // a_scale[m][g] for this token tile (<= 16 groups)
+  alignas(16) float ascale[16 * NTOK];     // a_scale of this token tile, [group][token]
   unsigned long long full[Cfg<NTOK, MODE>::STAGES], empty[Cfg<NTOK, MODE>::STAGES];
   unsigned long long tfull[Cfg<NTOK, MODE>::NBUF], tempty[Cfg<NTOK, MODE>::NBUF], done;
   uint32_t tmem_base;
@@ -93,6 +112,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               const __grid_constant__ CUtensorMap tmB, const TcArgs args) {
   using C = Cfg<NTOK, MODE>;
   constexpr int STAGES = C::STAGES;
+  constexpr int HT = C::HT;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   Smem<NTOK, MODE> &sm = *reinterpret_cast<Smem<NTOK, MODE> *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -106,6 +126,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   // (feature tile fastest, so the CTAs in flight share weights and activations)
   auto tile_rows = [&](int tile) { return (tile % tiles_x) * 128 * C::TILES; };
   auto tile_m0 = [&](int tile) { return (tile / tiles_x) * NTOK; };
+  // epilogue warp w: TMEM lanes (feature rows) 32 (w % 4) .., tokens c0 .. c0 + HT - 1
+  const int f = (warp & 3) * 32 + lane, c0 = (warp >> 2) * HT;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -120,17 +142,22 @@ __global__ void __launch_bounds__(THREADS, 1)
     sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == EPI_WARPS + 1) {   // TMEM allocation (whole warp)
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     su32(&sm.tmem_base)),
-                 "n"(C::TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
+  if (warp == EPI_WARPS + 1) tmem_alloc<C::TMEM_COLS>(&sm.tmem_base);
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = sm.tmem_base;
+  const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+  if (warp < EPI_WARPS) {                          // every accumulator starts at the bias
+#pragma unroll
+    for (int b = 0; b < C::NBUF * C::NACC; ++b)
+#pragma unroll
+      for (int c = 0; c < HT; c += 16) tmem_st16(lane_addr + b * NTOK + c0 + c, kAccBias);
+    tmem_wait_st();
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
 
   if (warp == EPI_WARPS) {
     // ------------------------------------------------------------ TMA producer
@@ -165,6 +192,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == EPI_WARPS + 1) {
     // ------------------------------------------------------------ MMA issuer
+    // every MMA accumulates: the buffers hold the bias, not zero
     constexpr uint32_t ID = idesc_i8(NTOK);
     bool ok = true;
     int it = 0;
@@ -188,8 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               const uint32_t dt = tmem + (buf * C::NACC + a) * NTOK;
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
-                mma_i8(dt, sdesc_sw128(sa + a * C::A_BYTES + ks * 32), sdesc_sw128(sb + ks * 32), ID,
-                       (box | ks) != 0);
+                mma_i8(dt, sdesc_sw128(sa + a * C::A_BYTES + ks * 32), sdesc_sw128(sb + ks * 32), ID, 1);
             }
             mma_commit(&sm.empty[st]);          // frees the stage when these MMAs finish
           }
@@ -208,13 +235,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // warp w: feature rows 32 (w % 4) + lane of the tile (its TMEM lane
-    // quadrant) and tokens c0 .. c0 + HT - 1 of the token tile, c0 = HT (w / 4)
-    constexpr int HT = NTOK / 2;
     constexpr int TPW = NTOK / EPI_WARPS;          // tokens per warp in the per-token passes
-    const int f = (warp & 3) * 32 + lane, c0 = (warp >> 2) * HT;
     const int etid = threadIdx.x;                  // 0 .. EPI_WARPS*32 - 1
-    const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     float nwv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (MODE == EPI_NORMROPE) {
 #pragma unroll
@@ -227,7 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int mvalid = min(NTOK, p.M - m0);
     epi_sync();                                  // the previous tile's readers are done
     for (int i = etid; i < NTOK * G; i += EPI_WARPS * 32) {   // this tile's activation scales
-      const int m = i / G, g = i % G;
+      const int g = i / NTOK, m = i % NTOK;
       sm.ascale[i] = (m < mvalid)
                          ? *reinterpret_cast<const float *>(p.a_scale + (long)(m0 + m) * p.as_rb + g * 4)
                          : 0.0f;
@@ -235,36 +257,45 @@ __global__ void __launch_bounds__(THREADS, 1)
     epi_sync();
     for (int t = 0; t < C::TILES && ok; ++t) {
       const int n = row0 + t * 128 + f;
-      const float bs = p.b_scale[n];
-      const float bs2 = (C::NACC == 2) ? p.b2_scale[n] : 0.0f;
-      float acc[C::NACC][HT];
+      float bs[C::NACC];
+      bs[0] = p.b_scale[n];
+      if (C::NACC == 2) bs[C::NACC - 1] = p.b2_scale[n];
+      float accf[C::NACC][HT];
 #pragma unroll
       for (int a = 0; a < C::NACC; ++a)
 #pragma unroll
-        for (int m = 0; m < HT; ++m) acc[a][m] = 0.0f;
+        for (int i = 0; i < HT; ++i) accf[a][i] = 0.0f;
       for (int g = 0; g < G; ++g, ++gi) {
         const int buf = gi % C::NBUF;
         if (!mbar_wait(&sm.tfull[buf], (gi / C::NBUF) & 1, &sm.abort)) { ok = false; break; }
         fence_after();
-        int v[C::NACC][HT];
+        const float *asg = sm.ascale + g * NTOK + c0;
 #pragma unroll
-        for (int a = 0; a < C::NACC; ++a)
+        for (int a = 0; a < C::NACC; ++a) {
+          const uint32_t col = lane_addr + (buf * C::NACC + a) * NTOK + c0;
 #pragma unroll
-          for (int c = 0; c < HT; c += 16)
-            tmem_ld16(lane_addr + (buf * C::NACC + a) * NTOK + c0 + c,
-                      *reinterpret_cast<int(*)[16]>(&v[a][c]));
-        tmem_wait_ld();
+          for (int c = 0; c < HT; c += 16) {       // 16 token columns at a time
+            int v[16];
+            tmem_ld16(col + c, v);
+            tmem_wait_ld();
+            tmem_st16(col + c, kAccBias);          // ready for the buffer's next use
+            // acc += (f32(part) * b_scale[n]) * a_scale[m][g]   (ref_qwen3.py:152-157)
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              const float4 as4 = *reinterpret_cast<const float4 *>(asg + c + i);
+              const float asv[4] = {as4.x, as4.y, as4.z, as4.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float x = __fsub_rn(__int_as_float(v[i + j]), kAccBiasF);   // exact
+                accf[a][c + i + j] = __fadd_rn(accf[a][c + i + j], __fmul_rn(__fmul_rn(x, bs[a]), asv[j]));
+              }
+            }
+          }
+        }
+        tmem_wait_st();
         fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.tempty[buf]);
-#pragma unroll
-        for (int a = 0; a < C::NACC; ++a) {
-          const float b = a ? bs2 : bs;
-#pragma unroll
-          for (int i = 0; i < HT; ++i)
-            acc[a][i] = __fadd_rn(acc[a][i],
-                                  __fmul_rn(__fmul_rn(i2f_small(v[a][i]), b), sm.ascale[(c0 + i) * G + g]));
-        }
       }
       if (!ok) break;
 
@@ -282,7 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < HT; ++i) {
           if (c0 + i < mvalid) {
             float *row = reinterpret_cast<float *>(p.out + (long)(m0 + c0 + i) * p.out_rb);
-            row[n] = (MODE == EPI_ADD) ? __fadd_rn(xv[i], acc[0][i]) : acc[0][i];
+            row[n] = (MODE == EPI_ADD) ? __fadd_rn(xv[i], accf[0][i]) : accf[0][i];
           }
         }
       } else if (MODE == EPI_ARGMAX) {
@@ -290,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // packed key (monotone value << 32 | ~index): largest value, then smallest index
 #pragma unroll
         for (int i = 0; i < HT; ++i) {
-          const float v = __fadd_rn(acc[0][i], 0.0f);   // -0 -> +0: equal maxima compare equal
+          const float v = __fadd_rn(accf[0][i], 0.0f);   // -0 -> +0: equal maxima compare equal
           const unsigned b = __float_as_uint(v);
           const unsigned key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
           unsigned long long k =
@@ -311,11 +342,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int i = 0; i < HT; ++i) {
             float sw = 0.0f;
             if (c0 + i < mvalid) {
-              const float gt = acc[0][i];
+              const float gt = accf[0][i];
               float e = exp_ref(__fmul_rn(gt, -1.0f));
               e = __fadd_rn(e, 1.0f);
               e = __fdiv_rn(1.0f, e);
-              sw = __fmul_rn(__fmul_rn(gt, e), acc[1][i]);
+              sw = __fmul_rn(__fmul_rn(gt, e), accf[C::NACC - 1][i]);
             }
             sm.xchg[t * 128 + f][c0 + i] = sw;
           }
@@ -341,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < HT; ++i) sm.xchg[f][c0 + i] = acc[0][i];
+          for (int i = 0; i < HT; ++i) sm.xchg[f][c0 + i] = accf[0][i];
           // rope rows of this warp's tokens, loaded while the others stage
           float cs[TPW][2], sn[TPW][2];
           if (MODE == EPI_NORMROPE) {
@@ -410,10 +441,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   fence_before();
   __syncthreads();
   fence_after();
-  if (warp == EPI_WARPS + 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "n"(C::TMEM_COLS)
-                 : "memory");
+  if (warp == EPI_WARPS + 1) tmem_dealloc<C::TMEM_COLS>(tmem);
 }
 
 // ---------------------------------------------------------------- host side
@@ -501,10 +529,17 @@ bool gemm_tc_eligible(const GemmArgs &p) {
 
 int gemm_tc(const GemmArgs &p, cudaStream_t s) {
   switch (p.mode) {
-    case EPI_STORE: return tc::launch<64, EPI_STORE>(p, s);
-    case EPI_ADD: return tc::launch<64, EPI_ADD>(p, s);
-    case EPI_QUANT: return tc::launch<64, EPI_QUANT>(p, s);
-    case EPI_NORMROPE: return tc::launch<64, EPI_NORMROPE>(p, s);
+    // wider token tiles cut the weight traffic per MAC; SwiGLU stages 256
+    // features per token and keeps 64, and so do the few-row GEMMs
+    case EPI_STORE:
+      return p.M > 64 ? tc::launch<Q3_GEMM_NTOK_BIG, EPI_STORE>(p, s) : tc::launch<64, EPI_STORE>(p, s);
+    case EPI_ADD:
+      return p.M > 64 ? tc::launch<Q3_GEMM_NTOK_BIG, EPI_ADD>(p, s) : tc::launch<64, EPI_ADD>(p, s);
+    case EPI_QUANT:
+      return p.M > 64 ? tc::launch<Q3_GEMM_NTOK_BIG, EPI_QUANT>(p, s) : tc::launch<64, EPI_QUANT>(p, s);
+    case EPI_NORMROPE:
+      return p.M > 64 ? tc::launch<Q3_GEMM_NTOK_BIG, EPI_NORMROPE>(p, s)
+                      : tc::launch<64, EPI_NORMROPE>(p, s);
     case EPI_SWIGLU: return tc::launch<64, EPI_SWIGLU>(p, s);
     case EPI_ARGMAX: return tc::launch<64, EPI_ARGMAX>(p, s);
   }

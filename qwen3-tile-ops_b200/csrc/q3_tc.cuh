@@ -156,6 +156,17 @@ __device__ __forceinline__ void tmem_ld2(uint32_t taddr, int &v0, int &v1) {
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 16 columns of this warp's 32 TMEM lanes set to `v`
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
+          taddr),
+      "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
 }  // namespace tcx
 }  // namespace q3

@@ -164,6 +164,76 @@ def test_lm_head_argmax(ops, m):
         same_bits(gb[r:r + 1], logits[r].max(keepdims=True))
 
 
+# ---- config 2: the per-group GEMM microbench shapes -------
+# M beyond 64 takes the wide token tiles; 700 leaves a ragged last tile.
+@pytest.mark.parametrize("m", [512, 700, 4096])
+@pytest.mark.parametrize("k,n,g", [(1024, 2048, 256), (2048, 1024, 128), (3072, 1024, 256)])
+def test_gemm_config2_store_add(ops, m, k, n, g):
+    rng = np.random.default_rng(m + k + n)
+    a, as_, w, ws = _rand_gemm(rng, m, k, n, g)
+    ref = O.gemm_group(a, as_, w, ws, g)
+    out = torch.zeros(m, n, dtype=torch.float32, device="cuda")
+    ops.gemm_nt_group_store(dev(a), dev(as_), dev(w), dev(ws), out, g)
+    same_bits(host(out), ref)
+    x0 = rng.standard_normal((m, n)).astype(F)
+    x = dev(x0)
+    ops.gemm_nt_group_store(dev(a), dev(as_), dev(w), dev(ws), None, g, add=x)
+    same_bits(host(x), (x0 + ref).astype(F))
+
+
+@pytest.mark.parametrize("m", [512, 700])
+def test_gate_up_swiglu_config2(ops, m):
+    rng = np.random.default_rng(100 + m)
+    a, as_, wg, wgs = _rand_gemm(rng, m, 1024, 3072, 256)
+    wu = rng.integers(-127, 128, (3072, 1024)).astype(np.int8)
+    wus = rng.uniform(1e-3, 1e-2, 3072).astype(F)
+    ref8, refs = O.quant_groups(O.swiglu(O.gemm_group(a, as_, wg, wgs, 256),
+                                         O.gemm_group(a, as_, wu, wus, 256)), 256)
+    s8 = torch.zeros(m, 3072, dtype=torch.int8, device="cuda")
+    ss = torch.zeros(m, 12, dtype=torch.float32, device="cuda")
+    ops.gemm_gate_up_swiglu_quant(dev(a), dev(as_), dev(wg), dev(wgs), dev(wu), dev(wus), s8, ss,
+                                  256)
+    same_bits(host(s8), ref8)
+    same_bits(host(ss), refs)
+
+
+@pytest.mark.parametrize("m", [200, 700])
+def test_gemm_head_epilogues_wide_tiles(ops, m):
+    from oracle import synth
+    rng = np.random.default_rng(200 + m)
+    a, as_, w, ws = _rand_gemm(rng, m, 1024, 2048, 256)
+    y = O.gemm_group(a, as_, w, ws, 256)
+    q8 = torch.zeros(m, 2048, dtype=torch.int8, device="cuda")
+    qs = torch.zeros(m, 16, dtype=torch.float32, device="cuda")
+    ops.gemm_nt_group_store(dev(a), dev(as_), dev(w), dev(ws), None, 256, q8=q8, qs=qs)
+    ref8, refs = O.quant_groups(y, 128)
+    same_bits(host(q8), ref8)
+    same_bits(host(qs), refs)
+    nw = (1 + 0.05 * rng.standard_normal(128)).astype(F)
+    cos, sin = synth.rope_tables(m + 8, 128)
+    cos, sin = cos[8:8 + m], sin[8:8 + m]
+    _, ref8, refs = O.qk_norm_rope_quant(y, nw, cos, sin, 16, 128)
+    ops.gemm_nt_group_store(dev(a), dev(as_), dev(w), dev(ws), None, 256, q8=q8, qs=qs,
+                            nw=dev(nw), cos=dev(np.ascontiguousarray(cos)),
+                            sin=dev(np.ascontiguousarray(sin)), inv_hd=float(F(1) / F(128)))
+    same_bits(host(q8), ref8)
+    same_bits(host(qs), refs)
+
+
+@pytest.mark.parametrize("m", [1, 32])
+def test_lm_head_argmax_config2(ops, m):
+    rng = np.random.default_rng(300 + m)
+    a, as_, w, ws = _rand_gemm(rng, m, 1024, 151936, 256)
+    logits = O.gemm_group(a, as_, w, ws, 256)
+    best = dev(np.full(m, -3.0e38, F))
+    bidx = dev(np.zeros(m, np.int32))
+    ops.gemm_nt_group_argmax(dev(a), dev(as_), dev(w), dev(ws), best, bidx, 256)
+    gb, gi = host(best), host(bidx)
+    for r in range(m):
+        assert gi[r] == int(np.argmax(logits[r]))
+        same_bits(gb[r:r + 1], logits[r].max(keepdims=True))
+
+
 def test_argmax_logits_golden(ops, gold):
     out = dev(np.zeros(1, np.int32))
     ops.argmax_logits(dev(gold["argmax_logits"]), out)
