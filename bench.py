@@ -60,6 +60,12 @@ def parse():
     ap.add_argument("--prefill-len", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer count (only for small profiling captures; the metric needs 28)")
+    ap.add_argument("--gemm-microbench", action="store_true",
+                    help="config 2: time the per-group w8a8 GEMM shapes through the operator API "
+                         "(one JSON line per shape) instead of the decode step")
+    ap.add_argument("--gemm-ms", default="512,4096,65536")
+    ap.add_argument("--gemm-modes", default="qkv,o,gateup,down,lmhead,vquant,qnormrope")
+    ap.add_argument("--gemm-reps", type=int, default=5)
     ap.add_argument("--parallel", default=None, choices=["tp", "replicas"],
                     help="N > 1: tensor parallel over the KV heads (default) or replicas; "
                          "'tp' at N = 1 runs the tensor-parallel kernels with one rank")
@@ -435,6 +441,86 @@ def measure_prefill(args, q3, lib, dev, rank, world, dist) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# config 2: per-group w8a8 GEMM microbench (shapes of BASELINE configs[1])
+# ---------------------------------------------------------------------------
+GEMM_SHAPES = {   # name: (K, N, group, epilogue)
+    "qkv": (1024, 2048, 256, "store"), "o": (2048, 1024, 128, "add"),
+    "gateup": (1024, 3072, 256, "swiglu"), "down": (3072, 1024, 256, "add"),
+    "lmhead": (1024, VOCAB, 256, "argmax"), "vquant": (1024, 1024, 256, "quant"),
+    "qnormrope": (1024, 2048, 256, "normrope"),
+}
+
+
+def run_gemm_microbench(args) -> None:
+    """int8 operands uniform in [-127, 127], f32 scales U[1e-3, 1e-2] (device
+    generator, seed 0); one warm-up call, then the mean of --gemm-reps calls
+    timed with CUDA events.  ops = 2 M N K (x2 for gate+up)."""
+    import torch
+    sys.path.insert(0, str(REPO))
+    import __graft_entry__ as ge
+    q3 = ge.load_package()
+    from q3b200 import ops
+    from q3b200.ops import MatrixView as MV
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def i8(r, c):
+        return torch.randint(-127, 128, (r, c), generator=g, device=dev,
+                             dtype=torch.int16).to(torch.int8)
+
+    def f32(r, c, lo=1e-3, hi=1e-2):
+        return torch.empty((r, c), device=dev).uniform_(lo, hi, generator=g)
+
+    for M in [int(x) for x in args.gemm_ms.split(",")]:
+        for name in args.gemm_modes.split(","):
+            K, N, grp, epi = GEMM_SHAPES[name]
+            if epi == "argmax" and M > 4096:
+                continue
+            A, As, W, Ws = i8(M, K), f32(M, K // grp), i8(N, K), f32(N, 1)
+            av, asv, wv, wsv = MV.of(A), MV.of(As), MV.of(W), MV.of(Ws)
+            if epi in ("store", "add"):
+                out = torch.zeros((M, N), device=dev)
+                fn = lambda: ops.gemm_nt_group_store(av, asv, wv, wsv, None if epi == "add" else MV.of(out),
+                                                     grp, add=MV.of(out) if epi == "add" else None)
+            elif epi in ("quant", "normrope"):
+                q8 = torch.zeros((M, N), dtype=torch.int8, device=dev)
+                qs = torch.zeros((M, N // 128), device=dev)
+                kw = {}
+                if epi == "normrope":
+                    kw = dict(nw=MV.of(torch.ones(128, device=dev)), cos=MV.of(f32(M, 64, -1, 1)),
+                              sin=MV.of(f32(M, 64, -1, 1)), inv_hd=1.0 / 128)
+                fn = lambda: ops.gemm_nt_group_store(av, asv, wv, wsv, None, grp, q8=MV.of(q8),
+                                                     qs=MV.of(qs), **kw)
+            elif epi == "swiglu":
+                W2, W2s = i8(N, K), f32(N, 1)
+                s8 = torch.zeros((M, N), dtype=torch.int8, device=dev)
+                ss = torch.zeros((M, N // 256), device=dev)
+                fn = lambda: ops.gemm_gate_up_swiglu_quant(av, asv, wv, wsv, MV.of(W2), MV.of(W2s),
+                                                           MV.of(s8), MV.of(ss), grp)
+            else:
+                best = torch.full((M,), -3e38, device=dev)
+                bidx = torch.zeros(M, dtype=torch.int32, device=dev)
+                fn = lambda: ops.gemm_nt_group_argmax(av, asv, wv, wsv, best, bidx, grp)
+            fn()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.gemm_reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1) / args.gemm_reps
+            nops = 2.0 * M * N * K * (2 if epi == "swiglu" else 1)
+            print(json.dumps({"gemm": name, "epilogue": epi, "M": M, "K": K, "N": N, "group": grp,
+                              "ms": round(ms, 4), "tops": round(nops / ms / 1e9, 1),
+                              "frac_of_nominal_4500": round(nops / ms / 1e9 / 4500, 4)}), flush=True)
+    st = q3._lib.lib().q3_device_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st}")
+
+
+# ---------------------------------------------------------------------------
 # CPU: the oracle port of tools/ref_qwen3.py on the host cores
 # ---------------------------------------------------------------------------
 def _oracle_setup(ctx: int, seqs: int):
@@ -506,7 +592,9 @@ def run_reference(args) -> None:
 
 if __name__ == "__main__":
     a = parse()
-    if a.impl == "reference":
+    if a.gemm_microbench:
+        run_gemm_microbench(a)
+    elif a.impl == "reference":
         run_reference(a)
     else:
         run_ours(a)
