@@ -251,6 +251,41 @@ def test_quant_rows_heads_golden(ops, gold, group):
     same_bits(host(s), gold[f"quant_s{group}"])
 
 
+def _near_tie_rows(seed=77):
+    """Rows of 256 whose first column fixes the group's absmax A (so the scale
+    is RN(A / 127 ...)) and whose other columns sit within 3 ulps of (k + 1/2)
+    times that scale: the quotients land on or next to the rounding ties of
+    the int8 quantisation.  Magnitudes from subnormal to 1e30, plus a zero row
+    (scale 0: every quotient is NaN -> 0)."""
+    rng = np.random.default_rng(seed)
+    rows = []
+    for a in [1.0, 3.7e-3, 1234.5, 2.0 ** -120, 1e30, 0.5, 2.0 ** -140, 9.99e-8]:
+        a = F(a)
+        scale = F(a * O.INV127)
+        k = rng.integers(-126, 127, 255).astype(np.float64)
+        x = ((k + 0.5) * np.float64(scale)).astype(F)
+        for i, n in enumerate(rng.integers(-3, 4, 255)):
+            for _ in range(abs(int(n))):
+                x[i] = np.nextafter(x[i], F(np.inf) if n > 0 else F(-np.inf))
+        x = np.clip(x, -a, a)
+        rows.append(np.concatenate([[a], x]).astype(F))
+    rows.append(np.zeros(256, F))
+    return np.stack(rows)
+
+
+def test_quant_near_rounding_ties(ops):
+    """The requantisation rounds from a reciprocal and falls back to the exact
+    division near half-integers; it must match RN(x / scale) rounded to even
+    everywhere (ref_qwen3.py:69-76)."""
+    x = _near_tie_rows()
+    ref8, refs = O.quant_groups(x, 256)
+    q = torch.zeros(x.shape, dtype=torch.int8, device="cuda")
+    s = torch.zeros(x.shape[0], 1, dtype=torch.float32, device="cuda")
+    ops.quant_rows_heads(dev(x), q, s, 256)
+    same_bits(host(s), refs)
+    same_bits(host(q), ref8)
+
+
 def test_rmsnorm_golden(ops, gold):
     for xk, wk, ok, inv in (("rms_x", "rms_w", "rms_out", F(1) / F(1024)),
                             ("rmsh_x", "rmsh_w", "rmsh_out", F(1) / F(128))):
