@@ -92,6 +92,8 @@ struct __align__(1024) Smem {
   // epilogue staging [feature][token], rows padded by one word (conflict-free)
   float xchg[Cfg<NTOK, MODE>::XROWS][NTOK + 1];
   alignas(16) float ascale[16 * NTOK];     // a_scale of this token tile, [group][token]
+  // ARGMAX with one token tile: this CTA's best key per token over all its tiles
+  unsigned long long akey[MODE == EPI_ARGMAX ? NTOK : 1];
   unsigned long long full[Cfg<NTOK, MODE>::STAGES], empty[Cfg<NTOK, MODE>::STAGES];
   unsigned long long tfull[Cfg<NTOK, MODE>::NBUF], tempty[Cfg<NTOK, MODE>::NBUF], done;
   uint32_t tmem_base;
@@ -159,6 +161,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = 0; c < HT; c += 16) tmem_st16(lane_addr + b * NTOK + c0 + c, kAccBias);
     tmem_wait_st();
   }
+  // ARGMAX: with a single token tile the keys are reduced in shared memory over
+  // all of this CTA's tiles and written to global memory once (a global atomic
+  // per tile and token would serialise ~1200 updates on each token's key)
+  const bool cta_keys = MODE == EPI_ARGMAX && p.M <= NTOK;
+  if (MODE == EPI_ARGMAX && threadIdx.x < NTOK) sm.akey[threadIdx.x] = 0ull;
   fence_before();
   __syncthreads();
   fence_after();
@@ -248,17 +255,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     bool ok = true;
     int gi = 0;
+    int scales_m0 = -1;                          // token tile whose scales sm.ascale holds
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
     const int row0 = tile_rows(tile), m0 = tile_m0(tile);
     const int mvalid = min(NTOK, p.M - m0);
-    epi_sync();                                  // the previous tile's readers are done
-    for (int i = etid; i < NTOK * G; i += EPI_WARPS * 32) {   // this tile's activation scales
-      const int g = i / NTOK, m = i % NTOK;
-      sm.ascale[i] = (m < mvalid)
-                         ? *reinterpret_cast<const float *>(p.a_scale + (long)(m0 + m) * p.as_rb + g * 4)
-                         : 0.0f;
+    if (m0 != scales_m0) {                       // (uniform: m0 is the CTA's)
+      epi_sync();                                // the previous tile's readers are done
+      for (int i = etid; i < NTOK * G; i += EPI_WARPS * 32) {   // this tile's activation scales
+        const int g = i / NTOK, m = i % NTOK;
+        sm.ascale[i] = (m < mvalid)
+                           ? *reinterpret_cast<const float *>(p.a_scale + (long)(m0 + m) * p.as_rb + g * 4)
+                           : 0.0f;
+      }
+      epi_sync();
+      scales_m0 = m0;
     }
-    epi_sync();
     for (int t = 0; t < C::TILES && ok; ++t) {
       const int n = row0 + t * 128 + f;
       float bs[C::NACC];
@@ -335,7 +346,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
             k = k2 > k ? k2 : k;
           }
-          if (lane == 0 && c0 + i < mvalid) atomicMax(p.arg_keys + m0 + c0 + i, k);
+          if (lane == 0 && c0 + i < mvalid) {
+            if (cta_keys) atomicMax(&sm.akey[c0 + i], k);
+            else atomicMax(p.arg_keys + m0 + c0 + i, k);
+          }
         }
       } else {
         // stage this tile's values [feature][token] in shared memory (padded rows)
@@ -445,6 +459,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   fence_before();
   __syncthreads();
   fence_after();
+  if (cta_keys && threadIdx.x < p.M && blockIdx.x < ntiles) {
+    const unsigned long long k = sm.akey[threadIdx.x];
+    if (k) atomicMax(p.arg_keys + threadIdx.x, k);
+  }
   if (warp == EPI_WARPS + 1) tmem_dealloc<C::TMEM_COLS>(tmem);
 }
 
