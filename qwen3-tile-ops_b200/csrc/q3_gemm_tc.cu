@@ -60,6 +60,9 @@ constexpr unsigned kErrGemmTimeout = 1u << 16;
 #ifndef Q3_GEMM_STAGES_PLAIN
 #define Q3_GEMM_STAGES_PLAIN 4
 #endif
+#ifndef Q3_GEMM_STAGES_64
+#define Q3_GEMM_STAGES_64 4
+#endif
 constexpr int EPI_WARPS = Q3_GEMM_EPI_WARPS;   // a multiple of 4 (TMEM lane quadrants)
 constexpr int THREADS = (EPI_WARPS + 2) * 32;
 // Accumulators start at the bit pattern of 1.5 * 2^23: the int32 sum of a
@@ -82,7 +85,10 @@ struct Cfg {
                                    : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int XROWS = (MODE == EPI_SWIGLU) ? 256 : (MODE == EPI_NORMROPE || MODE == EPI_QUANT) ? 128 : 1;
   // stage ring: as deep as shared memory allows next to the staging buffer
-  static constexpr int STAGES = (MODE == EPI_SWIGLU) ? 3 : (XROWS > 1 ? 4 : Q3_GEMM_STAGES_PLAIN);
+  static constexpr int STAGES = (MODE == EPI_SWIGLU) ? 3
+                               : XROWS > 1              ? 4
+                               : NTOK == 64             ? Q3_GEMM_STAGES_64
+                                                        : Q3_GEMM_STAGES_PLAIN;
   static constexpr int HT = NTOK / (EPI_WARPS / 4);                    // tokens per epilogue warp
 };
 
