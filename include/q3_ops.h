@@ -266,6 +266,64 @@ int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv_pool *pool
                      uint32_t n_seqs, uint32_t T, int32_t *next_ids, void *workspace,
                      size_t workspace_bytes, void *stream);
 
+/* ---- host batching engine (extension; tools/engine.py:81-243) -------------
+ * The reference's PagePool / Scheduler / Sampler / Engine.step in native code:
+ * requests in admission order, prompts fed in chunks of up to 32 rows, one
+ * decode row per generating request, at most max_rows rows per step, 32-token
+ * pages taken from the end of the free list and returned when a request
+ * finishes (the reference's policy exactly; a request that cannot get its
+ * pages waits).  Each step runs the batch's rows through the model on the GPU
+ * (blob non-null: the engine owns a page pool of num_pages pages for every
+ * layer, q3_engine_device_bytes() of device memory, allocated at create) or
+ * through a guest callback that fills the logits of the rows that need them
+ * (the reference's guest_step; blob may be null).  Greedy picks
+ * (temperature <= 0) are the first maximum, as np.argmax; sampling applies
+ * temperature, repetition penalty, top-k and top-p as tools/engine.py:118-149
+ * does and draws from this engine's own per-request random stream (seeded by
+ * `seed`, not numpy's generator).  Ids per request are bit-identical to
+ * running the request alone through forward_chunk. */
+typedef struct q3_sampling_params {
+  uint32_t max_new;
+  float temperature;
+  uint32_t top_k;
+  float top_p;
+  float repetition_penalty;
+  uint64_t seed;
+  const int32_t *stop_tokens;   /* copied at add_request */
+  uint32_t n_stop;
+} q3_sampling_params;
+
+typedef struct q3_engine_item {  /* one request's rows in a step (BatchItem) */
+  int32_t rid;
+  uint32_t row_start, rows, pos;
+  int32_t prefill, needs_logits;
+  const int32_t *tokens;         /* rows ids, valid until the next step       */
+} q3_engine_item;
+
+/* logits: one row of layout->vocab floats for each item with needs_logits, in
+ * item order; return 0 (non-zero aborts the step with that status) */
+typedef int (*q3_engine_guest_fn)(void *user, const q3_engine_item *items, uint32_t n_items,
+                                  float *logits);
+
+size_t q3_engine_device_bytes(const q3_layout *layout, uint32_t num_pages, uint32_t max_rows);
+int q3_engine_create(void *blob, const q3_layout *layout, uint32_t num_pages, uint32_t max_rows,
+                     void **engine);
+int q3_engine_set_guest(void *engine, q3_engine_guest_fn fn, void *user);
+/* Q3_ERR_CAPACITY when n_prompt + max_new exceeds layout->max_seq */
+int q3_engine_add_request(void *engine, const int32_t *prompt, uint32_t n_prompt,
+                          const q3_sampling_params *params, int32_t *rid);
+/* one Engine.step; *did_work = 0 when no request could run (the step then
+ * finishes requests that reached max_new, as the reference does) */
+int q3_engine_step(void *engine, int32_t *did_work, void *stream);
+int q3_engine_run(void *engine, uint32_t max_steps, void *stream);
+int q3_engine_last_batch(const void *engine, q3_engine_item *items, uint32_t cap,
+                         uint32_t *n_items);
+int q3_engine_result(const void *engine, int32_t rid, int32_t *ids, uint32_t cap,
+                     uint32_t *n_generated, int32_t *finished);
+uint32_t q3_engine_free_pages(const void *engine);
+uint64_t q3_engine_steps(const void *engine);
+int q3_engine_destroy(void *engine);
+
 /* ---- tensor-parallel batched decode (extension) ---------------------------
  * The batched decode step split over `world` GPUs of one node, one process per
  * GPU.  The reference runs one hart and has no such split; this follows its

@@ -37,10 +37,11 @@ __global__ void __launch_bounds__(512) k_attention_paged(AttnArgs p) {
   const int lr = blockIdx.x * rows_per_cta + warp / grp;   // row within the sequence
   const int h = kvh * grp + warp % grp;                    // q head
   const int kv_len = p.kv_len_dev ? p.kv_len_dev[seq] : p.kv_len;
-  const int q_rows = p.q_rows;
+  const int q_rows = p.item_rows ? p.item_rows[seq] : p.q_rows;
+  if (static_cast<int>(blockIdx.x) * rows_per_cta >= q_rows) return;   // (uniform) no rows here
   const bool active = lr < q_rows;
   const int qpos = p.causal ? (kv_len - q_rows + lr) : (kv_len - 1);
-  const long qrow = static_cast<long>(seq) * q_rows + lr;
+  const long qrow = (p.item_row0 ? static_cast<long>(p.item_row0[seq]) : static_cast<long>(seq) * q_rows) + lr;
   const uint16_t *table = p.table + static_cast<long>(seq) * p.table_stride;
 
   // this CTA's last visible key (blocks beyond it are skipped by every row)

@@ -24,6 +24,10 @@ struct AttnArgs {
   const int *kv_len_dev;         // [n_seqs] per-sequence kv length
   int causal;
   float qk_scale;
+  // optional, a mixed batch: sequence s has item_rows[s] query rows (at most
+  // q_rows) starting at row item_row0[s] of q8/qs/o8/os; null: q_rows rows
+  // each, sequence s at row s * q_rows
+  const int *item_rows, *item_row0;
 };
 
 int attention_launch(const AttnArgs &p, int n_seqs, cudaStream_t s);
