@@ -36,7 +36,7 @@ enum { Q3_DT_I8 = 0, Q3_DT_U8 = 1, Q3_DT_I32 = 2, Q3_DT_U32 = 3, Q3_DT_F32 = 4 }
 enum {
   Q3_OK = 0,
   Q3_ERR_NULL = 1,     /* a required view/pointer is null                     */
-  Q3_ERR_MODE = 2,     /* CTRL mode > 1 (main_big.cpp:346-348 returns 2)      */
+  Q3_ERR_MODE = 2,     /* CTRL mode > 1 (main_big.cpp:346-348 returns 2), or an unknown flag */
   Q3_ERR_SHAPE = 3,    /* sizes do not fit the operator                       */
   Q3_ERR_DTYPE = 4,    /* view dtype code does not match the operand          */
   Q3_ERR_ALIGN = 5,    /* pointer/stride alignment the kernels need is missing */
@@ -208,6 +208,27 @@ typedef struct q3_layout {
 } q3_layout;
 
 int q3_layout_compute(q3_layout *layout);
+
+/* ---- blob producer (tools/convert_pqwf.py:125-219, tools/pqwf.py:279-360) --
+ * q3_blob_from_safetensors writes the weight regions of a device blob laid
+ * out by `layout` from an HF Qwen3 `model.safetensors`: per-row int8 codes and
+ * scales of the embedding, lm_head (embed_tokens when the file has no
+ * lm_head.weight) and the seven projections of layers [0, layout->layers),
+ * vocab rows [0, layout->vocab); the five norm vectors as float32; RoPE cos/sin
+ * tables for rope_theta (config.json "rope_theta", 1e6 by default).  BF16, F16
+ * and F32 tensors are read; F16 is decoded as IEEE half unless `flags` holds
+ * Q3_CONVERT_F16_AS_UINT16, which widens the 16-bit patterns as unsigned
+ * integers the way pqwf.SafeTensors.block_f32 / vector_f32 do (pqwf.py:302,
+ * 313, 320).  IDS / CTRL / scratch are left to the caller.
+ * Synchronous on `stream`; Q3_ERR_SHAPE when a tensor is missing or its shape
+ * or file range does not fit.
+ * q3_safetensors_tensor (host only) reports one tensor of the file's header:
+ * dtype 0 F32, 1 BF16, 2 F16, -1 other; up to 4 dims of shape. */
+enum { Q3_CONVERT_F16_AS_UINT16 = 1 };
+int q3_blob_from_safetensors(const char *path, const q3_layout *layout, double rope_theta,
+                             uint32_t flags, void *blob, void *stream);
+int q3_safetensors_tensor(const char *path, const char *name, int32_t *dtype, uint64_t *shape,
+                          int32_t *ndim);
 
 /* LmHeadOut of main_big.cpp:142. */
 enum { Q3_LM_NONE = 0, Q3_LM_LOGITS = 1, Q3_LM_ARGMAX = 2 };

@@ -85,6 +85,10 @@ SIGS = {
     "q3_argmax_logits": [VP, C.c_void_p, C.c_void_p],
     "q3_layout_compute": [C.POINTER(Layout)],
     "q3_forward_workspace_bytes": [C.POINTER(Layout)],
+    "q3_blob_from_safetensors": [C.c_char_p, C.POINTER(Layout), C.c_double, C.c_uint32,
+                                 C.c_void_p, C.c_void_p],
+    "q3_safetensors_tensor": [C.c_char_p, C.c_char_p, C.POINTER(C.c_int32),
+                              C.POINTER(C.c_uint64), C.POINTER(C.c_int32)],
     "q3_forward_chunk": [C.c_void_p, C.POINTER(Layout), C.c_uint32, C.c_uint32, C.c_int, C.c_int,
                          C.c_void_p, C.c_size_t, C.c_void_p],
     "q3_generate": [C.c_void_p, C.POINTER(Layout), C.c_void_p, C.c_size_t, C.c_void_p],

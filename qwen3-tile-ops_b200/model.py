@@ -12,7 +12,9 @@ one float32 scale per output row).
 from __future__ import annotations
 
 import ctypes as C
+import json
 from dataclasses import dataclass
+from pathlib import Path
 
 import numpy as np
 import torch
@@ -65,6 +67,16 @@ def header_text(d: Dims) -> str:
     return "\n".join(lines)
 
 
+def safetensors_tensor(path, name: str) -> tuple[str, tuple[int, ...]]:
+    """(dtype, shape) of one tensor of a safetensors header, read by the
+    library's own parser (tools/pqwf.py:279-304)."""
+    dt, nd = C.c_int32(), C.c_int32()
+    shape = (C.c_uint64 * 4)()
+    check("q3_safetensors_tensor", lib().q3_safetensors_tensor(
+        str(path).encode(), name.encode(), C.byref(dt), shape, C.byref(nd)))
+    return {0: "F32", 1: "BF16", 2: "F16"}.get(dt.value, "other"), tuple(shape[:nd.value])
+
+
 class BlobModel:
     """A device copy of the pqwf blob plus the workspace its entry points need."""
 
@@ -105,6 +117,31 @@ class BlobModel:
             self.put(nb + (o["kNK"] - o["kN1"]), ly.nk)
             self.put(nb + (o["kN2"] - o["kN1"]), ly.n2)
         return self
+
+    @classmethod
+    def from_checkpoint(cls, model_dir, layers: int = 0, vocab: int = 0, seq: int = 32,
+                        max_seq: int = 256, device: str | torch.device = "cuda",
+                        f16_as_uint16: bool = False) -> "BlobModel":
+        """tools/convert_pqwf.py:125-219 on the device: the blob of an HF Qwen3
+        checkpoint directory (``config.json`` + ``model.safetensors``), its
+        weights quantised on the GPU by ``q3_blob_from_safetensors``.  ``layers``
+        / ``vocab`` = 0 keep the config's counts (the converter's --layers /
+        --vocab).  F16 tensors are decoded as IEEE half; ``f16_as_uint16``
+        reads them as the reference's pqwf.SafeTensors does (the 16-bit
+        patterns widened as unsigned integers, pqwf.py:302, 313)."""
+        cfg = json.loads((Path(model_dir) / "config.json").read_text())
+        d = Dims(hidden=int(cfg["hidden_size"]), layers=layers or int(cfg["num_hidden_layers"]),
+                 heads=int(cfg["num_attention_heads"]), kv_heads=int(cfg["num_key_value_heads"]),
+                 head_dim=int(cfg["head_dim"]), inter=int(cfg["intermediate_size"]),
+                 vocab=vocab or int(cfg["vocab_size"]), seq=seq, max_seq=max_seq)
+        bm = cls(d, device)
+        path = str(Path(model_dir) / "model.safetensors").encode()
+        stream = torch.cuda.current_stream(bm.device).cuda_stream
+        check("q3_blob_from_safetensors",
+              lib().q3_blob_from_safetensors(path, C.byref(bm.L), float(cfg.get("rope_theta", 1e6)),
+                                             1 if f16_as_uint16 else 0,
+                                             C.c_void_p(bm.blob.data_ptr()), C.c_void_p(stream)))
+        return bm
 
     def set_ids(self, ids) -> None:
         self.put(self.off["kIDS"], np.asarray(ids, np.int32))
