@@ -64,6 +64,10 @@ def parse():
     ap.add_argument("--gemm-microbench", action="store_true",
                     help="config 2: time the per-group w8a8 GEMM shapes through the operator API "
                          "(one JSON line per shape) instead of the decode step")
+    ap.add_argument("--sample-microbench", action="store_true",
+                    help="time the device sampler (q3_sample_logits) on rows x vocab 151936 "
+                         "logits next to the numpy sampler of tools/engine.py on the host")
+    ap.add_argument("--sample-rows", type=int, default=64)
     ap.add_argument("--gemm-ms", default="512,4096,65536")
     ap.add_argument("--gemm-modes", default="qkv,o,gateup,down,lmhead,vquant,qnormrope")
     ap.add_argument("--gemm-reps", type=int, default=5)
@@ -610,10 +614,79 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_sample_microbench(args) -> None:
+    """Seeded N(0, 2^2) float32 logits, rows x 151936; per setting one warm-up
+    call, then the mean of 5 calls timed with CUDA events (the sampler's own
+    workspace and parameter upload outside the timed region).  The host figure
+    is the numpy restatement of tools/engine.py's Sampler.sample on 4 of the
+    rows (one thread)."""
+    import time
+
+    import numpy as np
+    import torch
+    sys.path.insert(0, str(REPO))
+    import __graft_entry__ as ge
+    q3 = ge.load_package()
+    from q3b200._lib import SampleRow, check, lib
+    from q3b200.ops import MatrixView as MV
+    from oracle import sampler
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    R, V = args.sample_rows, 151936
+    rng = np.random.default_rng(5)
+    host = (rng.standard_normal((R, V)) * 2.0).astype(np.float32)
+    lg = torch.from_numpy(host).to(dev)
+    gens = [[int(v) for v in rng.integers(0, V, 32)] for _ in range(R)]
+    gen = torch.tensor(sum(gens, []), dtype=torch.int32, device=dev)
+    out = torch.empty(R, dtype=torch.int32, device=dev)
+    ws = torch.empty(int(lib().q3_sample_workspace_bytes(R, V)), dtype=torch.uint8, device=dev)
+    lv = MV.of(lg).c()
+    settings = {"temperature": dict(temperature=0.8), "top_k50": dict(temperature=0.8, top_k=50),
+                "top_p0.9": dict(temperature=0.8, top_p=0.9),
+                "top_k50_top_p0.9_rep1.2": dict(temperature=0.8, top_k=50, top_p=0.9,
+                                                repetition_penalty=1.2)}
+    us = rng.random(R)
+    for name, st in settings.items():
+        spec = (SampleRow * R)()
+        for r in range(R):
+            spec[r] = SampleRow(st["temperature"], st.get("top_p", 1.0),
+                                st.get("repetition_penalty", 1.0), float(us[r]), st.get("top_k", 0),
+                                32 * r, 32, 0)
+        sp = torch.frombuffer(bytearray(spec), dtype=torch.uint8).to(dev)
+
+        def fn():
+            check("q3_sample_logits", lib().q3_sample_logits(
+                C.byref(lv), sp.data_ptr(), gen.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                ws.numel(), torch.cuda.current_stream().cuda_stream))
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / 5
+        picks = out.cpu().tolist()
+        t0 = time.perf_counter()
+        ref = [sampler.sample(host[r], st["temperature"], st.get("top_k", 0), st.get("top_p", 1.0),
+                              st.get("repetition_penalty", 1.0), gens[r], float(us[r]))
+               for r in range(4)]
+        host_ms = (time.perf_counter() - t0) * 1e3 / 4
+        print(json.dumps({"sampler": name, "rows": R, "vocab": V, "ms": round(ms, 4),
+                          "us_per_row_device": round(ms * 1e3 / R, 2),
+                          "host_numpy_ms_per_row": round(host_ms, 2),
+                          "picks_match_numpy": picks[:4] == ref}), flush=True)
+    if q3._lib.lib().q3_device_status() != 0:
+        raise RuntimeError("device status")
+
+
 if __name__ == "__main__":
     a = parse()
     if a.gemm_microbench:
         run_gemm_microbench(a)
+    elif a.sample_microbench:
+        run_sample_microbench(a)
     elif a.impl == "reference":
         run_reference(a)
     else:

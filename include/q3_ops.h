@@ -300,15 +300,19 @@ int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv_pool *pool
  * (the reference's guest_step; blob may be null).  Greedy picks
  * (temperature <= 0) are the first maximum, as np.argmax; sampling applies
  * temperature, repetition penalty, top-k and top-p as tools/engine.py:118-149
- * does and draws from this engine's own per-request random stream (seeded by
- * `seed`, not numpy's generator).  Ids per request are bit-identical to
- * running the request alone through forward_chunk. */
+ * does, in float64, and draws one uniform per sample from the request's
+ * np.random.default_rng(seed) stream (the same stream as the reference's
+ * Request.rng), so a request's sampled ids follow the reference's for the same
+ * logits.  On the GPU step the sampler runs on the device after the lm_head
+ * (q3_sample_logits); with a guest it runs on the host.  Greedy ids per
+ * request are bit-identical to running the request alone through
+ * forward_chunk. */
 typedef struct q3_sampling_params {
   uint32_t max_new;
-  float temperature;
+  double temperature;
   uint32_t top_k;
-  float top_p;
-  float repetition_penalty;
+  double top_p;
+  double repetition_penalty;
   uint64_t seed;
   const int32_t *stop_tokens;   /* copied at add_request */
   uint32_t n_stop;
@@ -344,6 +348,33 @@ int q3_engine_result(const void *engine, int32_t rid, int32_t *ids, uint32_t cap
 uint32_t q3_engine_free_pages(const void *engine);
 uint64_t q3_engine_steps(const void *engine);
 int q3_engine_destroy(void *engine);
+
+/* ---- sampling after the lm_head (tools/engine.py:118-149) -----------------
+ * q3_sample_logits picks one id per row of `logits` (rows x vocab f32) on the
+ * device, with the Sampler's steps in float64: temperature <= 0 -> the first
+ * maximum; else x = logits / temperature, the repetition penalty on the row's
+ * generated ids (x / rp where x > 0, else x * rp), top-k (every x below the
+ * k-th largest dropped), top-p (in descending order, every element whose
+ * cumulative normalised probability exceeds top_p dropped, the first always
+ * kept; equal values are ordered by index), then the first index whose
+ * cumulative probability (index order) exceeds u, as Generator.choice(V, p)
+ * does with its uniform u.  `params` and `generated` are DEVICE arrays; row r's
+ * generated ids are generated[gen_offset .. gen_offset + gen_count).  Results
+ * agree with the reference's float64 numpy arithmetic except where u or top_p
+ * falls within a few float64 ulps of a cumulative sum (summation order). */
+typedef struct q3_sample_row {
+  double temperature, top_p, repetition_penalty;
+  double u;                 /* the draw: Generator.random() of the request   */
+  int32_t top_k;
+  uint32_t gen_offset, gen_count, pad;
+} q3_sample_row;
+
+size_t q3_sample_workspace_bytes(uint32_t rows, uint32_t vocab);
+int q3_sample_logits(const q3_view *logits, const q3_sample_row *params, const int32_t *generated,
+                     int32_t *out_ids, void *workspace, size_t workspace_bytes, void *stream);
+
+/* The first n draws of np.random.default_rng(seed).random() (host). */
+int q3_rng_uniforms(uint64_t seed, uint32_t n, double *out);
 
 /* ---- tensor-parallel batched decode (extension) ---------------------------
  * The batched decode step split over `world` GPUs of one node, one process per

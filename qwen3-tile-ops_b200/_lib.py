@@ -39,6 +39,12 @@ class View(C.Structure):
                 ("rows", C.c_uint32), ("cols", C.c_uint32), ("dtype", C.c_uint8)]
 
 
+class SampleRow(C.Structure):
+    _fields_ = [("temperature", C.c_double), ("top_p", C.c_double),
+                ("repetition_penalty", C.c_double), ("u", C.c_double), ("top_k", C.c_int32),
+                ("gen_offset", C.c_uint32), ("gen_count", C.c_uint32), ("pad", C.c_uint32)]
+
+
 class PagedKV(C.Structure):
     _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("ks", C.c_void_p), ("vs", C.c_void_p),
                 ("table", C.c_void_p), ("page_tokens", C.c_uint32), ("page_bytes", C.c_uint32),
@@ -100,6 +106,10 @@ SIGS = {
     "q3_prefill_batch": [C.c_void_p, C.POINTER(Layout), C.POINTER(KVPool), C.c_void_p, C.c_uint32,
                          C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_size_t,
                          C.c_void_p],
+    "q3_sample_workspace_bytes": [C.c_uint32, C.c_uint32],
+    "q3_sample_logits": [VP, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                         C.c_void_p],
+    "q3_rng_uniforms": [C.c_uint64, C.c_uint32, C.POINTER(C.c_double)],
     "q3_exp_rows": [VP, VP, C.c_void_p],
     "q3_exp2_rows": [VP, VP, C.c_void_p],
     "q3_last_cuda_error": [],
@@ -110,6 +120,7 @@ SIGS = {
     "q3_timer_detach": [],
 }
 RESTYPE = {"q3_gemm_nt_group_argmax_workspace_bytes": C.c_size_t,
+           "q3_sample_workspace_bytes": C.c_size_t,
            "q3_forward_workspace_bytes": C.c_size_t, "q3_decode_workspace_bytes": C.c_size_t,
            "q3_prefill_workspace_bytes": C.c_size_t,
            "q3_last_cuda_error": C.c_char_p, "q3_launch_count": C.c_uint64}

@@ -15,10 +15,14 @@
 // into each request's pages, one paged attention launch over all requests
 // (each row sees its own request's keys up to its position), O + residual, the
 // MLP, and for the requests that need logits the final norm and the lm_head:
-// argmax for greedy requests, full logits for sampled ones.
+// the fused argmax when every pick is greedy, else the logits and the device
+// sampler (q3_sample_logits), so only the picked ids come back.
 //
 // Instead of the GPU step, a guest callback may produce the logits (the
 // reference's guest_step), which runs the scheduler and sampler on the host.
+// Either way a sampled pick draws its uniform from the request's
+// np.random.default_rng(seed) stream (q3_rng.h), as the reference's
+// Request.rng does.
 #include <stdlib.h>
 #include <string.h>
 
@@ -29,6 +33,7 @@
 
 #include "q3_attention.h"
 #include "q3_common.cuh"
+#include "q3_rng.h"
 
 namespace {
 
@@ -44,7 +49,7 @@ struct Req {
   uint32_t n_fed = 0;
   std::vector<uint32_t> pages;
   ReqState state = S_WAITING;
-  uint64_t rng = 0;
+  q3rng::Pcg64 rng;
 };
 
 struct Item {
@@ -61,9 +66,12 @@ struct Dev {
   // rows of a batch
   size_t x, h, h8, hs, q8, qs, k8, ks, v8, vs, o8, os, s8, ss, cosr, sinr;
   // step inputs, copied in one piece
-  size_t in, ids, pos, row_item, item_rows, item_row0, item_kvlen, logit_rows, tables, in_bytes;
-  // lm_head rows
-  size_t lx, lh, lh8, lhs, best, bidx, keys, logits;
+  size_t in, ids, pos, row_item, item_rows, item_row0, item_kvlen, logit_rows, tables, sparams,
+      in_bytes;
+  // generated ids of the sampled rows (repetition penalty), copied after `in`
+  size_t gen, gen_bytes;
+  // lm_head rows, sampler
+  size_t lx, lh, lh8, lhs, best, bidx, keys, logits, sout, sws;
   // page pool
   size_t pk, pv, pks, pvs;
   size_t total;
@@ -170,8 +178,11 @@ Dev carve(const q3_layout &L, uint32_t R, uint32_t num_pages) {
   d.item_kvlen = itake(4 * R);
   d.logit_rows = itake(4 * R);
   d.tables = itake(2 * R * MP);
+  d.sparams = itake(sizeof(q3_sample_row) * R);
   d.in_bytes = io;
   off += align256(io);
+  d.gen_bytes = 4 * R * static_cast<size_t>(L.max_seq);
+  d.gen = take(d.gen_bytes);
   d.lx = take(4 * R * H);
   d.lh = take(4 * R * H);
   d.lh8 = take(R * H);
@@ -180,6 +191,8 @@ Dev carve(const q3_layout &L, uint32_t R, uint32_t num_pages) {
   d.bidx = take(4 * R);
   d.keys = take(8 * R);
   d.logits = take(4 * R * V);
+  d.sout = take(4 * R);
+  d.sws = take(q3_sample_workspace_bytes(R, static_cast<uint32_t>(V)));
   const size_t pool_rows = static_cast<size_t>(L.layers) * num_pages * kPT;
   d.pk = take(pool_rows * KW);
   d.pv = take(pool_rows * KW);
@@ -261,27 +274,45 @@ std::vector<Item> build_batch(q3_engine &e) {
 }
 
 // ------------------------------------------------------------ sampler
-uint64_t splitmix64(uint64_t &s) {
-  uint64_t z = (s += 0x9E3779B97F4A7C15ull);
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
+// numpy's pairwise summation of a float64 array (the loop np.sum runs)
+double pairwise_sum(const double *a, size_t n) {
+  if (n < 8) {
+    double s = 0.0;
+    for (size_t i = 0; i < n; ++i) s += a[i];
+    return s;
+  }
+  if (n <= 128) {
+    double r[8];
+    for (int j = 0; j < 8; ++j) r[j] = a[j];
+    size_t i = 8;
+    for (; i < n - n % 8; i += 8)
+      for (int j = 0; j < 8; ++j) r[j] += a[i + j];
+    double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+    for (; i < n; ++i) res += a[i];
+    return res;
+  }
+  size_t n2 = n / 2;
+  n2 -= n2 % 8;
+  return pairwise_sum(a, n2) + pairwise_sum(a + n2, n - n2);
 }
 
-// tools/engine.py:118-149: greedy = first maximum; otherwise temperature,
-// repetition penalty, top-k, top-p in the reference's order, then a draw from
-// the softmax (this engine's own random stream, seeded per request)
+// tools/engine.py:118-149 in float64 with numpy's operation order: greedy =
+// np.argmax; x / T; penalty over set(generated); top-k threshold at
+// np.partition's k-th largest; top-p over the descending order (equal values
+// by index; numpy's default argsort leaves them to its introsort); then
+// Generator.choice(V, p): cdf = cumsum(p) / cdf[-1], the first index whose
+// cdf exceeds u.  u is the request's next default_rng(seed).random().
 int32_t sample(const float *logits, uint32_t V, Req &r) {
   const q3_sampling_params &p = r.sp;
-  if (p.temperature <= 0.0f) {
+  if (!(p.temperature > 0.0)) {
     uint32_t best = 0;
     for (uint32_t i = 1; i < V; ++i)
       if (static_cast<double>(logits[i]) > static_cast<double>(logits[best])) best = i;
     return static_cast<int32_t>(best);
   }
   std::vector<double> x(logits, logits + V);
-  for (double &v : x) v /= static_cast<double>(p.temperature);
-  if (p.repetition_penalty != 1.0f) {
+  for (double &v : x) v /= p.temperature;
+  if (p.repetition_penalty != 1.0) {
     std::vector<int32_t> seen(r.generated);
     std::sort(seen.begin(), seen.end());
     seen.erase(std::unique(seen.begin(), seen.end()), seen.end());
@@ -298,28 +329,29 @@ int32_t sample(const float *logits, uint32_t V, Req &r) {
     for (double &v : x)
       if (v < kth) v = -INFINITY;
   }
-  if (p.top_p < 1.0f) {
+  std::vector<double> probs(V);
+  if (p.top_p < 1.0) {
     std::vector<uint32_t> order(V);
     for (uint32_t i = 0; i < V; ++i) order[i] = i;
     std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return x[a] > x[b]; });
-    std::vector<double> probs(V);
-    double sum = 0.0;
-    for (uint32_t i = 0; i < V; ++i) sum += probs[i] = std::exp(x[order[i]] - x[order[0]]);
+    const double top = x[order[0]];
+    for (uint32_t i = 0; i < V; ++i) probs[i] = std::exp(x[order[i]] - top);
+    const double sum = pairwise_sum(probs.data(), V);
     double cum = 0.0;
     for (uint32_t i = 0; i < V; ++i) {
       cum += probs[i] / sum;
-      if (i > 0 && cum > p.top_p) x[order[i]] = -INFINITY;
+      if (i > 0 && !(cum <= p.top_p)) x[order[i]] = -INFINITY;
     }
   }
   const double m = *std::max_element(x.begin(), x.end());
-  double sum = 0.0;
-  for (double &v : x) sum += v = std::exp(v - m);
-  const double u = static_cast<double>(splitmix64(r.rng) >> 11) * 0x1.0p-53 * sum;
+  for (uint32_t i = 0; i < V; ++i) probs[i] = std::exp(x[i] - m);
+  const double sum = pairwise_sum(probs.data(), V);
   double cum = 0.0;
-  for (uint32_t i = 0; i < V; ++i) {
-    cum += x[i];
-    if (u < cum) return static_cast<int32_t>(i);
-  }
+  for (double &v : probs) v = cum += v / sum;
+  const double last = probs[V - 1];
+  const double u = r.rng.random();
+  for (uint32_t i = 0; i < V; ++i)
+    if (probs[i] / last > u) return static_cast<int32_t>(i);
   return static_cast<int32_t>(V - 1);
 }
 
@@ -353,6 +385,9 @@ int gpu_step(q3_engine &e, const std::vector<Item> &items, std::vector<int32_t> 
   int32_t *item_kvlen = reinterpret_cast<int32_t *>(in + d.item_kvlen);
   int32_t *logit_rows = reinterpret_cast<int32_t *>(in + d.logit_rows);
   uint16_t *tables = reinterpret_cast<uint16_t *>(in + d.tables);
+  q3_sample_row *sp = reinterpret_cast<q3_sample_row *>(in + d.sparams);
+  int32_t *gen = reinterpret_cast<int32_t *>(in + d.in_bytes);
+  uint32_t n_gen = 0;
   for (size_t i = 0; i < items.size(); ++i) {
     const Item &it = items[i];
     for (uint32_t t = 0; t < it.rows; ++t) {
@@ -366,13 +401,33 @@ int gpu_step(q3_engine &e, const std::vector<Item> &items, std::vector<int32_t> 
     for (size_t pg = 0; pg < it.req->pages.size(); ++pg)
       tables[i * MP + pg] = static_cast<uint16_t>(it.req->pages[pg]);
     if (it.needs_logits) {
+      // the sampler's inputs; u is drawn only for a sampled pick, as the
+      // reference's rng.choice is only reached then
+      Req &rq = *it.req;
+      q3_sample_row &row = sp[n_logit];
+      row.temperature = rq.sp.temperature;
+      row.top_p = rq.sp.top_p;
+      row.repetition_penalty = rq.sp.repetition_penalty;
+      row.top_k = static_cast<int32_t>(std::min<uint32_t>(rq.sp.top_k, 0x7FFFFFFF));
+      row.gen_offset = n_gen;
+      row.gen_count = 0;
+      if (rq.sp.temperature > 0.0) {
+        any_sampled = true;
+        row.u = rq.rng.random();
+        if (rq.sp.repetition_penalty != 1.0) {
+          memcpy(gen + n_gen, rq.generated.data(), 4 * rq.generated.size());
+          row.gen_count = static_cast<uint32_t>(rq.generated.size());
+          n_gen += row.gen_count;
+        }
+      }
       logit_rows[n_logit++] = static_cast<int32_t>(it.row_start + it.rows - 1);
-      any_sampled |= it.req->sp.temperature > 0.0f;
     }
     R = std::max(R, it.row_start + it.rows);
     maxr = std::max(maxr, it.rows);
   }
   ce = cudaMemcpyAsync(D + d.in, in, d.in_bytes, cudaMemcpyHostToDevice, st);
+  if (ce == cudaSuccess && n_gen)
+    ce = cudaMemcpyAsync(D + d.gen, gen, 4 * static_cast<size_t>(n_gen), cudaMemcpyHostToDevice, st);
   if (ce == cudaSuccess) ce = cudaEventRecord(e.in_copied, st);
   if (ce != cudaSuccess) {
     q3h::set_cuda_error(ce);
@@ -498,21 +553,26 @@ int gpu_step(q3_engine &e, const std::vector<Item> &items, std::vector<int32_t> 
   Q3_TRY(q3_gemm_nt_group_argmax(&lh8, &lhs, &lm, &lm_s, reinterpret_cast<float *>(D + d.best),
                                  reinterpret_cast<int32_t *>(D + d.bidx), 256, D + d.keys,
                                  8 * static_cast<size_t>(e.max_rows), s));
-  ce = cudaMemcpyAsync(e.host_out, D + d.bidx, 4 * n_logit, cudaMemcpyDeviceToHost, st);
-  if (ce == cudaSuccess && any_sampled) {
+  const char *picked = D + d.bidx;
+  if (any_sampled) {
+    // full logits of the rows, then the sampler on the device: only the
+    // picked ids come back
     const q3_view lg = vw(D + d.logits, n_logit, V, Q3_DT_F32);
     Q3_TRY(q3_gemm_nt_group_store(&lh8, &lhs, &lm, &lm_s, &lg, 256, nullptr, nullptr, nullptr,
                                   nullptr, nullptr, nullptr, 0.0f, s));
-    ce = cudaMemcpyAsync(e.host_out + align256(4 * e.max_rows), D + d.logits,
-                         4 * static_cast<size_t>(n_logit) * V, cudaMemcpyDeviceToHost, st);
+    Q3_TRY(q3_sample_logits(&lg, reinterpret_cast<const q3_sample_row *>(D + d.in + d.sparams),
+                            reinterpret_cast<const int32_t *>(D + d.gen),
+                            reinterpret_cast<int32_t *>(D + d.sout), D + d.sws,
+                            q3_sample_workspace_bytes(e.max_rows, V), s));
+    picked = D + d.sout;
   }
+  ce = cudaMemcpyAsync(e.host_out, picked, 4 * n_logit, cudaMemcpyDeviceToHost, st);
   if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
   if (ce != cudaSuccess) {
     q3h::set_cuda_error(ce);
     return Q3_ERR_CUDA;
   }
   memcpy(ids_out.data(), e.host_out, 4 * n_logit);
-  if (any_sampled) logits_out = reinterpret_cast<const float *>(e.host_out + align256(4 * e.max_rows));
   return Q3_OK;
 }
 
@@ -548,10 +608,10 @@ extern "C" int q3_engine_create(void *blob, const q3_layout *layout, uint32_t nu
   e->used.assign(num_pages, 0);
   if (blob) {   // device step: pool, row buffers and pinned staging
     e->d = carve(L, max_rows, num_pages);
-    e->host_out_bytes = align256(4 * max_rows) + 4 * static_cast<size_t>(max_rows) * L.vocab;
+    e->host_out_bytes = align256(4 * max_rows);
     cudaError_t ce = cudaMalloc(&e->dev, e->d.total);
     if (ce == cudaSuccess) ce = cudaMemset(e->dev, 0, e->d.total);
-    if (ce == cudaSuccess) ce = cudaMallocHost(&e->host_in, e->d.in_bytes);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->host_in, e->d.in_bytes + e->d.gen_bytes);
     if (ce == cudaSuccess) ce = cudaMallocHost(&e->host_out, e->host_out_bytes);
     if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&e->in_copied, cudaEventDisableTiming);
     if (ce == cudaSuccess) ce = cudaEventRecord(e->in_copied, 0);
@@ -595,7 +655,7 @@ extern "C" int q3_engine_add_request(void *engine, const int32_t *prompt, uint32
   r->sp = *params;
   r->stop.assign(params->stop_tokens, params->stop_tokens + params->n_stop);
   r->sp.stop_tokens = nullptr;
-  r->rng = params->seed;
+  r->rng = q3rng::Pcg64(params->seed);
   e->reqs.push_back(r);
   *rid = r->rid;
   return Q3_OK;
@@ -641,7 +701,7 @@ extern "C" int q3_engine_step(void *engine, int32_t *did_work, void *stream) {
     r.n_fed += it.rows;
     if (it.needs_logits) {
       int32_t tok;
-      if (!e->guest && r.sp.temperature <= 0.0f) tok = greedy[li];
+      if (!e->guest) tok = greedy[li];   // picked on the device
       else tok = sample(logits + static_cast<size_t>(li) * V, V, r);
       ++li;
       r.generated.push_back(tok);

@@ -22,8 +22,8 @@ from ._lib import Layout, check, lib
 
 
 class _Params(C.Structure):
-    _fields_ = [("max_new", C.c_uint32), ("temperature", C.c_float), ("top_k", C.c_uint32),
-                ("top_p", C.c_float), ("repetition_penalty", C.c_float), ("seed", C.c_uint64),
+    _fields_ = [("max_new", C.c_uint32), ("temperature", C.c_double), ("top_k", C.c_uint32),
+                ("top_p", C.c_double), ("repetition_penalty", C.c_double), ("seed", C.c_uint64),
                 ("stop_tokens", C.POINTER(C.c_int32)), ("n_stop", C.c_uint32)]
 
 

@@ -14,7 +14,7 @@ from dataclasses import dataclass, replace
 
 import torch
 
-from ._lib import (DT_F32, DT_I8, DT_I32, DT_U32, DT_U8, PagedKV, View, check, lib)
+from ._lib import (DT_F32, DT_I8, DT_I32, DT_U32, DT_U8, PagedKV, SampleRow, View, check, lib)
 
 _TORCH_DT = {torch.int8: DT_I8, torch.uint8: DT_U8, torch.int32: DT_I32, torch.float32: DT_F32}
 _ESIZE = {DT_I8: 1, DT_U8: 1, DT_I32: 4, DT_U32: 4, DT_F32: 4}
@@ -165,6 +165,34 @@ def gemm_nt_group_argmax(a, a_scale, b, b_scale, best: torch.Tensor, bidx: torch
 
 def argmax_logits(logits, out_id: torch.Tensor, stream=None) -> None:
     check("q3_argmax_logits", lib().q3_argmax_logits(_v(logits), out_id.data_ptr(), _s(stream)))
+
+
+def sample_logits(logits, params, generated=None, stream=None) -> torch.Tensor:
+    """tools/engine.py:118-149 (Sampler.sample) for every row of ``logits``
+    (rows x vocab float32, CUDA) on the device.  ``params``: one dict per row
+    with ``temperature``, ``top_k``, ``top_p``, ``repetition_penalty`` and the
+    draw ``u`` (the request's next ``default_rng(seed).random()``);
+    ``generated``: per row, the ids the repetition penalty applies to.
+    Returns the picked ids (int32, on the device)."""
+    lv = MatrixView.of(logits) if isinstance(logits, torch.Tensor) else logits
+    rows = len(params)
+    gen_all, spec = [], (SampleRow * max(rows, 1))()
+    for r, p in enumerate(params):
+        g = list(generated[r]) if generated is not None else []
+        spec[r] = SampleRow(float(p.get("temperature", 0.0)), float(p.get("top_p", 1.0)),
+                            float(p.get("repetition_penalty", 1.0)), float(p.get("u", 0.0)),
+                            int(p.get("top_k", 0)), len(gen_all), len(g), 0)
+        gen_all += g
+    dev = torch.device("cuda", torch.cuda.current_device()) if stream is None else stream.device
+    sp = torch.frombuffer(bytearray(spec), dtype=torch.uint8).to(dev)
+    gen = torch.tensor(gen_all or [0], dtype=torch.int32, device=dev)
+    out = torch.empty(max(rows, 1), dtype=torch.int32, device=dev)
+    ws = torch.empty(max(int(lib().q3_sample_workspace_bytes(rows, lv.cols)), 8), dtype=torch.uint8,
+                     device=dev)
+    check("q3_sample_logits", lib().q3_sample_logits(_v(lv.rows_of(0, rows)), sp.data_ptr(),
+                                                     gen.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                                                     ws.numel(), _s(stream)))
+    return out[:rows]
 
 
 def exp_rows(x, out, stream=None) -> None:

@@ -2,7 +2,8 @@
 on the CPU: the batch of every step, the generated ids, the finished flags and
 the free pages must match the trace ``tests/golden/engine_trace.json`` that
 ``tests/golden/gen_engine_trace.py`` recorded from the reference with the mock
-guest of its ``tools/check_engine.py``."""
+guest of its ``tools/check_engine.py`` (and, in the sampling scenario, a table
+guest: the sampled ids follow the reference's Sampler and random streams)."""
 
 from __future__ import annotations
 
@@ -28,15 +29,22 @@ def _mock_engine(q3, sc):
     from q3b200.engine import Engine
     vocab = sc["vocab"]
     generated = {}
+    table = None
+    if sc.get("guest") == "table":     # gen_engine_trace.table_logits
+        table = (np.random.default_rng(77).standard_normal((64, vocab)) * 2.0).astype(np.float32)
 
     def guest(items):        # tools/check_engine.py mock_guest
         out = {}
         for it in items:
             if it.needs_logits:
                 n = generated.get(it.rid, 0)
-                x = np.full(vocab, -100.0, np.float32)
-                x[(it.rid * 7 + n + it.rows) % vocab] = 100.0
-                out[it.rid] = x
+                j = it.rid * 7 + n + it.rows
+                if table is not None:
+                    out[it.rid] = table[j % 64]
+                else:
+                    x = np.full(vocab, -100.0, np.float32)
+                    x[j % vocab] = 100.0
+                    out[it.rid] = x
                 generated[it.rid] = n + 1
         return out
     return Engine(None, num_pages=sc["num_pages"], max_rows=sc["max_rows"], guest=guest,
@@ -48,8 +56,10 @@ def test_engine_matches_reference_trace(q3, k):
     from q3b200.engine import SamplingParams
     sc = TRACE[k]
     eng = _mock_engine(q3, sc)
-    rids = [eng.add_request(r["prompt"], SamplingParams(max_new=r["max_new"],
-                                                         stop_tokens=set(r["stop"])))
+    rids = [eng.add_request(r["prompt"], SamplingParams(
+        max_new=r["max_new"], temperature=r.get("temperature", 0.0), top_k=r.get("top_k", 0),
+        top_p=r.get("top_p", 1.0), repetition_penalty=r.get("repetition_penalty", 1.0),
+        seed=r.get("seed", 0), stop_tokens=set(r["stop"])))
             for r in sc["requests"]]
     steps = []
     while eng.step():
