@@ -29,6 +29,8 @@ namespace {
 
 constexpr int kT = 512;           // threads per row
 constexpr int kW = kT / 32;
+constexpr int kB = 8;             // loads a thread issues before using them
+constexpr int kCap = 4096;        // bucket size from which a descent continues in shared memory
 
 __device__ __forceinline__ uint64_t okey(double x) {
   const uint64_t b = static_cast<uint64_t>(__double_as_longlong(x));
@@ -43,7 +45,8 @@ struct Shared {
   double seg[kW];
   uint32_t tie_cnt[kW], tie_base[kW];
   uint64_t prefix, pmask;
-  uint32_t need;
+  uint32_t need, ccount;
+  int compact;
   double above;
   int digit, stop;
   double m;
@@ -97,31 +100,61 @@ __device__ double block_sum(double v, Shared &sm) {
   return sm.total;
 }
 
+// the candidates of a descent once they fit in shared memory
+struct Cand {
+  uint64_t *key;
+  double *e;
+};
+
 // one level of the descent: counts (and masses) of the elements under
-// (prefix, pmask) per 8-bit digit at `shift`; runs of equal digits in a
-// thread's elements are added to the shared histogram once
-__device__ void histogram(const double *X, const double *E, int V, int shift, Shared &sm) {
+// (prefix, pmask) per 8-bit digit at `shift`, over the row or, once
+// compacted, over the shared candidates; runs of equal digits in a thread's
+// elements are added to the shared histogram once
+__device__ void histogram(const double *X, const double *E, int V, int shift, Shared &sm,
+                          Cand c) {
   for (int d = threadIdx.x; d < 256; d += kT) { sm.hc[d] = 0; sm.hm[d] = 0.0; }
   __syncthreads();
   const uint64_t prefix = sm.prefix, pmask = sm.pmask;
   int cur = -1;
   uint32_t cnt = 0;
   double mass = 0.0;
-  for (int i = threadIdx.x; i < V; i += kT) {
-    const uint64_t key = okey(X[i]);
-    if ((key & pmask) != prefix) continue;
-    const int d = static_cast<int>((key >> shift) & 255u);
-    if (d != cur) {
-      if (cnt) {
-        atomicAdd(&sm.hc[cur], cnt);
-        if (E) atomicAdd(&sm.hm[cur], mass);
-      }
-      cur = d;
-      cnt = 0;
-      mass = 0.0;
+  if (sm.compact) {
+    for (uint32_t j = threadIdx.x; j < sm.ccount; j += kT) {
+      const uint64_t key = c.key[j];
+      if ((key & pmask) != prefix) continue;
+      const int d = static_cast<int>((key >> shift) & 255u);
+      atomicAdd(&sm.hc[d], 1u);
+      if (E) atomicAdd(&sm.hm[d], c.e[j]);
     }
-    ++cnt;
-    if (E) mass += E[i];
+    __syncthreads();
+    return;
+  }
+  for (int base = threadIdx.x; base < V; base += kB * kT) {
+    double xv[kB], ev[kB];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const int i = base + j * kT;
+      xv[j] = i < V ? X[i] : 0.0;
+      ev[j] = (E && i < V) ? E[i] : 0.0;
+    }
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      if (base + j * kT >= V) break;
+      const uint64_t key = okey(xv[j]);
+      if ((key & pmask) != prefix) continue;
+      const int d = static_cast<int>((key >> shift) & 255u);
+      if (d != cur) {
+        if (cnt) {
+          atomicAdd(&sm.hc[cur], cnt);
+          if (E) atomicAdd(&sm.hm[cur], mass);
+        }
+        cur = d;
+        cnt = 0;
+        mass = 0.0;
+      }
+      ++cnt;
+      mass += ev[j];
+    }
   }
   if (cnt) {
     atomicAdd(&sm.hc[cur], cnt);
@@ -130,12 +163,40 @@ __device__ void histogram(const double *X, const double *E, int V, int shift, Sh
   __syncthreads();
 }
 
+// after a level: when the chosen bucket fits, copy its elements (key, mass)
+// into shared memory; later levels read them there
+__device__ void maybe_compact(const double *X, const double *E, int V, uint32_t count, Shared &sm,
+                              Cand c) {
+  if (sm.compact || count > static_cast<uint32_t>(kCap)) return;
+  const uint64_t prefix = sm.prefix, pmask = sm.pmask;
+  for (int base = threadIdx.x; base < V; base += kB * kT) {
+    double xv[kB];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) xv[j] = base + j * kT < V ? X[base + j * kT] : 0.0;
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const int i = base + j * kT;
+      if (i >= V) break;
+      const uint64_t key = okey(xv[j]);
+      if ((key & pmask) != prefix) continue;
+      const uint32_t slot = atomicAdd(&sm.ccount, 1u);
+      if (slot < static_cast<uint32_t>(kCap)) {
+        c.key[slot] = key;
+        c.e[slot] = E ? E[i] : 0.0;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) sm.compact = 1;
+  __syncthreads();
+}
+
 // key of the k-th largest x (np.partition(x, -k)[-k])
-__device__ uint64_t kth_key(const double *X, int V, uint32_t k, Shared &sm) {
-  if (threadIdx.x == 0) { sm.prefix = 0; sm.pmask = 0; sm.need = k; }
+__device__ uint64_t kth_key(const double *X, int V, uint32_t k, Shared &sm, Cand c) {
+  if (threadIdx.x == 0) { sm.prefix = 0; sm.pmask = 0; sm.need = k; sm.compact = 0; sm.ccount = 0; }
   __syncthreads();
   for (int shift = 56; shift >= 0; shift -= 8) {
-    histogram(X, nullptr, V, shift, sm);
+    histogram(X, nullptr, V, shift, sm, c);
     if (threadIdx.x == 0) {
       uint32_t acc = 0;
       int d = 255;
@@ -146,8 +207,10 @@ __device__ uint64_t kth_key(const double *X, int V, uint32_t k, Shared &sm) {
       sm.need -= acc;
       sm.prefix |= static_cast<uint64_t>(d) << shift;
       sm.pmask |= 255ull << shift;
+      sm.digit = d;
     }
     __syncthreads();
+    if (shift) maybe_compact(X, nullptr, V, sm.hc[sm.digit], sm, c);
   }
   return sm.prefix;
 }
@@ -155,11 +218,18 @@ __device__ uint64_t kth_key(const double *X, int V, uint32_t k, Shared &sm) {
 // top-p boundary: keep key >= t_ge, plus the first r_ties (index order) of
 // the elements whose key is t_tie
 __device__ void top_p_bound(const double *X, const double *E, int V, double S, double top_p,
-                            double m, Shared &sm) {
-  if (threadIdx.x == 0) { sm.prefix = 0; sm.pmask = 0; sm.above = 0.0; sm.stop = 0; }
+                            double m, Shared &sm, Cand c) {
+  if (threadIdx.x == 0) {
+    sm.prefix = 0;
+    sm.pmask = 0;
+    sm.above = 0.0;
+    sm.stop = 0;
+    sm.compact = 0;
+    sm.ccount = 0;
+  }
   __syncthreads();
   for (int shift = 56; shift >= 0; shift -= 8) {
-    histogram(X, E, V, shift, sm);
+    histogram(X, E, V, shift, sm, c);
     if (threadIdx.x == 0) {
       int d = 255, found = 0;
       double above = sm.above;
@@ -185,6 +255,7 @@ __device__ void top_p_bound(const double *X, const double *E, int V, double S, d
     }
     __syncthreads();
     if (sm.stop) return;
+    if (shift) maybe_compact(X, E, V, sm.hc[sm.digit], sm, c);
   }
   if (threadIdx.x == 0) {
     // one key value: c equal elements of mass e_c; keep the first r
@@ -216,9 +287,16 @@ __global__ void __launch_bounds__(kT, 1)
   if (!(p.temperature > 0.0)) {   // np.argmax: the first maximum
     double bv = -INFINITY;
     int bi = -1;
-    for (int i = tid; i < V; i += kT) {
-      const double v = static_cast<double>(lg[i]);
-      if (bi < 0 || v > bv) { bv = v; bi = i; }
+    for (int base = tid; base < V; base += kB * kT) {
+      float lv[kB];
+#pragma unroll
+      for (int j = 0; j < kB; ++j) lv[j] = base + j * kT < V ? lg[base + j * kT] : 0.0f;
+#pragma unroll
+      for (int j = 0; j < kB; ++j) {
+        const int i = base + j * kT;
+        const double v = static_cast<double>(lv[j]);
+        if (i < V && (bi < 0 || v > bv)) { bv = v; bi = i; }
+      }
     }
     double m;
     int a;
@@ -230,6 +308,9 @@ __global__ void __launch_bounds__(kT, 1)
   double *X = ws + static_cast<size_t>(r) * 2 * V;
   double *E = X + V;
   const int nb = (V + 31) >> 5;
+  Cand cand;
+  cand.key = reinterpret_cast<uint64_t *>(bitmap + ((nb + 1) & ~1));
+  cand.e = reinterpret_cast<double *>(cand.key + kCap);
   const bool pen = p.repetition_penalty != 1.0;
   if (pen) {
     for (int j = tid; j < nb; j += kT) bitmap[j] = 0;
@@ -243,32 +324,48 @@ __global__ void __launch_bounds__(kT, 1)
   // x = logits / T, repetition penalty; the first maximum
   double bv = -INFINITY;
   int bi = -1;
-  for (int i = tid; i < V; i += kT) {
-    double v = static_cast<double>(lg[i]) / p.temperature;
-    if (pen && ((bitmap[i >> 5] >> (i & 31)) & 1u)) v = v > 0.0 ? v / p.repetition_penalty : v * p.repetition_penalty;
-    X[i] = v;
-    if (bi < 0 || v > bv) { bv = v; bi = i; }
+  for (int base = tid; base < V; base += kB * kT) {
+    float lv[kB];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) lv[j] = base + j * kT < V ? lg[base + j * kT] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const int i = base + j * kT;
+      if (i >= V) break;
+      double v = static_cast<double>(lv[j]) / p.temperature;
+      if (pen && ((bitmap[i >> 5] >> (i & 31)) & 1u))
+        v = v > 0.0 ? v / p.repetition_penalty : v * p.repetition_penalty;
+      X[i] = v;
+      if (bi < 0 || v > bv) { bv = v; bi = i; }
+    }
   }
   double m;
   int amax;
   block_argmax(bv, bi, sm, m, amax);   // its barriers also publish X
 
   uint64_t kkey = 0;
-  if (p.top_k > 0 && p.top_k < V) kkey = kth_key(X, V, static_cast<uint32_t>(p.top_k), sm);
+  if (p.top_k > 0 && p.top_k < V) kkey = kth_key(X, V, static_cast<uint32_t>(p.top_k), sm, cand);
 
   const bool topp = p.top_p < 1.0;
   uint64_t t_ge = 0, t_tie = 0;
   uint32_t r_ties = 0;
   if (topp) {
     double s = 0.0;
-    for (int i = tid; i < V; i += kT) {
-      const double x = X[i];
-      const double e = okey(x) >= kkey ? exp(x - m) : 0.0;
-      E[i] = e;
-      s += e;
+    for (int base = tid; base < V; base += kB * kT) {
+      double xv[kB];
+#pragma unroll
+      for (int j = 0; j < kB; ++j) xv[j] = base + j * kT < V ? X[base + j * kT] : 0.0;
+#pragma unroll
+      for (int j = 0; j < kB; ++j) {
+        const int i = base + j * kT;
+        if (i >= V) break;
+        const double e = okey(xv[j]) >= kkey ? exp(xv[j] - m) : 0.0;
+        E[i] = e;
+        s += e;
+      }
     }
     const double S = block_sum(s, sm);   // barriers publish E
-    top_p_bound(X, E, V, S, p.top_p, m, sm);
+    top_p_bound(X, E, V, S, p.top_p, m, sm, cand);
     t_ge = sm.t_ge;
     t_tie = sm.t_tie;
     r_ties = sm.r_ties;
@@ -277,12 +374,25 @@ __global__ void __launch_bounds__(kT, 1)
   // the draw: warp w owns [w * seg, (w + 1) * seg)
   const int seg = ((V + kW - 1) / kW + 31) & ~31;
   const int lo = w * seg, hi = min(V, lo + seg);
+  // kB chunks of 32 consecutive elements per batch, loads first
+  double xv[kB], ev[kB];
+  auto load = [&](int b0) {
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const int i = b0 + j * 32 + lane;
+      xv[j] = i < hi ? X[i] : 0.0;
+      ev[j] = (topp && i < hi) ? E[i] : 0.0;
+    }
+  };
   if (topp && r_ties) {
     uint32_t c = 0;
-    for (int i0 = lo; i0 < hi; i0 += 32) {
-      const int i = i0 + lane;
-      const bool tie = i < hi && okey(X[i]) == t_tie;
-      c += __popc(__ballot_sync(0xffffffffu, tie));
+    for (int b0 = lo; b0 < hi; b0 += kB * 32) {
+      load(b0);
+#pragma unroll
+      for (int j = 0; j < kB; ++j) {
+        const bool tie = b0 + j * 32 + lane < hi && okey(xv[j]) == t_tie;
+        c += __popc(__ballot_sync(0xffffffffu, tie));
+      }
     }
     if (lane == 0) sm.tie_cnt[w] = c;
     __syncthreads();
@@ -292,25 +402,29 @@ __global__ void __launch_bounds__(kT, 1)
     }
     __syncthreads();
   }
-  auto mass = [&](int i, bool valid, uint32_t &ties) -> double {
-    double e = 0.0;
-    uint64_t key = 0;
-    double x = 0.0;
-    if (valid) { x = X[i]; key = okey(x); }
+  // the kept mass of element i (ties ranked in index order across the warp)
+  auto mass = [&](int i, double x, double e_topp, uint32_t &ties) -> double {
+    const bool valid = i < hi;
+    const uint64_t key = okey(x);
     const bool tie = valid && topp && r_ties && key == t_tie;
     const unsigned bal = __ballot_sync(0xffffffffu, tie);
     const uint32_t rank = ties + __popc(bal & ((1u << lane) - 1u));
     ties += __popc(bal);
+    double e = 0.0;
     if (valid) {
       const bool keep = !topp || key >= t_ge || (tie && rank < r_ties) || i == amax;
-      if (keep) e = topp ? E[i] : (key >= kkey ? exp(x - m) : 0.0);
+      if (keep) e = topp ? e_topp : (key >= kkey ? exp(x - m) : 0.0);
     }
     return e;
   };
   {
     uint32_t ties = (topp && r_ties) ? sm.tie_base[w] : 0u;
     double s = 0.0;
-    for (int i0 = lo; i0 < hi; i0 += 32) s += mass(i0 + lane, i0 + lane < hi, ties);
+    for (int b0 = lo; b0 < hi; b0 += kB * 32) {
+      load(b0);
+#pragma unroll
+      for (int j = 0; j < kB; ++j) s += mass(b0 + j * 32 + lane, xv[j], ev[j], ties);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (lane == 0) sm.seg[w] = s;
@@ -343,20 +457,25 @@ __global__ void __launch_bounds__(kT, 1)
     double base = sm.pick_base;
     const double target = sm.total;
     int pick = -1, last = -1;
-    for (int i0 = lo; i0 < hi && pick < 0; i0 += 32) {
-      const int i = i0 + lane;
-      const double e = mass(i, i < hi, ties);
-      double inc = e;   // inclusive scan in index order
+    for (int b0 = lo; b0 < hi && pick < 0; b0 += kB * 32) {
+      load(b0);
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const double t = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += t;
+      for (int j = 0; j < kB; ++j) {
+        const int i0 = b0 + j * 32;
+        if (pick >= 0 || i0 >= hi) break;
+        const double e = mass(i0 + lane, xv[j], ev[j], ties);
+        double inc = e;   // inclusive scan in index order
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const double t = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += t;
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, e > 0.0 && base + inc > target);
+        const unsigned pos = __ballot_sync(0xffffffffu, e > 0.0);
+        if (hit) pick = i0 + __ffs(hit) - 1;
+        else if (pos) last = i0 + 31 - __clz(pos);
+        base += __shfl_sync(0xffffffffu, inc, 31);
       }
-      const unsigned hit = __ballot_sync(0xffffffffu, e > 0.0 && base + inc > target);
-      const unsigned pos = __ballot_sync(0xffffffffu, e > 0.0);
-      if (hit) pick = i0 + __ffs(hit) - 1;
-      else if (pos) last = i0 + 31 - __clz(pos);
-      base += __shfl_sync(0xffffffffu, inc, 31);
     }
     if (lane == 0) out[r] = pick >= 0 ? pick : (last >= 0 ? last : amax);
   }
@@ -379,12 +498,12 @@ extern "C" int q3_sample_logits(const q3_view *logits, const q3_sample_row *para
       l.row_bytes < static_cast<int32_t>(4 * l.cols) || l.rows > 65535)
     return Q3_ERR_SHAPE;
   if (workspace_bytes < q3_sample_workspace_bytes(l.rows, l.cols) || !workspace) return Q3_ERR_CAPACITY;
-  const size_t smem = 4 * ((l.cols + 31) / 32);
-  if (smem > 160 * 1024) return Q3_ERR_SHAPE;
+  const size_t smem = 4 * (((l.cols + 31) / 32 + 1) & ~1u) + 16 * static_cast<size_t>(kCap);
+  if (smem > 200 * 1024) return Q3_ERR_SHAPE;
   static bool attr = false;
   if (!attr) {
     const cudaError_t e = cudaFuncSetAttribute(k_sample_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               160 * 1024);
+                                               200 * 1024);
     if (e != cudaSuccess) { q3h::set_cuda_error(e); return Q3_ERR_CUDA; }
     attr = true;
   }
