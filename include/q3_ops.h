@@ -376,6 +376,22 @@ int q3_sample_logits(const q3_view *logits, const q3_sample_row *params, const i
 /* The first n draws of np.random.default_rng(seed).random() (host). */
 int q3_rng_uniforms(uint64_t seed, uint32_t n, double *out);
 
+/* ---- tokenizer (tools/tokenizer.py:39-192), host only ---------------------
+ * The byte-level BPE of an HF tokenizer.json: added tokens matched literally
+ * (leftmost-longest), the GPT-2 style pretokenizer split, byte symbols merged
+ * by rank.  Text is UTF-8.  encode/decode report the needed size in *n_ids /
+ * *n_bytes and return Q3_ERR_CAPACITY when `cap` is smaller; an id or symbol
+ * outside the vocabulary, or malformed input, gives Q3_ERR_SHAPE.  Decoding
+ * replaces invalid UTF-8 as Python's errors="replace" does.  eos_id is the id
+ * of <|im_end|> (151645 when the file has none). */
+int q3_tokenizer_load(const char *tokenizer_json, void **tokenizer);
+int q3_tokenizer_encode(const void *tokenizer, const char *text, size_t text_bytes, int32_t *ids,
+                        uint32_t cap, uint32_t *n_ids);
+int q3_tokenizer_decode(const void *tokenizer, const int32_t *ids, uint32_t n, char *text,
+                        size_t cap, size_t *n_bytes);
+int32_t q3_tokenizer_eos_id(const void *tokenizer);
+int q3_tokenizer_destroy(void *tokenizer);
+
 /* ---- tensor-parallel batched decode (extension) ---------------------------
  * The batched decode step split over `world` GPUs of one node, one process per
  * GPU.  The reference runs one hart and has no such split; this follows its

@@ -110,6 +110,13 @@ SIGS = {
     "q3_sample_logits": [VP, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                          C.c_void_p],
     "q3_rng_uniforms": [C.c_uint64, C.c_uint32, C.POINTER(C.c_double)],
+    "q3_tokenizer_load": [C.c_char_p, C.POINTER(C.c_void_p)],
+    "q3_tokenizer_encode": [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_int32), C.c_uint32,
+                            C.POINTER(C.c_uint32)],
+    "q3_tokenizer_decode": [C.c_void_p, C.POINTER(C.c_int32), C.c_uint32, C.c_char_p, C.c_size_t,
+                            C.POINTER(C.c_size_t)],
+    "q3_tokenizer_eos_id": [C.c_void_p],
+    "q3_tokenizer_destroy": [C.c_void_p],
     "q3_exp_rows": [VP, VP, C.c_void_p],
     "q3_exp2_rows": [VP, VP, C.c_void_p],
     "q3_last_cuda_error": [],
@@ -120,7 +127,7 @@ SIGS = {
     "q3_timer_detach": [],
 }
 RESTYPE = {"q3_gemm_nt_group_argmax_workspace_bytes": C.c_size_t,
-           "q3_sample_workspace_bytes": C.c_size_t,
+           "q3_sample_workspace_bytes": C.c_size_t, "q3_tokenizer_eos_id": C.c_int32,
            "q3_forward_workspace_bytes": C.c_size_t, "q3_decode_workspace_bytes": C.c_size_t,
            "q3_prefill_workspace_bytes": C.c_size_t,
            "q3_last_cuda_error": C.c_char_p, "q3_launch_count": C.c_uint64}

@@ -25,99 +25,9 @@
 #include <cuda_fp16.h>
 
 #include "q3_common.cuh"
+#include "q3_json.h"
 
 namespace {
-
-// ------------------------------------------------------------ JSON (header)
-struct JVal {
-  enum Kind { NUL, NUM, STR, ARR, OBJ, BOOL } kind = NUL;
-  double num = 0;
-  std::string str;
-  std::vector<JVal> arr;
-  std::vector<std::pair<std::string, JVal>> obj;
-  const JVal *get(const char *k) const {
-    for (const auto &kv : obj)
-      if (kv.first == k) return &kv.second;
-    return nullptr;
-  }
-};
-
-struct JParser {
-  const char *p, *end;
-  bool ok = true;
-  void ws() { while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p; }
-  bool lit(const char *s) {
-    const size_t n = strlen(s);
-    if (static_cast<size_t>(end - p) >= n && !memcmp(p, s, n)) { p += n; return true; }
-    return false;
-  }
-  std::string string() {
-    std::string out;
-    if (p >= end || *p != '"') { ok = false; return out; }
-    ++p;
-    while (p < end && *p != '"') {
-      if (*p == '\\' && p + 1 < end) {
-        ++p;
-        const char c = *p++;
-        if (c == 'u') { p += 4; out += '?'; }          // not used by tensor names
-        else out += (c == 'n' ? '\n' : c == 't' ? '\t' : c);
-      } else {
-        out += *p++;
-      }
-    }
-    if (p >= end) { ok = false; return out; }
-    ++p;
-    return out;
-  }
-  JVal value(int depth = 0) {
-    JVal v;
-    ws();
-    if (p >= end || depth > 16) { ok = false; return v; }
-    if (*p == '{') {
-      v.kind = JVal::OBJ;
-      ++p;
-      ws();
-      if (p < end && *p == '}') { ++p; return v; }
-      while (ok) {
-        ws();
-        std::string k = string();
-        ws();
-        if (p >= end || *p != ':') { ok = false; break; }
-        ++p;
-        v.obj.emplace_back(std::move(k), value(depth + 1));
-        ws();
-        if (p < end && *p == ',') { ++p; continue; }
-        if (p < end && *p == '}') { ++p; break; }
-        ok = false;
-      }
-    } else if (*p == '[') {
-      v.kind = JVal::ARR;
-      ++p;
-      ws();
-      if (p < end && *p == ']') { ++p; return v; }
-      while (ok) {
-        v.arr.push_back(value(depth + 1));
-        ws();
-        if (p < end && *p == ',') { ++p; continue; }
-        if (p < end && *p == ']') { ++p; break; }
-        ok = false;
-      }
-    } else if (*p == '"') {
-      v.kind = JVal::STR;
-      v.str = string();
-    } else if (lit("true") || lit("false")) {
-      v.kind = JVal::BOOL;
-    } else if (lit("null")) {
-      v.kind = JVal::NUL;
-    } else {
-      char *e = nullptr;
-      v.num = strtod(p, &e);
-      if (e == p) ok = false;
-      else { v.kind = JVal::NUM; p = e; }
-    }
-    return v;
-  }
-};
 
 struct Tensor {
   int dtype = -1;                 // 0 F32, 1 BF16, 2 F16
@@ -138,19 +48,19 @@ struct SafeTensors {
     if (fread(&h[0], 1, hlen, f) != hlen) return Q3_ERR_SHAPE;
     if (fseeko(f, 0, SEEK_END)) return Q3_ERR_SHAPE;
     const uint64_t fsize = static_cast<uint64_t>(ftello(f));
-    JParser jp{h.data(), h.data() + h.size()};
-    JVal root = jp.value();
-    if (!jp.ok || root.kind != JVal::OBJ) return Q3_ERR_SHAPE;
+    q3json::Parser jp{h.data(), h.data() + h.size()};
+    q3json::Value root = jp.value();
+    if (!jp.ok || root.kind != q3json::Value::OBJ) return Q3_ERR_SHAPE;
     for (const auto &kv : root.obj) {
       if (kv.first == "__metadata__") continue;
-      const JVal *dt = kv.second.get("dtype"), *sh = kv.second.get("shape"),
+      const q3json::Value *dt = kv.second.get("dtype"), *sh = kv.second.get("shape"),
                  *of = kv.second.get("data_offsets");
-      if (!dt || !sh || !of || dt->kind != JVal::STR || sh->kind != JVal::ARR ||
-          of->kind != JVal::ARR || of->arr.size() != 2)
+      if (!dt || !sh || !of || dt->kind != q3json::Value::STR || sh->kind != q3json::Value::ARR ||
+          of->kind != q3json::Value::ARR || of->arr.size() != 2)
         return Q3_ERR_SHAPE;
       Tensor x;
       x.dtype = dt->str == "F32" ? 0 : dt->str == "BF16" ? 1 : dt->str == "F16" ? 2 : -1;
-      for (const JVal &d : sh->arr) x.shape.push_back(static_cast<uint64_t>(d.num));
+      for (const q3json::Value &d : sh->arr) x.shape.push_back(static_cast<uint64_t>(d.num));
       x.begin = 8 + hlen + static_cast<uint64_t>(of->arr[0].num);
       x.end = 8 + hlen + static_cast<uint64_t>(of->arr[1].num);
       uint64_t n = x.dtype < 0 ? 0 : (x.dtype == 0 ? 4 : 2);
