@@ -500,13 +500,10 @@ extern "C" int q3_sample_logits(const q3_view *logits, const q3_sample_row *para
   if (workspace_bytes < q3_sample_workspace_bytes(l.rows, l.cols) || !workspace) return Q3_ERR_CAPACITY;
   const size_t smem = 4 * (((l.cols + 31) / 32 + 1) & ~1u) + 16 * static_cast<size_t>(kCap);
   if (smem > 200 * 1024) return Q3_ERR_SHAPE;
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(k_sample_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               200 * 1024);
-    if (e != cudaSuccess) { q3h::set_cuda_error(e); return Q3_ERR_CUDA; }
-    attr = true;
-  }
+  // per device (the attribute belongs to the current device's context)
+  const cudaError_t e = cudaFuncSetAttribute(k_sample_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+  if (e != cudaSuccess) { q3h::set_cuda_error(e); return Q3_ERR_CUDA; }
   k_sample_rows<<<l.rows, kT, smem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const float *>(l.data), l.row_bytes / 4, static_cast<int>(l.cols), params, generated,
       out_ids, static_cast<double *>(workspace));
