@@ -68,6 +68,9 @@ def parse():
                     help="time the device sampler (q3_sample_logits) on rows x vocab 151936 "
                          "logits next to the numpy sampler of tools/engine.py on the host")
     ap.add_argument("--sample-rows", type=int, default=64)
+    ap.add_argument("--convert-microbench", action="store_true",
+                    help="time the blob producer (q3_blob_from_safetensors) on a full-shape "
+                         "synthetic BF16 checkpoint next to the numpy converter restatement")
     ap.add_argument("--gemm-ms", default="512,4096,65536")
     ap.add_argument("--gemm-modes", default="qkv,o,gateup,down,lmhead,vquant,qnormrope")
     ap.add_argument("--gemm-reps", type=int, default=5)
@@ -681,10 +684,64 @@ def run_sample_microbench(args) -> None:
         raise RuntimeError("device status")
 
 
+def run_convert_microbench(args) -> None:
+    """A Qwen3-0.6B-shaped checkpoint (28 layers, vocab 151936, BF16, seeded
+    random weights of magnitude 2^-7..2^-5; tests/golden/hf_synth.py, fast form)
+    is written to a temporary
+    directory (so it sits in the page cache); the device conversion into a
+    fresh blob is timed end to end on the host clock (file reads, copies,
+    quantisation, synchronous).  The host figure is the numpy restatement of
+    tools/convert_pqwf.py (oracle/convert.py) converting the same file (one
+    thread of numpy, the file in the page cache)."""
+    import shutil
+    import tempfile
+
+    import torch
+    sys.path.insert(0, str(REPO))
+    sys.path.insert(0, str(REPO / "tests" / "golden"))
+    import __graft_entry__ as ge
+    q3 = ge.load_package()
+    from hf_synth import write_hf_model
+    from oracle import convert
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    tmp = Path(tempfile.mkdtemp())
+    try:
+        t0 = time.perf_counter()
+        mdir = write_hf_model(tmp / "m", layers=28, vocab=151936, seed=1, fast=True)
+        t_write = time.perf_counter() - t0
+        nbytes = (mdir / "model.safetensors").stat().st_size
+        BM = q3.model.BlobModel
+        BM.from_checkpoint(mdir, layers=2, vocab=1024)          # warm-up (CUDA context, pinned pool)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        bm = BM.from_checkpoint(mdir)
+        torch.cuda.synchronize(dev)
+        t_dev = time.perf_counter() - t0
+        ok = q3._lib.lib().q3_device_status() == 0
+        t0 = time.perf_counter()
+        ref = convert.convert(mdir, bm.off, 28, 151936, 256)
+        t_host = time.perf_counter() - t0
+        # the weight regions must be the same bytes (the RoPE tables may differ in the last bit)
+        regs = convert.regions(bm.off, 28, 151936, 1024, 256, 64)
+        same = all(bm.blob[s0:e0].cpu().numpy().tobytes() == bytes(ref[s0:e0])
+                   for k, (s0, e0) in regs.items() if k not in ("cos", "sin"))
+        print(json.dumps({"convert": "safetensors -> blob", "layers": 28, "vocab": 151936,
+                          "checkpoint_bytes": nbytes, "device_s": round(t_dev, 3),
+                          "device_gbs": round(nbytes / t_dev / 1e9, 2),
+                          "host_numpy_s": round(t_host, 1), "weights_equal_numpy": same,
+                          "write_checkpoint_s": round(t_write, 1), "device_status_ok": ok,
+                          "blob_bytes": bm.off["kSCRATCH_END"]}), flush=True)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 if __name__ == "__main__":
     a = parse()
     if a.gemm_microbench:
         run_gemm_microbench(a)
+    elif a.convert_microbench:
+        run_convert_microbench(a)
     elif a.sample_microbench:
         run_sample_microbench(a)
     elif a.impl == "reference":

@@ -23,9 +23,14 @@ def _bf16(x: np.ndarray) -> np.ndarray:
 
 
 def write_hf_model(out_dir: str | Path, layers: int = 2, vocab: int = 1024, seed: int = 3,
-                   tied: bool = False, poison: bool = False) -> Path:
+                   tied: bool = False, poison: bool = False, fast: bool = False) -> Path:
     """``tied``: no lm_head.weight (the converters fall back to the embedding).
-    ``poison``: a NaN, an infinity and an all-zero row in layer 0's q_proj."""
+    ``poison``: a NaN, an infinity and an all-zero row in layer 0's q_proj.
+    ``fast``: every weight matrix BF16 with random bit patterns of magnitude
+    2^-7 .. 2^-5 and random sign (for timing full-size conversions; seconds
+    instead of minutes to write)."""
+    if fast:
+        return _write_fast(Path(out_dir), layers, vocab, seed)
     out = Path(out_dir)
     out.mkdir(parents=True, exist_ok=True)
     rng = np.random.default_rng(seed)
@@ -81,6 +86,44 @@ def write_hf_model(out_dir: str | Path, layers: int = 2, vocab: int = 1024, seed
         f.write(hj)
         for raw in blobs:
             f.write(raw)
+    cfg = dict(DIMS, vocab_size=vocab, num_hidden_layers=layers)
+    (out / "config.json").write_text(json.dumps(cfg))
+    return out
+
+
+def _write_fast(out: Path, layers: int, vocab: int, seed: int) -> Path:
+    out.mkdir(parents=True, exist_ok=True)
+    rng = np.random.default_rng(seed)
+    H, I, HD = DIMS["hidden_size"], DIMS["intermediate_size"], DIMS["head_dim"]
+    QW, KW = DIMS["num_attention_heads"] * HD, DIMS["num_key_value_heads"] * HD
+    shapes = [("model.embed_tokens.weight", (vocab, H))]
+    for i in range(layers):
+        p = f"model.layers.{i}."
+        shapes += [(p + "self_attn.q_proj.weight", (QW, H)), (p + "self_attn.k_proj.weight", (KW, H)),
+                   (p + "self_attn.v_proj.weight", (KW, H)), (p + "self_attn.o_proj.weight", (H, QW)),
+                   (p + "mlp.gate_proj.weight", (I, H)), (p + "mlp.up_proj.weight", (I, H)),
+                   (p + "mlp.down_proj.weight", (H, I)), (p + "input_layernorm.weight", (H,)),
+                   (p + "self_attn.q_norm.weight", (HD,)), (p + "self_attn.k_norm.weight", (HD,)),
+                   (p + "post_attention_layernorm.weight", (H,))]
+    shapes += [("model.norm.weight", (H,)), ("lm_head.weight", (vocab, H))]
+    header, off = {}, 0
+    for name, shape in shapes:
+        n = 2 * int(np.prod(shape))
+        header[name] = {"dtype": "BF16", "shape": list(shape), "data_offsets": [off, off + n]}
+        off += n
+    hj = json.dumps(header).encode()
+    hj += b" " * ((8 - len(hj) % 8) % 8)
+    with open(out / "model.safetensors", "wb") as f:
+        f.write(struct.pack("<Q", len(hj)))
+        f.write(hj)
+        for name, shape in shapes:
+            n = int(np.prod(shape))
+            if len(shape) == 1:     # norm weights near 1
+                bits = rng.integers(0x3F70, 0x3F90, n, dtype=np.uint16)
+            else:                   # exponent 2^-7 .. 2^-5, random mantissa and sign
+                bits = rng.integers(0x3C00, 0x3D00, n, dtype=np.uint16)
+                bits |= (rng.integers(0, 2, n, dtype=np.uint16) << 15).astype(np.uint16)
+            f.write(bits.tobytes())
     cfg = dict(DIMS, vocab_size=vocab, num_hidden_layers=layers)
     (out / "config.json").write_text(json.dumps(cfg))
     return out
