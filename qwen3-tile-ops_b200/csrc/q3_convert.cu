@@ -58,13 +58,30 @@ struct SafeTensors {
       if (!dt || !sh || !of || dt->kind != q3json::Value::STR || sh->kind != q3json::Value::ARR ||
           of->kind != q3json::Value::ARR || of->arr.size() != 2)
         return Q3_ERR_SHAPE;
+      // every size is a non-negative integer (no wrap-around into the header)
+      auto count = [](const q3json::Value &v, uint64_t &out) {
+        if (v.kind != q3json::Value::NUM || !(v.num >= 0.0) || v.num > 9007199254740992.0 ||
+            v.num != static_cast<double>(static_cast<uint64_t>(v.num)))
+          return false;
+        out = static_cast<uint64_t>(v.num);
+        return true;
+      };
       Tensor x;
       x.dtype = dt->str == "F32" ? 0 : dt->str == "BF16" ? 1 : dt->str == "F16" ? 2 : -1;
-      for (const q3json::Value &d : sh->arr) x.shape.push_back(static_cast<uint64_t>(d.num));
-      x.begin = 8 + hlen + static_cast<uint64_t>(of->arr[0].num);
-      x.end = 8 + hlen + static_cast<uint64_t>(of->arr[1].num);
+      for (const q3json::Value &d : sh->arr) {
+        uint64_t v;
+        if (!count(d, v) || v > (1ull << 40)) return Q3_ERR_SHAPE;
+        x.shape.push_back(v);
+      }
+      uint64_t a, b;
+      if (!count(of->arr[0], a) || !count(of->arr[1], b)) return Q3_ERR_SHAPE;
+      x.begin = 8 + hlen + a;
+      x.end = 8 + hlen + b;
       uint64_t n = x.dtype < 0 ? 0 : (x.dtype == 0 ? 4 : 2);
-      for (uint64_t d : x.shape) n *= d;
+      for (uint64_t d : x.shape) {
+        if (d && n > UINT64_MAX / d) return Q3_ERR_SHAPE;
+        n *= d;
+      }
       if (x.end < x.begin || x.end > fsize || (x.dtype >= 0 && x.end - x.begin != n))
         return Q3_ERR_SHAPE;
       t[kv.first] = x;
