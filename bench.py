@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""bench.py — Qwen3-0.6B w8a8 greedy decode throughput on B200.
+"""bench.py — Qwen3-0.6B w8a8 greedy decode throughput on B200 (batched paged decode).
 
 Workload (one "step"): one greedy decode token for each of 64 sequences whose
 2048-token prefixes already sit in the paged int8 KV cache (32-token pages,
@@ -15,8 +15,8 @@ L2 flush is needed between steps.
 
 N > 1 (one process per GPU, torchrun env): the headline is data-parallel, an
 independent 64-sequence batch per GPU with no collective (weak scaling).  The
-same line carries a ``tp`` object: BASELINE config 4's tensor-parallel run of
-ONE 64-sequence batch (``q3_tp_decode_step_batch``: KV heads, MLP groups and
+same line carries a ``tp`` object: the tensor-parallel run of ONE
+64-sequence batch (``q3_tp_decode_step_batch``: KV heads, MLP groups and
 vocabulary split over the ranks, O/down partials exchanged over NVLink inside
 the GEMM kernels; strong scaling).  ``--parallel tp`` swaps the two.
 ``--impl reference`` times the reference algorithm's CPU restatement (the
@@ -40,6 +40,8 @@ REPO = Path(__file__).resolve().parent
 METRIC = "Qwen3-0.6B w8a8 prefill & decode tokens/s at 1/2/4/8 B200; % int8/HBM roofline"
 SEQS, CTX, LAYERS, VOCAB = 64, 2048, 28, 151936
 KV_BYTES_PER_TOKEN_LAYER = 2 * 1024 + 2 * 8 * 4   # K+V int8 rows + f32 per-head scales
+LAYER_WEIGHT_BYTES = 15777792                       # int8 weights + f32 row scales of one layer
+LM_HEAD_BYTES = 151936 * 1024 + 151936 * 4          # int8 lm_head + f32 row scales
 # DRAM bytes (read + write) of one k_attention_decode launch at ctx 2048, 64 seqs, from
 # one ncu capture of this bench (--layers 2 --no-graph); the profile summary gives it
 ATT_TRAFFIC_BYTES = 281348352 + 4959744
@@ -57,6 +59,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config-5 prefill measurement reported under 'prefill'")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="only the batched prefill measurement (one JSON line; with --layers 1 "
+                         "the small case the prefill profiles are captured on)")
+    ap.add_argument("--no-single", action="store_true",
+                    help="skip the batch-1 q3_generate measurement reported under 'single_sequence'")
     ap.add_argument("--prefill-seqs", type=int, default=16)
     ap.add_argument("--prefill-len", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -139,6 +146,28 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def family_times(lib, family: str, run, stream, dev, capacity: int = 512) -> list:
+    """Run ``run()`` once (eager) with CUDA events recorded around every
+    launch of one kernel family ("attention", "gemm", "exchange") on its own
+    stream; returns each launch's milliseconds."""
+    import torch
+    ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(capacity)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(capacity)]
+    for e in ev_s + ev_e:
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    hs = (C.c_void_p * capacity)(*[e.cuda_event for e in ev_s])
+    he = (C.c_void_p * capacity)(*[e.cuda_event for e in ev_e])
+    q3c = lib.q3_timer_attach(family.encode(), hs, he, capacity)
+    if q3c != 0:
+        raise RuntimeError(f"q3_timer_attach({family}) = {q3c}")
+    with torch.cuda.stream(stream):
+        run()
+    torch.cuda.synchronize(dev)
+    used = lib.q3_timer_detach()
+    return [ev_s[i].elapsed_time(ev_e[i]) for i in range(used)]
+
+
 def measure_decode(args, q3, lib, dev, rank, world, dist, mode: str) -> dict:
     """Time K graph-replayed decode steps of config 4.
 
@@ -151,7 +180,7 @@ def measure_decode(args, q3, lib, dev, rank, world, dist, mode: str) -> dict:
     from q3b200.model import Dims
 
     B, K, W = args.seqs, args.steps, args.warmup
-    max_seq = ((args.ctx + W + 2 * K + 2 + 31) // 32) * 32
+    max_seq = ((args.ctx + W + 2 * K + 8 + 31) // 32) * 32   # + the eager family-timing steps
     dims = Dims(layers=args.layers, vocab=VOCAB, max_seq=max_seq)
     rseed = rank if mode == "replicas" else 0
     bm = synthetic.random_blob_model(dims, seed=1000 + rseed, device=dev)
@@ -192,16 +221,6 @@ def measure_decode(args, q3, lib, dev, rank, world, dist, mode: str) -> dict:
             step(stream)
             advance()
     torch.cuda.synchronize(dev)
-
-    # attention launches of one step are timed live with CUDA events
-    n_ev = args.layers
-    ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    for e in ev_s + ev_e:
-        e.record(stream)
-    torch.cuda.synchronize(dev)
-    hs = (C.c_void_p * n_ev)(*[e.cuda_event for e in ev_s])
-    he = (C.c_void_p * n_ev)(*[e.cuda_event for e in ev_e])
 
     use_graph = not args.no_graph
     graph = None
@@ -246,15 +265,14 @@ def measure_decode(args, q3, lib, dev, rank, world, dist, mode: str) -> dict:
     if dist:
         dist.barrier()
     ms = t0.elapsed_time(t1)
-    # the attention kernels alone (roofline): one eager step with events around
-    # each attention launch, on the stream they are launched on
-    lib.q3_timer_attach(b"attention", hs, he, n_ev)
-    with torch.cuda.stream(stream):
-        step(stream)
-    torch.cuda.synchronize(dev)
-    lib.q3_timer_detach()
-    advance()
-    att_ms = [a.elapsed_time(b) for a, b in zip(ev_s, ev_e)]
+    # kernel families alone: one eager step per family with CUDA events around
+    # each of its launches, on the stream they are launched on (the attention
+    # launches give the roofline; the families' sums the per-step breakdown)
+    fam = {}
+    for name in ("attention", "gemm", "exchange"):
+        fam[name] = family_times(lib, name, lambda: step(stream), stream, dev)
+        advance()
+    att_ms = fam["attention"]
     att_avg = sum(att_ms) / len(att_ms)
 
     # e2e: host feeds ids/pos from pinned memory and reads the next ids back
@@ -287,16 +305,122 @@ def measure_decode(args, q3, lib, dev, rank, world, dist, mode: str) -> dict:
     if status != 0:
         raise RuntimeError(f"device status {status} after the {mode} decode measurement")
 
+    sums = [sum(fam[k]) for k in ("attention", "gemm", "exchange")]
     if dist:
-        t = torch.tensor([ms, e2e_ms, att_avg], device=dev)
+        t = torch.tensor([ms, e2e_ms, att_avg] + sums, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, att_avg = float(t[0]), float(t[1]), float(t[2])
+        sums = [float(v) for v in t[3:]]
     if graph is not None:
         del graph
     if comm is not None:
         comm.close()
+    breakdown = {f"{k}_ms_per_step": round(v, 4) for k, v in zip(("attention", "gemm", "exchange"), sums)}
+    breakdown.update({f"{k}_launches_per_step": len(fam[k]) for k in fam})
     return {"ms": ms, "e2e_ms": e2e_ms, "att_avg": att_avg, "launches": int(launches_per_step),
+            "breakdown": breakdown,
             "clocks": ck, "graph": use_graph, "kv_heads": shard.kv_heads, "q_heads": shard.q_heads}
+
+
+def tp_parity(args, q3, lib, dev, rank, world, dist, steps: int = 3) -> dict:
+    """Bit-exactness of the tensor-parallel step, checked in the same run: a
+    seeded batch of ``args.seqs`` sequences (ragged contexts just below
+    ``args.ctx``) takes ``steps`` greedy steps through
+    q3_tp_decode_step_batch on every rank, and on rank 0 through
+    q3_decode_step_batch over the whole pool.  The ids of every step, the
+    residual stream x after the last step and the new K/V rows (+ scales) of
+    every layer are compared bit for bit (each rank's K/V columns against
+    the matching columns of the single-GPU pool)."""
+    import hashlib
+
+    import torch
+    from q3b200 import synthetic, tp
+    from q3b200.model import Dims
+    B = args.seqs
+    max_seq = ((args.ctx + steps + 31) // 32) * 32
+    dims = Dims(layers=args.layers, vocab=VOCAB, max_seq=max_seq)
+    bm = synthetic.random_blob_model(dims, seed=6000, device=dev)
+    max_pages = max_seq // 32
+    g = torch.Generator().manual_seed(6001)
+    tables = torch.randperm(B * max_pages, generator=g).reshape(B, max_pages).to(torch.int16)
+    tab = tables.to(dev)
+    ids0 = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32)
+    lens = torch.randint(max(1, args.ctx - 64), args.ctx, (B,), generator=g, dtype=torch.int32)
+    pidx = torch.tensor([int(tables[s, t // 32]) & 0xFFFF for s in range(B)
+                         for t in range(int(lens[s]), int(lens[s]) + steps)], device=dev)
+    sidx = torch.tensor([t % 32 for s in range(B)
+                         for t in range(int(lens[s]), int(lens[s]) + steps)], device=dev)
+    wsb = lib.q3_decode_workspace_bytes(C.byref(bm.L), B)
+    stream = torch.cuda.Stream(device=dev)
+
+    def digest(*ts):
+        h = hashlib.sha256()
+        for t in ts:
+            h.update(t.contiguous().cpu().numpy().tobytes())
+        return h.hexdigest()
+
+    def run(step_fn, pool):
+        cpool = pool.c()
+        ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+        ids, pos = ids0.to(dev), lens.to(dev)
+        nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+        out = []
+        for _ in range(steps):
+            with torch.cuda.stream(stream):
+                step_fn(cpool, ids, pos, nxt, ws)
+            torch.cuda.synchronize(dev)
+            out.append(nxt.clone())
+            ids.copy_(nxt)
+            pos.add_(1)
+        return torch.stack(out), ws[:B * 1024 * 4].clone()
+
+    def new_rows(pool, c0=None, c1=None):
+        rows = [t[:, pidx, sidx] for t in (pool.k, pool.v, pool.ks, pool.vs)]
+        if c0 is not None:
+            rows = [rows[0][..., c0 * 128:c1 * 128], rows[1][..., c0 * 128:c1 * 128],
+                    rows[2][..., c0:c1], rows[3][..., c0:c1]]
+        return digest(*rows)
+
+    sh = tp.shard_of(bm.L, rank, world)
+    pool = synthetic.KVPoolTensors(args.layers, B * max_pages, sh.kv_heads, device=dev)
+    pool.fill_random(seed=6002, head0=sh.kv_head0, total_heads=8)
+    comm = tp.TPComm(bm.L, rank, world, B)
+    try:
+        dist.barrier()
+        tp_ids, tp_x = run(lambda cp, i, p, n, w: comm.decode_step(
+            bm.blob, bm.L, cp, tab, max_pages, i, p, B, n, w, stream), pool)
+        status = int(lib.q3_device_status())
+        mine = {"ids": digest(tp_ids), "x": digest(tp_x), "kv": new_rows(pool),
+                "status": status, "kv_head0": sh.kv_head0, "kv_heads": sh.kv_heads}
+        dist.barrier()
+    finally:
+        comm.close()
+    del pool
+    torch.cuda.empty_cache()
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    res = None
+    if rank == 0:
+        full = synthetic.KVPoolTensors(args.layers, B * max_pages, 8, device=dev)
+        full.fill_random(seed=6002)
+        ref_ids, ref_x = run(lambda cp, i, p, n, w: q3._lib.check(
+            "q3_decode_step_batch", lib.q3_decode_step_batch(
+                bm.blob.data_ptr(), C.byref(bm.L), C.byref(cp), tab.data_ptr(), max_pages,
+                i.data_ptr(), p.data_ptr(), B, n.data_ptr(), w.data_ptr(), wsb,
+                stream.cuda_stream)), full)
+        ref_status = int(lib.q3_device_status())
+        rid, rx = digest(ref_ids), digest(ref_x)
+        res = {"ids_equal": all(e["ids"] == rid for e in every),
+               "x_bits_equal": all(e["x"] == rx for e in every),
+               "kv_equal": all(e["kv"] == new_rows(full, e["kv_head0"], e["kv_head0"] + e["kv_heads"])
+                               for e in every),
+               "status_clean": ref_status == 0 and all(e["status"] == 0 for e in every),
+               "seqs": B, "steps": steps, "layers": args.layers,
+               "against": "q3_decode_step_batch on one GPU, whole pool"}
+        del full
+        torch.cuda.empty_cache()
+    dist.barrier()
+    return res
 
 
 def run_ours(args) -> None:
@@ -317,15 +441,28 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local_rank)
     B, K, W = args.seqs, args.steps, args.warmup
 
+    if args.prefill_only:
+        pf = measure_prefill(args, q3, lib, dev, rank, world, dist)
+        if dist:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(pf), flush=True)
+        return
+
     # N > 1: data-parallel (independent sequences, no collective) is the
-    # throughput headline; the tensor-parallel step of BASELINE config 4 (the
+    # throughput headline; the tensor-parallel step of the decode workload (the
     # same 64 sequences split by KV heads) is measured in the same run
     if world == 1:
         mode = "tp" if args.parallel == "tp" else "single"
     else:
         mode = "tp" if args.parallel == "tp" else "replicas"
     dec = measure_decode(args, q3, lib, dev, rank, world, dist, mode)
-    second = None
+    second, parity = None, None
+    if world > 1:
+        # the tensor-parallel step must stay bit-identical to one GPU: checked
+        # in every multi-GPU run, outside the timed regions
+        torch.cuda.empty_cache()
+        parity = tp_parity(args, q3, lib, dev, rank, world, dist)
     if world > 1 and not args.no_second:
         torch.cuda.empty_cache()
         other = "replicas" if mode == "tp" else "tp"
@@ -337,14 +474,21 @@ def run_ours(args) -> None:
                                             "vocab-parallel argmax, ordered partial exchange "
                                             "over NVLink",
                              "attention_avg_launch_ms": round(r2["att_avg"], 4),
+                             "kernel_ms_per_step": r2["breakdown"],
+                             "tp_parity": parity,
                              "gpu_launches": r2["launches"] * K,
-                             "note": f"BASELINE config 4's tensor-parallel run: the same {B} "
+                             "note": f"tensor-parallel run of one batch: the same {B} "
                                      "sequences as one GPU, split over the ranks"})
         else:
             second = ("dp", {"value": round(world * B * K / (r2["ms"] * 1e-3), 1),
                              "unit": "tokens/s", "ms_per_step": round(r2["ms"] / K, 4),
+                             "kernel_ms_per_step": r2["breakdown"],
                              "scaling": "weak", "parallelism": f"data-parallel x{world}",
                              "note": f"an independent {B}-sequence batch per GPU, no collective"})
+    single = None
+    if world == 1 and not args.no_single:
+        torch.cuda.empty_cache()
+        single = measure_single_sequence(args, q3, lib, dev)
     prefill = None
     if not args.no_prefill:
         torch.cuda.empty_cache()
@@ -391,20 +535,100 @@ def run_ours(args) -> None:
                      "frac": round(achieved / peak_gbs, 4),
                      "traffic": int(ATT_TRAFFIC_BYTES * kvh / 8),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one "
-                                       "launch at ctx 2048, 8 KV heads "
-                                       "(profiles/attention_decode_config4.md)"
+                                       "launch at ctx 2048, 8 KV heads, 64 sequences"
                                        + ("" if kvh == 8 else f", scaled by {kvh}/8 heads"),
                      "avg_launch_ms": round(dec["att_avg"], 4), "bytes_per_launch": att_bytes,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650"},
         "clocks": dec["clocks"],
+        "kernel_ms_per_step": dec["breakdown"],
     }
+    if not tp:
+        # whole decode step against HBM: weights once + every sequence's KV
+        # prefix (all layers) + the new K/V rows, per GPU
+        kv_avg = args.ctx + W + (K + 1) / 2.0
+        step_bytes = (args.layers * LAYER_WEIGHT_BYTES + LM_HEAD_BYTES
+                      + B * args.layers * KV_BYTES_PER_TOKEN_LAYER * (kv_avg + 1))
+        step_gbs = step_bytes / (ms / K * 1e-3) / 1e9
+        line["step_roofline"] = {
+            "bound": "hbm", "bytes_per_step": int(step_bytes), "achieved": round(step_gbs, 1),
+            "peak": peak_gbs, "unit": "GB/s", "frac": round(step_gbs / peak_gbs, 4),
+            "basis": "per GPU: 28 x 15,777,792 B layer weights + 156,190,208 B lm_head (+ scales) "
+                     "+ 2112 B per cached token per layer for every sequence + the new rows"}
+    if tp and parity is not None:
+        line["tp_parity"] = parity
     if second is not None:
         line[second[0]] = second[1]
     if prefill is not None:
         line["prefill"] = prefill
+    if single is not None:
+        line["single_sequence"] = single
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(args.ctx)
     print(json.dumps(line), flush=True)
+
+
+def measure_single_sequence(args, q3, lib, dev, gen: int = 64) -> dict:
+    """Batch-1 greedy decode through the drop-in greedy loop q3_generate (the
+    reference's main(): one blob, CTRL read once, every chunk asynchronous):
+    a 32-token seeded prompt, then ``gen`` + 1 greedy tokens against 1 token;
+    the difference of the two device times over ``gen`` is the time per
+    decoded token.  28 layers, vocab 151936, random-init weights."""
+    import numpy as np
+    import torch
+    from q3b200 import synthetic
+    from q3b200.model import Dims
+    n_prompt = 32
+    dims = Dims(layers=args.layers, vocab=VOCAB, max_seq=((n_prompt + gen + 1 + 31) // 32) * 32)
+    bm = synthetic.random_blob_model(dims, seed=7000, device=dev)
+    ids = [int(v) for v in np.random.default_rng(1).integers(0, VOCAB, n_prompt)]
+    stream = torch.cuda.Stream(device=dev)
+
+    def timed(n_gen):
+        bm.set_ids(ids + [0] * (n_gen))
+        bm.set_ctrl(n_prompt, n_gen, 0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            q3._lib.check("q3_generate", lib.q3_generate(
+                bm.blob.data_ptr(), C.byref(bm.L), bm.ws.data_ptr(), bm.ws.numel(),
+                stream.cuda_stream))
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1)
+
+    for _ in range(2):
+        timed(1)
+        timed(gen + 1)
+    t1 = min(timed(1) for _ in range(3))
+    tg = min(timed(gen + 1) for _ in range(3))
+    per_tok = (tg - t1) / gen
+    # end to end through the Python entry point: ids in from the host, CTRL,
+    # the loop, the generated ids back to the host
+    t = time.perf_counter()
+    out = bm.generate(ids, n_prompt, gen + 1, mode=0, stream=stream)
+    e2e_s = time.perf_counter() - t
+    if lib.q3_device_status() != 0 or len(out) != gen + 1:
+        raise RuntimeError("single-sequence decode failed")
+    kv_avg = n_prompt + 1 + gen / 2.0
+    tok_bytes = args.layers * LAYER_WEIGHT_BYTES + LM_HEAD_BYTES + \
+        args.layers * KV_BYTES_PER_TOKEN_LAYER * (kv_avg + 1)
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (
+        REPO / "MEASURED_PEAKS.json").exists() else {}
+    peak_gbs = float(peaks.get("hbm_gbs", 6650.0))
+    gbs = tok_bytes / (per_tok * 1e-3) / 1e9
+    return {"metric": "batch-1 greedy decode tokens/s (q3_generate)",
+            "value": round(1e3 / per_tok, 1), "unit": "tokens/s", "ms_per_token": round(per_tok, 4),
+            "config": {"workload": f"one sequence: {n_prompt}-token prompt then {gen + 1} greedy "
+                                   f"tokens, {args.layers} layers, vocab {VOCAB}",
+                       "timing": f"device time of q3_generate with {gen + 1} tokens minus with 1, "
+                                 f"over {gen}; best of 3"},
+            "e2e": {"value": round((gen + 1) / e2e_s, 1), "unit": "tokens/s",
+                    "note": "host clock around BlobModel.generate: ids host->device, the loop "
+                            "including the 32-token prompt, ids device->host"},
+            "roofline": {"bound": "hbm", "bytes_per_token": int(tok_bytes),
+                         "achieved": round(gbs, 1), "peak": peak_gbs, "unit": "GB/s",
+                         "frac": round(gbs / peak_gbs, 4)}}
 
 
 # config 5: 16 x 4096-token prompts, causal, 28 layers, vocab 151936
@@ -468,7 +692,7 @@ def measure_prefill(args, q3, lib, dev, rank, world, dist) -> dict:
 
 
 # ---------------------------------------------------------------------------
-# config 2: per-group w8a8 GEMM microbench (shapes of BASELINE configs[1])
+# per-group w8a8 GEMM microbench: the prefill-size GEMM shapes of the model
 # ---------------------------------------------------------------------------
 GEMM_SHAPES = {   # name: (K, N, group, epilogue)
     "qkv": (1024, 2048, 256, "store"), "o": (2048, 1024, 128, "add"),
@@ -570,6 +794,26 @@ def _oracle_setup(ctx: int, seqs: int):
     return O, w, kvs
 
 
+def host_numerics() -> dict:
+    """The host's numpy SIMD dispatch and BLAS threads (numpy's float32 exp2
+    and the BLAS kernels the port runs depend on them)."""
+    out = {"nproc": os.cpu_count()}
+    try:
+        from numpy._core._multiarray_umath import (__cpu_baseline__, __cpu_dispatch__,
+                                                    __cpu_features__)
+        out["numpy_simd_baseline"] = list(__cpu_baseline__)
+        out["numpy_simd_dispatch"] = [d for d in __cpu_dispatch__ if __cpu_features__.get(d)]
+    except ImportError:
+        pass
+    try:
+        import threadpoolctl
+        out["blas"] = [{"api": i.get("internal_api"), "threads": i.get("num_threads")}
+                       for i in threadpoolctl.threadpool_info()]
+    except ImportError:
+        pass
+    return out
+
+
 def cpu_baseline_sample(ctx: int) -> dict:
     O, w, kvs = _oracle_setup(ctx, 1)
     t = time.perf_counter()
@@ -579,7 +823,8 @@ def cpu_baseline_sample(ctx: int) -> dict:
     return {"value": round(1.0 / dt, 4), "unit": "tokens/s", "cores": os.cpu_count(),
             "kind": "port",
             "sample": f"1 sequence x 1 greedy decode step at context {ctx} (28 layers, vocab "
-                      f"151936), numpy oracle with BLAS on {os.cpu_count()} threads: {dt:.2f} s"}
+                      f"151936), numpy oracle with BLAS on {os.cpu_count()} threads: {dt:.2f} s",
+            "host": host_numerics()}
 
 
 def run_reference(args) -> None:
@@ -611,7 +856,8 @@ def run_reference(args) -> None:
                          "kind": "port",
                          "sample": f"per step 1 sequence x 1 greedy decode step at context "
                                    f"{args.ctx}+i (28 layers, vocab 151936), numpy oracle port of "
-                                   f"tools/ref_qwen3.py, BLAS on {os.cpu_count()} threads"},
+                                   f"tools/ref_qwen3.py, BLAS on {os.cpu_count()} threads",
+                         "host": host_numerics()},
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

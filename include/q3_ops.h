@@ -172,7 +172,8 @@ int q3_gemm_nt_group_argmax(const q3_view *a, const q3_view *a_scale,
  * every call.  More rows -> Q3_ERR_CAPACITY.  Each call clears the keys it
  * uses; calls that overlap on the GPU race on the array.  The first call on a
  * device looks the array's address up (cudaGetSymbolAddress) with that device
- * current: make it before any stream capture. */
+ * current, and so does the first call after the device's context changed (a
+ * device reset): make such a call before any stream capture. */
 #define Q3_NOALLOC_ARGMAX_MAX_ROWS 4096
 int q3_gemm_nt_group_argmax_noalloc(const q3_view *a, const q3_view *a_scale,
                                     const q3_view *b, const q3_view *b_scale,
@@ -435,6 +436,20 @@ int q3_tp_comm_create(const q3_layout *layout, int32_t rank, int32_t world,
 int q3_tp_comm_connect(void *comm, const void *handles);
 int q3_tp_comm_reset(void *comm, void *stream);
 int q3_tp_comm_destroy(void *comm);
+
+/* No counterpart in the reference (it runs on one NPU): failure detection of
+ * the exchange.  set_wait_ns sets how long this rank's kernels wait for a
+ * peer's signal before they give up, set device status bit 20 and return
+ * (default 2 s; 1 ms .. 60 s, else Q3_ERR_SHAPE).  inject_missing_signals
+ * raises this rank's expected signal count of one exchange buffer (0 = O
+ * partials, 1 = down partials, 2 = argmax keys) from `producer` by `count`,
+ * stream-ordered, exactly as if that producer had fallen behind: the next
+ * consumer of the buffer times out.  It exists to test the recovery path
+ * (timeout -> status bit 20 -> q3_tp_comm_reset -> clean step) without a
+ * peer process or a GPU fault. */
+int q3_tp_comm_set_wait_ns(void *comm, uint64_t ns);
+int q3_tp_comm_inject_missing_signals(void *comm, int32_t buf, int32_t producer,
+                                      uint32_t count, void *stream);
 
 /* One decode step of this rank (same arguments as q3_decode_step_batch; the
  * workspace size is q3_decode_workspace_bytes).  Every rank calls it with the

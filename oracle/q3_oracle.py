@@ -105,9 +105,15 @@ def quant_groups(x: np.ndarray, group: int) -> tuple[np.ndarray, np.ndarray]:
 # groups in order (ref_qwen3.py:145-158)
 # ---------------------------------------------------------------------------
 def int_dot_nt(a8: np.ndarray, b8: np.ndarray) -> np.ndarray:
-    """Exact int32 ``a8 @ b8.T`` for int8 operands (batched on leading dims)."""
-    out = np.matmul(a8.astype(np.float64), np.swapaxes(b8.astype(np.float64), -1, -2))
-    return np.rint(out).astype(np.int32)
+    """Exact int32 ``a8 @ b8.T`` for int8 operands (batched on leading dims).
+
+    With an inner dimension of at most 1024, every partial sum is an integer
+    of magnitude <= 1024 * 128^2 = 2^24, exact in float32 whatever order
+    (or fused multiply-adds) the BLAS uses; longer dots go through float64
+    (exact below 2^53)."""
+    ft = np.float32 if a8.shape[-1] <= 1024 else np.float64
+    out = np.matmul(a8.astype(ft), np.swapaxes(b8.astype(ft), -1, -2))
+    return out.astype(np.int32)
 
 
 def group_partials(a8: np.ndarray, w8: np.ndarray, group: int, chunk: int = 8192) -> np.ndarray:
@@ -377,6 +383,43 @@ def forward_chunk(model: Model, ids, kv: KV, pos: int, rows: int,
         if record is not None:
             record["logits"] = logits
     return logits
+
+
+def forward_prompt_rows(w: Model, ids, rows):
+    """forward_chunk of a one-layer model over a whole T-token prompt as one
+    chunk (ref_qwen3.py:366-444), evaluated past the K/V write only for the
+    prompt rows ``rows``: rows interact only through attention, which reads
+    the K/V of every row, so each selected row gets exactly its bits of the
+    full computation.  Returns (k8, ks, v8, vs) of every row, x of the
+    selected rows, and the logits of the last selected row."""
+    assert len(w.layers) == 1, "later layers need the x of every row"
+    L = w.layers[0]
+    H, HD = w.hidden, w.head_dim
+    T = len(ids)
+    inv_h = F(F(1.0) / F(H))
+    qk_scale = F(1.0 / np.sqrt(float(HD)))
+    ids = np.asarray(ids, np.int64)
+    x = (w.emb8[ids].astype(F) * w.emb_s[ids][:, None]).astype(F)
+    h = rmsnorm(x, L.n1, inv_h)
+    h8, hs = quant_groups(h, 256)
+    k = gemm_group(h8, hs, L.wk, L.wk_s, 256)
+    v = gemm_group(h8, hs, L.wv, L.wv_s, 256)
+    _, k8, ks = qk_norm_rope_quant(k, L.nk, w.cos[:T], w.sin[:T], w.kv_heads, HD)
+    v8, vs = quant_groups(v, HD)
+    r = np.asarray(rows)
+    q = gemm_group(h8[r], hs[r], L.wq, L.wq_s, 256)
+    _, q8, qs = qk_norm_rope_quant(q, L.nq, w.cos[r], w.sin[r], w.heads, HD)
+    attn = attention(q8, qs, k8, ks, v8, vs, r, w.heads, w.kv_heads, HD, qk_scale)
+    o8, os_ = quant_groups(attn, HD)
+    xr = (x[r] + gemm_group(o8, os_, L.wo, L.wo_s, HD)).astype(F)
+    h = rmsnorm(xr, L.n2, inv_h)
+    h8, hs = quant_groups(h, 256)
+    sw = swiglu(gemm_group(h8, hs, L.wg, L.wg_s, 256), gemm_group(h8, hs, L.wu, L.wu_s, 256))
+    s8, ss = quant_groups(sw, 256)
+    xr = (xr + gemm_group(s8, ss, L.wd, L.wd_s, 256)).astype(F)
+    hl = rmsnorm(xr[-1:], w.nf, inv_h)
+    h8l, hsl = quant_groups(hl, 256)
+    return (k8, ks, v8, vs), xr, gemm_group(h8l, hsl, w.lm8, w.lm_s, 256)
 
 
 def generate(model: Model, ids, n_prompt: int, n_gen: int, record: dict | None = None,

@@ -60,7 +60,7 @@ def _normal_q(rng, rows, cols):
 
 
 def build_model(shape: Shape, seed: int = 0) -> Model:
-    """The random-init model of BASELINE configs 1/3/4/5 (shape-dependent)."""
+    """The seeded random-init model of the parity and benchmark cases (shape-dependent)."""
     s = shape
     rng = np.random.default_rng(seed)
     nrng = np.random.default_rng(seed + 2)

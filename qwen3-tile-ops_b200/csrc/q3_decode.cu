@@ -412,6 +412,7 @@ int tp_decode(const q3::TpComm &c, char *bl, const q3_layout &L, const q3_kv_poo
       r.H = (int)H;
       r.h8 = w.h8;
       r.hs = w.hs;
+      r.wait_ns = c.wait_ns;
       return q3::tp_reduce_norm(r, st);
     };
     // O: partials of this rank's heads (one 128-wide K group each) -> every rank

@@ -18,9 +18,12 @@
 //    call uses it; each call zeroes the keys of its own rows first, but two
 //    calls that overlap on the GPU (for example on two streams) race on it;
 //  * the array's device address is looked up with cudaGetSymbolAddress on the
-//    first call made on each device, with that device current, and cached;
-//    make that first call before any stream capture.
+//    first call made on each device, with that device current, and cached
+//    together with the identity of the device's context; a call that finds a
+//    different context (after cudaDeviceReset, for example) looks it up again.
+//    Make the first call on a device before any stream capture.
 //  * nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+#include <cuda.h>
 #include <mutex>
 #include <stdio.h>
 
@@ -32,9 +35,38 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void *g_scratch[kMaxDevices] = {};
+struct Cached {
+  unsigned long long ctx_id;   // cuCtxGetId of the context the address belongs to
+  void *ptr;
+};
+Cached g_scratch[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device (looked up once).
+// Unique id of the calling thread's current CUDA context (false if none).
+// The driver functions are fetched through the runtime, so the library does
+// not link libcuda directly and still loads on a host without a GPU driver.
+bool current_context_id(unsigned long long *id) {
+  using GetCurrent = CUresult (*)(CUcontext *);
+  using GetId = CUresult (*)(CUcontext, unsigned long long *);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  if (!get_current || !get_id) {
+    void *f = nullptr, *g = nullptr;
+    cudaDriverEntryPointQueryResult q1, q2;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q1) != cudaSuccess ||
+        q1 != cudaDriverEntryPointSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &g, cudaEnableDefault, &q2) != cudaSuccess ||
+        q2 != cudaDriverEntryPointSuccess)
+      return false;
+    get_current = reinterpret_cast<GetCurrent>(f);
+    get_id = reinterpret_cast<GetId>(g);
+  }
+  CUcontext ctx = nullptr;
+  return get_current(&ctx) == CUDA_SUCCESS && ctx && get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of the scratch array in the current device's context.  The
+// lookup is cached per device and redone when the context changed: a device
+// reset unloads this module, and the array may come back at another address.
 int scratch_on_current_device(void **out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -42,18 +74,33 @@ int scratch_on_current_device(void **out) {
     q3h::set_cuda_error(e);
     return Q3_ERR_CUDA;
   }
-  if (dev < 0 || dev >= kMaxDevices) return Q3_ERR_CAPACITY;
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch[dev]) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_argmax_keys);
-    if (e != cudaSuccess || !p) {
-      q3h::set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
-      return Q3_ERR_CUDA;
-    }
-    g_scratch[dev] = p;
+  if (dev < 0 || dev >= kMaxDevices) {
+    char msg[128];
+    snprintf(msg, sizeof msg,
+             "q3_gemm_nt_group_argmax_noalloc: device %d is beyond the %d devices this entry "
+             "point serves", dev, kMaxDevices);
+    q3h::set_error_message(msg);
+    return Q3_ERR_CAPACITY;
   }
-  *out = g_scratch[dev];
+  std::lock_guard<std::mutex> lk(g_mu);
+  Cached &c = g_scratch[dev];
+  unsigned long long ctx_id = 0;
+  if (c.ptr && current_context_id(&ctx_id) && c.ctx_id == ctx_id) {
+    *out = c.ptr;
+    return Q3_OK;
+  }
+  void *p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_argmax_keys);   // initialises the context if needed
+  if (e != cudaSuccess || !p) {
+    q3h::set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+    return Q3_ERR_CUDA;
+  }
+  if (!current_context_id(&ctx_id)) {
+    q3h::set_error_message("q3_gemm_nt_group_argmax_noalloc: no current CUDA context");
+    return Q3_ERR_CUDA;
+  }
+  c = Cached{ctx_id, p};
+  *out = c.ptr;
   return Q3_OK;
 }
 

@@ -37,8 +37,9 @@ int tp_device_status_take() {
 
 namespace {
 
-// wait (bounded, ~2 s) until the counter has reached `target` (wrap-safe)
-__device__ bool wait_count(const unsigned *ctr, unsigned target) {
+// wait (bounded by limit_ns, 2 s by default) until the counter has reached
+// `target` (wrap-safe)
+__device__ bool wait_count(const unsigned *ctr, unsigned target, unsigned long long limit_ns) {
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     unsigned v;
@@ -47,7 +48,7 @@ __device__ bool wait_count(const unsigned *ctr, unsigned target) {
     if ((it & 63) == 0) {
       const uint64_t t = tcx::gtime();
       if (t0 == 0) t0 = t;
-      else if (t - t0 > 2000000000ull) return false;
+      else if (t - t0 > limit_ns) return false;
     }
   }
 }
@@ -65,7 +66,8 @@ __global__ void __launch_bounds__(1024) k_tp_reduce_norm(TpReduceArgs a) {
   __shared__ float bsum[32];
   __shared__ float gmax[32];
   const int m = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  if (t < a.world && !wait_count(a.sig + t, a.expect[t])) atomicOr(&g_tp_error, kErrTpWait);
+  if (t < a.world && !wait_count(a.sig + t, a.expect[t], a.wait_ns))
+    atomicOr(&g_tp_error, kErrTpWait);
   __syncthreads();
   // group-ordered sum of the partials (ref_qwen3.py:151-157)
   const float *base = a.recv + static_cast<size_t>(m) * a.H + t;
@@ -112,6 +114,7 @@ struct TpArgmaxArgs {
   const unsigned *sig;                         // this rank's sig[TP_KEYS][.]
   unsigned *expect;                            // this rank's expect[TP_KEYS][.]
   int32_t *next_ids;
+  unsigned long long wait_ns;
 };
 
 // (max, first index) of every rank's slice as one key (monotone value << 32 |
@@ -133,7 +136,7 @@ __global__ void __launch_bounds__(64) k_tp_argmax_exchange(TpArgmaxArgs a) {
     for (int q = 0; q < a.world; ++q) sys_signal(a.sig_dst[q]);
   if (i < a.world) {
     const unsigned target = a.expect[i] + 1u;
-    if (!wait_count(a.sig + i, target)) atomicOr(&g_tp_error, kErrTpWait);
+    if (!wait_count(a.sig + i, target, a.wait_ns)) atomicOr(&g_tp_error, kErrTpWait);
     a.expect[i] = target;
   }
   __syncthreads();
@@ -148,6 +151,8 @@ __global__ void __launch_bounds__(64) k_tp_argmax_exchange(TpArgmaxArgs a) {
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+__global__ void k_tp_expect_add(unsigned *expect, unsigned count) { *expect += count; }
 
 }  // namespace
 
@@ -180,6 +185,7 @@ int tp_argmax_exchange(const TpComm &c, const float *best, const int32_t *bidx, 
   a.sig = tp_sig(c, c.rank, TP_KEYS, 0);
   a.expect = tp_expect(c, TP_KEYS);
   a.next_ids = next_ids;
+  a.wait_ns = c.wait_ns;
   q3h::timer_begin(q3h::TIMER_EXCHANGE, s);
   k_tp_argmax_exchange<<<1, 64, 0, s>>>(a);
   const int st = q3h::launch_status();
@@ -241,6 +247,7 @@ extern "C" int q3_tp_comm_create(const q3_layout *L, int32_t rank, int32_t world
   }
   c->rank = rank;
   c->world = world;
+  c->wait_ns = q3::kTpDefaultWaitNs;
   c->max_seqs = max_seqs;
   c->hidden = L->hidden;
   c->heads = L->heads;
@@ -294,6 +301,24 @@ extern "C" int q3_tp_comm_reset(void *comm, void *stream) {
     return Q3_ERR_CUDA;
   }
   return Q3_OK;
+}
+
+extern "C" int q3_tp_comm_set_wait_ns(void *comm, uint64_t ns) {
+  if (!comm) return Q3_ERR_NULL;
+  if (ns < 1000000ull || ns > 60000000000ull) return Q3_ERR_SHAPE;
+  static_cast<TpComm *>(comm)->wait_ns = ns;
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_comm_inject_missing_signals(void *comm, int32_t buf, int32_t producer,
+                                                 uint32_t count, void *stream) {
+  if (!comm) return Q3_ERR_NULL;
+  TpComm *c = static_cast<TpComm *>(comm);
+  if (buf < 0 || buf >= q3::TP_NBUF || producer < 0 || producer >= c->world || count == 0)
+    return Q3_ERR_SHAPE;
+  q3::k_tp_expect_add<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(
+      q3::tp_expect(*c, buf) + producer, count);
+  return q3h::launch_status();
 }
 
 extern "C" int q3_tp_comm_destroy(void *comm) {

@@ -24,8 +24,11 @@ struct TpComm {
   bool opened[kTpMaxRanks];       // peer[q] came from cudaIpcOpenMemHandle
   size_t bytes;
   size_t off_sig, off_expect, off_orecv, off_drecv, off_keys;
+  unsigned long long wait_ns;     // limit of every bounded wait on the peers' signals
   q3_tp_shard shard[kTpMaxRanks];
 };
+
+constexpr unsigned long long kTpDefaultWaitNs = 2000000000ull;
 
 // per-buffer counters of a region: sig[buf][producer rank], expect[buf][producer rank]
 inline unsigned *tp_sig(const TpComm &c, int q, int buf, int producer) {
@@ -49,6 +52,7 @@ struct TpReduceArgs {
   int B, H;
   int8_t *h8;                     // [B][H]
   float *hs;                      // [B][H/256]
+  unsigned long long wait_ns;     // bounded wait on the signals
 };
 int tp_reduce_norm(const TpReduceArgs &a, cudaStream_t s);
 

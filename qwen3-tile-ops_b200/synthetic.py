@@ -1,7 +1,7 @@
 """Seeded random-init Qwen3-shaped w8a8 weights and KV prefixes, generated on
 the device (the reference's HF weights are not available).
 
-Weights follow the BASELINE configs' recipe: N(0, 0.02) float32 per matrix,
+Weights follow the random-init recipe of the benchmarks: N(0, 0.02) float32 per matrix,
 quantised per output row with the path's own quantiser
 (``q3_quant_rows_heads`` with one group per row == ``tools/pqwf.py:72-89``);
 RMSNorm weights ``1 + 0.05 N(0,1)``; RoPE tables as

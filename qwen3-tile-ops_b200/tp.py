@@ -56,8 +56,12 @@ def _bind():
                                           C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
                                           C.c_uint32, C.c_void_p, C.c_void_p, C.c_size_t,
                                           C.c_void_p]
+    h.q3_tp_comm_set_wait_ns.argtypes = [C.c_void_p, C.c_uint64]
+    h.q3_tp_comm_inject_missing_signals.argtypes = [C.c_void_p, C.c_int32, C.c_int32, C.c_uint32,
+                                                    C.c_void_p]
     for name in ("q3_tp_shard_of", "q3_tp_comm_create", "q3_tp_comm_connect", "q3_tp_comm_reset",
-                 "q3_tp_comm_destroy", "q3_tp_decode_step_batch"):
+                 "q3_tp_comm_destroy", "q3_tp_decode_step_batch", "q3_tp_comm_set_wait_ns",
+                 "q3_tp_comm_inject_missing_signals"):
         getattr(h, name).restype = C.c_int
     h._q3_tp_bound = True
     return h
@@ -121,6 +125,19 @@ class TPComm:
         check("q3_tp_comm_reset", _bind().q3_tp_comm_reset(self.ptr, None))
         torch.cuda.synchronize()
         self._barrier()
+
+    def set_wait_ns(self, ns: int) -> None:
+        """How long this rank's kernels wait for a peer's signal before they
+        give up and set device status bit 20 (default 2 s)."""
+        check("q3_tp_comm_set_wait_ns", _bind().q3_tp_comm_set_wait_ns(self.ptr, int(ns)))
+
+    def inject_missing_signals(self, buf: int, producer: int, count: int = 1, stream=None) -> None:
+        """Failure injection on the host side: raise this rank's expected
+        signal count of exchange buffer ``buf`` (0 O, 1 down, 2 argmax keys)
+        from ``producer`` by ``count``, as if that producer had fallen behind."""
+        st = None if stream is None else stream.cuda_stream
+        check("q3_tp_comm_inject_missing_signals",
+              _bind().q3_tp_comm_inject_missing_signals(self.ptr, buf, producer, count, st))
 
     def close(self) -> None:
         if self.ptr:

@@ -257,3 +257,126 @@ def test_prefill_batch(q3, layers, vocab, B, T):
                 assert np.array_equal(pool["pv"][L, p, sl], kvs[s].v8[L][t])
                 same_bits(pool["pks"][L, p, sl], kvs[s].ks[L][t])
                 same_bits(pool["pvs"][L, p, sl], kvs[s].vs[L][t])
+
+
+# ------------------------------------------- batched decode at the benchmark shape
+def test_decode_step_batch_benchmark_shape(q3):
+    """The benchmarked decode regime: 64 sequences at contexts 2048-2111 (512
+    attention CTAs, full 64-token cluster GEMM tiles), 2 layers, vocab 4096,
+    shuffled page tables.  The seeded int8 K/V prefixes and their scales are
+    written into the page pool and, through each sequence's page table, into
+    the oracle's per-sequence cache (no CPU prefill).  One batched step on the
+    GPU against the oracle's forward_chunk per sequence: the greedy ids, the
+    residual stream x and the new K/V rows of every layer, bit for bit."""
+    layers, vocab, B = 2, 4096, 64
+    rng = np.random.default_rng(44)
+    lens = [int(v) for v in rng.integers(2048, 2112, B)]
+    max_seq = 2176
+    shape = synth.Shape(layers=layers, vocab=vocab, max_seq=max_seq)
+    w = synth.build_model(shape)
+    max_pages = max_seq // 32
+    total_pages = B * max_pages
+    tables = rng.permutation(total_pages).reshape(B, max_pages).astype(np.uint16)
+    kw = 8 * 128
+    pk = rng.integers(-127, 128, (layers, total_pages, 32, kw), dtype=np.int8)
+    pv = rng.integers(-127, 128, (layers, total_pages, 32, kw), dtype=np.int8)
+    pks = rng.uniform(1e-3, 1e-2, (layers, total_pages, 32, 8)).astype(F)
+    pvs = rng.uniform(1e-3, 1e-2, (layers, total_pages, 32, 8)).astype(F)
+    ids_now = [int(v) for v in rng.integers(0, vocab, B)]
+    dims = q3.model.Dims(layers=layers, vocab=vocab, max_seq=max_seq)
+    bm = q3.model.BlobModel(dims).load_weights(w)
+    d = {k: torch.from_numpy(v).cuda() for k, v in
+         (("pk", pk), ("pv", pv), ("pks", pks), ("pvs", pvs))}
+    pool = q3._lib.KVPool(d["pk"].data_ptr(), d["pv"].data_ptr(), d["pks"].data_ptr(),
+                          d["pvs"].data_ptr(), total_pages * 32 * kw, total_pages * 32 * 8 * 4,
+                          total_pages)
+    tab = torch.from_numpy(tables.view(np.int16)).cuda()
+    ids_d = torch.tensor(ids_now, dtype=torch.int32, device="cuda")
+    pos_d = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    nxt = torch.zeros(B, dtype=torch.int32, device="cuda")
+    lib = q3._lib.lib()
+    wsb = lib.q3_decode_workspace_bytes(C.byref(bm.L), B)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
+        bm.blob.data_ptr(), C.byref(bm.L), C.byref(pool), tab.data_ptr(), max_pages,
+        ids_d.data_ptr(), pos_d.data_ptr(), B, nxt.data_ptr(), ws.data_ptr(), wsb,
+        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert lib.q3_device_status() == 0
+    got_ids = nxt.cpu().numpy()
+    got_x = ws[:B * 1024 * 4].cpu().numpy().view(F).reshape(B, 1024)
+    got = {k: v.cpu().numpy() for k, v in d.items()}
+    slots = np.arange(max_seq) % 32
+    for s, n in enumerate(lens):
+        kv = O.KV.empty(w, max_seq)
+        pages = tables[s, np.arange(n) // 32]
+        for L in range(layers):
+            kv.k8[L][:n] = pk[L, pages, slots[:n]]
+            kv.v8[L][:n] = pv[L, pages, slots[:n]]
+            kv.ks[L][:n] = pks[L, pages, slots[:n]]
+            kv.vs[L][:n] = pvs[L, pages, slots[:n]]
+        rec = {}
+        lg = O.forward_chunk(w, [ids_now[s]], kv, n, 1, True, rec)
+        assert int(got_ids[s]) == O.argmax_logits(lg), f"sequence {s}"
+        same_bits(got_x[s:s + 1], rec["x"], f"x of sequence {s}")
+        p, sl = tables[s, n // 32], n % 32
+        for L in range(layers):
+            assert np.array_equal(got["pk"][L, p, sl], kv.k8[L][n]), (s, L)
+            assert np.array_equal(got["pv"][L, p, sl], kv.v8[L][n]), (s, L)
+            same_bits(got["pks"][L, p, sl], kv.ks[L][n], f"ks {s} {L}")
+            same_bits(got["pvs"][L, p, sl], kv.vs[L][n], f"vs {s} {L}")
+
+
+# ------------------------------------------- batched prefill at the benchmark length
+def test_prefill_batch_4096_causal(q3):
+    """The long-prompt regime: 2 prompts of 4096 tokens, one layer, vocab 1024,
+    in ONE batched prefill (8192 stacked GEMM rows; causal attention over 128
+    pages per prompt).  Every prompt row's K/V in the pool, the residual stream
+    x of a sample of rows (page edges, the first and last rows, 64 random rows;
+    x carries the attention output through the O GEMM) and the greedy next id
+    of each prompt, bit for bit against the oracle."""
+    layers, vocab, B, T = 1, 1024, 2, 4096
+    shape = synth.Shape(layers=layers, vocab=vocab, max_seq=T)
+    w = synth.build_model(shape)
+    rng = np.random.default_rng(45)
+    max_pages = T // 32
+    total_pages = B * max_pages
+    tables = rng.permutation(total_pages).reshape(B, max_pages).astype(np.uint16)
+    prompts = rng.integers(0, vocab, (B, T))
+    dims = q3.model.Dims(layers=layers, vocab=vocab, max_seq=T)
+    bm = q3.model.BlobModel(dims).load_weights(w)
+    kw = 8 * 128
+    d = {"pk": torch.zeros((layers, total_pages, 32, kw), dtype=torch.int8, device="cuda"),
+         "pv": torch.zeros((layers, total_pages, 32, kw), dtype=torch.int8, device="cuda"),
+         "pks": torch.zeros((layers, total_pages, 32, 8), dtype=torch.float32, device="cuda"),
+         "pvs": torch.zeros((layers, total_pages, 32, 8), dtype=torch.float32, device="cuda")}
+    pool = q3._lib.KVPool(d["pk"].data_ptr(), d["pv"].data_ptr(), d["pks"].data_ptr(),
+                          d["pvs"].data_ptr(), total_pages * 32 * kw, total_pages * 32 * 8 * 4,
+                          total_pages)
+    tab = torch.from_numpy(tables.view(np.int16)).cuda()
+    ids_d = torch.from_numpy(prompts.astype(np.int32).reshape(-1)).cuda()
+    nxt = torch.full((B,), -1, dtype=torch.int32, device="cuda")
+    lib = q3._lib.lib()
+    wsb = lib.q3_prefill_workspace_bytes(C.byref(bm.L), B, T)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
+        bm.blob.data_ptr(), C.byref(bm.L), C.byref(pool), tab.data_ptr(), max_pages,
+        ids_d.data_ptr(), B, T, nxt.data_ptr(), ws.data_ptr(), wsb,
+        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert lib.q3_device_status() == 0
+    got_x = ws[:B * T * 1024 * 4].cpu().numpy().view(F).reshape(B, T, 1024)
+    got = {k: v.cpu().numpy() for k, v in d.items()}
+    got_ids = nxt.cpu().numpy()
+    edges = [0, 1, 31, 32, 33, 127, 128, 1023, 1024, 2047, 2048, 2049, 3071, 4063, 4064, 4094]
+    for s in range(B):
+        rows = sorted(set(edges) | set(int(v) for v in rng.integers(0, T - 1, 64))) + [T - 1]
+        (k8, ks, v8, vs), xr, logits = O.forward_prompt_rows(w, prompts[s], rows)
+        t = np.arange(T)
+        pages = tables[s, t // 32]
+        assert np.array_equal(got["pk"][0, pages, t % 32], k8), f"K of prompt {s}"
+        assert np.array_equal(got["pv"][0, pages, t % 32], v8), f"V of prompt {s}"
+        same_bits(got["pks"][0, pages, t % 32], ks, f"K scales of prompt {s}")
+        same_bits(got["pvs"][0, pages, t % 32], vs, f"V scales of prompt {s}")
+        same_bits(got_x[s, rows], xr, f"x rows of prompt {s}")
+        assert int(got_ids[s]) == O.argmax_logits(logits), f"next id of prompt {s}"

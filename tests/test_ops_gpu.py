@@ -2,7 +2,7 @@
 reference's API against the oracle and the golden vectors made by the
 reference's own numpy mirror.  Integer/int8 results and float32 results are
 compared bit for bit (the path's floats are rounded exactly as the
-reference's), which is stricter than BASELINE's 1e-3 relative tolerance."""
+reference's), which is stricter than the 1e-3 relative tolerance allowed for f32 stages."""
 
 from __future__ import annotations
 
@@ -164,7 +164,7 @@ def test_lm_head_argmax(ops, m):
         same_bits(gb[r:r + 1], logits[r].max(keepdims=True))
 
 
-# ---- config 2: the per-group GEMM microbench shapes -------
+# ---- the per-group GEMM microbench shapes (prefill-size GEMMs) ------------------
 # M beyond 64 takes the wide token tiles; 700 leaves a ragged last tile.
 @pytest.mark.parametrize("m", [512, 700, 4096])
 @pytest.mark.parametrize("k,n,g", [(1024, 2048, 256), (2048, 1024, 128), (3072, 1024, 256)])

@@ -3,7 +3,7 @@ mirror (``tests/golden/gen_golden.py`` imports ``tools/ref_qwen3.py``).
 
 Everything here is CPU-only and bit-exact (``cr`` exp flavour); the
 ``native`` flavour is bit-exact only on a host whose numpy SIMD dispatch equals
-the one recorded in the fixture, and is otherwise held to BASELINE tolerances.
+the one recorded in the fixture, and is otherwise held to the f32 tolerance (1e-3 relative).
 """
 
 from __future__ import annotations
@@ -163,7 +163,7 @@ def test_config1_native_exp():
     lg = recs[-1][3]
     if here == json.loads(str(g["cpu"])):
         assert bits_equal(lg, g["logits"])
-    else:  # different numpy exp2 dispatch: BASELINE f32 tolerance
+    else:  # different numpy exp2 dispatch: f32 tolerance
         np.testing.assert_allclose(lg, g["logits"], rtol=1e-3, atol=1e-3)
 
 
@@ -178,3 +178,21 @@ def test_config3_full_shape():
     assert gen == [int(v) for v in g["generated"]]
     import hashlib
     assert hashlib.sha256(np.ascontiguousarray(last).tobytes()).hexdigest() == str(g["logits_sha"])
+
+
+def test_forward_prompt_rows_matches_forward_chunk():
+    """The row-sampled one-layer prompt forward (used by the long-prompt GPU
+    test) gives, for every selected row, the bits forward_chunk gives for that
+    row when the whole prompt is one chunk: K/V of all rows, x, logits."""
+    w = synth.build_model(synth.Shape(layers=1, vocab=1024, max_seq=128))
+    ids = [int(v) for v in np.random.default_rng(3).integers(0, 1024, 100)]
+    kv = O.KV.empty(w, 128)
+    rec = {}
+    lg = O.forward_chunk(w, ids, kv, 0, 100, True, rec)
+    rows = [0, 5, 31, 32, 63, 64, 98, 99]
+    (k8, ks, v8, vs), xr, logits = O.forward_prompt_rows(w, ids, rows)
+    assert np.array_equal(k8, kv.k8[0][:100]) and np.array_equal(v8, kv.v8[0][:100])
+    assert np.array_equal(ks.view(np.uint32), kv.ks[0][:100].view(np.uint32))
+    assert np.array_equal(vs.view(np.uint32), kv.vs[0][:100].view(np.uint32))
+    assert np.array_equal(xr.view(np.uint32), rec["x"][rows].view(np.uint32))
+    assert np.array_equal(logits.view(np.uint32), lg.view(np.uint32))

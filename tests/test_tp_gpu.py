@@ -144,3 +144,65 @@ def test_tp_decode_matches_single_gpu(q3, tmp_path, world):
         np.testing.assert_array_equal(d["ids"], ref_ids)
         np.testing.assert_array_equal(d["x"].view(np.uint32), ref_x.view(np.uint32))
         np.testing.assert_array_equal(d["kv"], ref_kv[..., r * kvh * 128:(r + 1) * kvh * 128])
+
+
+@pytest.mark.parametrize("buf", [0, 1, 2], ids=["o", "down", "keys"])
+def test_tp_wait_timeout_then_reset(q3, buf):
+    """Failure detection on one GPU, with no fault: a one-rank communicator is
+    told that its own producer fell one signal behind on one exchange buffer
+    (O partials, down partials or the argmax keys).  The consumer's bounded
+    wait (set to 20 ms) runs out, the step returns, device status bit 20 is
+    set and the context stays usable; after q3_tp_comm_reset the same step
+    gives the single-GPU ids again with a clean status."""
+    import ctypes as C
+    import time
+
+    from q3b200 import synthetic, tp
+    from q3b200.model import Dims
+    lib = q3._lib.lib()
+    dev = torch.device("cuda", 0)
+    Bq, ctx, layers = 4, 70, 1
+    max_seq = 128
+    dims = Dims(layers=layers, vocab=4096, max_seq=max_seq)
+    bm = synthetic.random_blob_model(dims, seed=31, device=dev)
+    max_pages = max_seq // 32
+    pool = synthetic.KVPoolTensors(layers, Bq * max_pages, 8, device=dev)
+    pool.fill_random(seed=32)
+    g = torch.Generator().manual_seed(33)
+    tab = torch.randperm(Bq * max_pages, generator=g).reshape(Bq, max_pages).to(torch.int16).to(dev)
+    ids = torch.randint(0, 4096, (Bq,), generator=g, dtype=torch.int32).to(dev)
+    pos = torch.full((Bq,), ctx, dtype=torch.int32, device=dev)
+    wsb = lib.q3_decode_workspace_bytes(C.byref(bm.L), Bq)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+    cpool = pool.c()
+    stream = torch.cuda.current_stream()
+    assert lib.q3_device_status() == 0
+
+    ref = torch.zeros(Bq, dtype=torch.int32, device=dev)
+    q3._lib.check("q3_decode_step_batch", lib.q3_decode_step_batch(
+        bm.blob.data_ptr(), C.byref(bm.L), C.byref(cpool), tab.data_ptr(), max_pages,
+        ids.data_ptr(), pos.data_ptr(), Bq, ref.data_ptr(), ws.data_ptr(), wsb,
+        stream.cuda_stream))
+    torch.cuda.synchronize()
+    want = ref.cpu().tolist()
+
+    comm = tp.TPComm(bm.L, 0, 1, Bq)
+    try:
+        comm.set_wait_ns(20_000_000)
+        nxt = torch.zeros(Bq, dtype=torch.int32, device=dev)
+        comm.inject_missing_signals(buf, 0, 1, stream)
+        t0 = time.perf_counter()
+        comm.decode_step(bm.blob, bm.L, cpool, tab, max_pages, ids, pos, Bq, nxt, ws, stream)
+        torch.cuda.synchronize()
+        waited = time.perf_counter() - t0
+        st = lib.q3_device_status()
+        assert st & (1 << 20), f"status {st:#x}: the wait did not time out"
+        assert waited < 1.5, f"the step took {waited:.2f} s with a 20 ms wait limit"
+        comm.reset()
+        nxt.zero_()
+        comm.decode_step(bm.blob, bm.L, cpool, tab, max_pages, ids, pos, Bq, nxt, ws, stream)
+        torch.cuda.synchronize()
+        assert lib.q3_device_status() == 0
+        assert nxt.cpu().tolist() == want
+    finally:
+        comm.close()

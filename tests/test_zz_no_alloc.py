@@ -5,8 +5,9 @@ fixed device buffer planned up front, or a serving loop that keeps
 allocation calls (which can synchronize the device) off its hot path.
 ``q3_gemm_nt_group_argmax_noalloc`` serves them with a built-in device scratch
 array instead of a caller workspace.  This test drives it through the C ABI,
-twice in a row on different inputs (the array keeps the previous call's
-contents), and requires exactly the (best, bidx) of the workspace entry point
+three times in a row on different inputs (the array keeps the previous call's
+contents; the last call has more rows and smaller maxima than the
+first), and requires exactly the (best, bidx) of the workspace entry point
 ``q3_gemm_nt_group_argmax`` — the same bit-exact bar the other argmax tests use.
 It also checks that a call beyond the array's row limit is refused.
 
@@ -26,11 +27,11 @@ torch = pytest.importorskip("torch")
 F = np.float32
 
 
-def _case(rng, m, k=1024, n=4096, g=256):
+def _case(rng, m, k=1024, n=4096, g=256, a_scale=1.0):
     a = rng.integers(-127, 128, (m, k)).astype(np.int8)
     w = rng.integers(-127, 128, (n, k)).astype(np.int8)
     w[n - 5] = w[3]                    # a tied maximum candidate
-    a_s = rng.uniform(1e-3, 1e-2, (m, k // g)).astype(F)
+    a_s = (rng.uniform(1e-3, 1e-2, (m, k // g)) * a_scale).astype(F)
     w_s = rng.uniform(1e-3, 1e-2, n).astype(F)
     w_s[n - 5] = w_s[3]
     return [torch.from_numpy(x).cuda() for x in (a, a_s, w, w_s)]
@@ -65,8 +66,11 @@ def _run(q3, tensors, noalloc: bool):
 def test_noalloc_argmax_matches_workspace_entry_twice(q3):
     assert torch.cuda.is_available()
     rng = np.random.default_rng(2024)
-    for m in (40, 3):                 # second call reuses the (now stale) scratch
-        tensors = _case(rng, m)
+    # 40 rows, then 3, then 64 rows whose maxima are 1000x smaller than the
+    # first call's: keys the first call left in the array would win their rows
+    # unless each call clears every row it reads
+    for m, a_scale in ((40, 1.0), (3, 1.0), (64, 1e-3)):
+        tensors = _case(rng, m, a_scale=a_scale)
         want_best, want_idx = _run(q3, tensors, noalloc=False)
         got_best, got_idx = _run(q3, tensors, noalloc=True)
         assert np.array_equal(got_idx, want_idx)
