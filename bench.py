@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the batched prefill measurement (one JSON line; with --layers 1 "
                          "the small case the prefill profiles are captured on)")
+    ap.add_argument("--single-only", action="store_true",
+                    help="only the batch-1 q3_generate measurement (one JSON line)")
     ap.add_argument("--no-single", action="store_true",
                     help="skip the batch-1 q3_generate measurement reported under 'single_sequence'")
     ap.add_argument("--prefill-seqs", type=int, default=16)
@@ -441,6 +443,9 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local_rank)
     B, K, W = args.seqs, args.steps, args.warmup
 
+    if args.single_only:
+        print(json.dumps(measure_single_sequence(args, q3, lib, dev)), flush=True)
+        return
     if args.prefill_only:
         pf = measure_prefill(args, q3, lib, dev, rank, world, dist)
         if dist:

@@ -468,6 +468,15 @@ int q3_tp_decode_step_batch(void *comm, void *blob, const q3_layout *layout,
 int q3_exp_rows(const q3_view *x, const q3_view *out, void *stream);
 int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream);
 
+/* No counterpart in the reference: self-check of the two device evaluations
+ * of the correctly rounded exp2 (the short one every kernel uses and the
+ * longer double-precision one it falls back to near rounding midpoints).  Every float32 bit pattern in
+ * [lo_bits, hi_bits) is evaluated both ways; *count (device, caller-zeroed)
+ * gains the number of results that differ and *first_bad (device, caller-set
+ * to 0xffffffff) the smallest differing bit pattern. */
+int q3_exp2_selfcheck(uint32_t lo_bits, uint32_t hi_bits, unsigned long long *count,
+                      uint32_t *first_bad, void *stream);
+
 /* ---- misc ---------------------------------------------------------------- */
 const char *q3_last_cuda_error(void);
 int q3_device_check(void); /* Q3_OK on an sm_100 device, else Q3_ERR_ARCH */

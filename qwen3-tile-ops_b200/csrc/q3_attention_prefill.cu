@@ -70,9 +70,11 @@ struct Smem {
   alignas(1024) int8_t k[NST][32 * 128];             // page tiles, 128-byte swizzled
   alignas(1024) int8_t v[NST][32 * 128];
   alignas(1024) int8_t pq[2][2 * ROWS * 16];         // [key half][16 row groups][8 rows][16 B]
-  float ks[NST][32], vs[NST][32];
-  float xmax[2][KP][ROWS];                           // [block parity][part][row]
-  float xsum[2][KP][ROWS], xam[2][KP][ROWS];
+  alignas(16) float ks[NST][32];
+  alignas(16) float vs[NST][32];
+  alignas(16) float xmax[2][ROWS][KP];               // [block parity][row][part]
+  alignas(16) float xsum[2][ROWS][KP];
+  alignas(16) float xam[2][ROWS][KP];
   float xout[KP][ROWS];
   unsigned long long q_full, kv_full[NST], kv_empty[NST];
   unsigned long long s_full[2], s_free[2], p_full[2], o_full, o_free, final_done;
@@ -227,9 +229,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_wait_ld();
       fence_before();
       mbar_arrive(&sm.o_free);
+      if (__all_sync(0xffffffffu, corr == 1.0f)) {          // res * 1 = res exactly
 #pragma unroll
-      for (int d = 0; d < KPC; ++d)
-        res[d] = __fadd_rn(__fmul_rn(res[d], corr), __fmul_rn(i2f_small(o[d]), pm));
+        for (int d = 0; d < KPC; ++d) res[d] = __fadd_rn(res[d], __fmul_rn(i2f_small(o[d]), pm));
+      } else {
+#pragma unroll
+        for (int d = 0; d < KPC; ++d)
+          res[d] = __fadd_rn(__fmul_rn(res[d], corr), __fmul_rn(i2f_small(o[d]), pm));
+      }
     };
 
     for (int j = 0; j < J; ++j) {
@@ -242,43 +249,46 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_before();
       mbar_arrive(&sm.s_free[slot]);
       wait_or_abort(&sm.kv_full[st], (j / NST) & 1, &sm.abort);   // the block's scales
-      float s[KPK];
+      float s[KPK], ksv[KPK], vsv[KPK];
+      *reinterpret_cast<float4 *>(&ksv[0]) = *reinterpret_cast<const float4 *>(&sm.ks[st][KPK * pt]);
+      *reinterpret_cast<float4 *>(&ksv[4]) = *reinterpret_cast<const float4 *>(&sm.ks[st][KPK * pt + 4]);
       float bm = kNegInf;
 #pragma unroll
       for (int i = 0; i < KPK; ++i) {
         const int key = 32 * j + KPK * pt + i;
         s[i] = (key <= pos)
-                   ? __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a[i]), sm.ks[st][KPK * pt + i]), qsc), p.qk_scale)
+                   ? __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a[i]), ksv[i]), qsc), p.qk_scale)
                    : kNegInf;
         bm = fmaxf(bm, s[i]);
       }
-      sm.xmax[slot][pt][r] = bm;
+      sm.xmax[slot][r][pt] = bm;
       rows_sync();
-      float bmax = sm.xmax[slot][0][r];
-#pragma unroll
-      for (int q = 1; q < KP; ++q) bmax = fmaxf(bmax, sm.xmax[slot][q][r]);
+      const float4 xm = *reinterpret_cast<const float4 *>(sm.xmax[slot][r]);
+      const float bmax = fmaxf(fmaxf(xm.x, xm.y), fmaxf(xm.z, xm.w));
       const float mn = fmaxf(m, bmax);
-      const float corr = exp_ref(__fsub_rn(m, mn));
+      // exp(m - mn) is exp(0) = 1 exactly when the running maximum did not move
+      const float corr = (mn == m) ? 1.0f : exp_ref_fast(__fsub_rn(m, mn));
       float pv[KPK];
       float am = 0.0f;
 #pragma unroll
-      for (int i = 0; i < KPK; ++i) s[i] = exp_ref(__fsub_rn(s[i], mn));   // p
+      for (int i = 0; i < KPK; ++i) s[i] = exp_ref_fast(__fsub_rn(s[i], mn));   // p
       const float ps = tree8_sum(s);
+      *reinterpret_cast<float4 *>(&vsv[0]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt]);
+      *reinterpret_cast<float4 *>(&vsv[4]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt + 4]);
 #pragma unroll
       for (int i = 0; i < KPK; ++i) {
         const int key = 32 * j + KPK * pt + i;
-        pv[i] = (key <= pos) ? __fmul_rn(s[i], sm.vs[st][KPK * pt + i]) : 0.0f;
+        pv[i] = (key <= pos) ? __fmul_rn(s[i], vsv[i]) : 0.0f;
         am = fmaxf(am, fabsf(pv[i]));
       }
-      sm.xsum[slot][pt][r] = ps;
-      sm.xam[slot][pt][r] = am;
+      sm.xsum[slot][r][pt] = ps;
+      sm.xam[slot][r][pt] = am;
       rows_sync();
       // the two top levels of the 32-key tree: (s0 + s1) + (s2 + s3)
-      const float psum = __fadd_rn(__fadd_rn(sm.xsum[slot][0][r], sm.xsum[slot][1][r]),
-                                   __fadd_rn(sm.xsum[slot][2][r], sm.xsum[slot][3][r]));
-      float amx = sm.xam[slot][0][r];
-#pragma unroll
-      for (int q = 1; q < KP; ++q) amx = fmaxf(amx, sm.xam[slot][q][r]);
+      const float4 xs = *reinterpret_cast<const float4 *>(sm.xsum[slot][r]);
+      const float psum = __fadd_rn(__fadd_rn(xs.x, xs.y), __fadd_rn(xs.z, xs.w));
+      const float4 xa = *reinterpret_cast<const float4 *>(sm.xam[slot][r]);
+      const float amx = fmaxf(fmaxf(xa.x, xa.y), fmaxf(xa.z, xa.w));
       const float pm = __fmul_rn(amx, kInv127);
       den = __fadd_rn(__fmul_rn(den, corr), psum);
       m = mn;

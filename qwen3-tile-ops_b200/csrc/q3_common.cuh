@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include "../../include/q3_ops.h"
+#include "exp2_t256_table.inc"
 #include "exp2_hard_table.inc"
 
 namespace q3 {
@@ -88,7 +89,9 @@ static __device__ const unsigned long long g_exp2_frac64[64] = {
 // pattern, rounding it to float32 rounds 2^x; otherwise the input is looked up
 // in the hard-case table (every input within 2^-46 of a midpoint).  Results
 // below 2^-125 (float32 subnormals) and non-finite inputs take exp2_cr_libm.
-__device__ __forceinline__ float exp2_cr(float x) {
+// `tab` is g_exp2_frac64 or a copy of it (kernels that evaluate many exps keep
+// one in shared memory: the index varies per lane).
+__device__ __forceinline__ float exp2_cr_t(float x, const unsigned long long *tab) {
   if (!(x >= -125.0f && x < 128.0f)) return x < -151.0f ? 0.0f : exp2_cr_libm(x);
   const float kf = rintf(__fmul_rn(x, 64.0f));                  // exact
   const int k = static_cast<int>(kf);
@@ -99,7 +102,7 @@ __device__ __forceinline__ float exp2_cr(float x) {
   p = __fma_rn(p, r, 0.24022650695910072);                       // (ln2)^2 / 2!
   p = __fma_rn(p, r, 0.6931471805599453);                        // ln2
   p = __fma_rn(p, r, 1.0);
-  const double t = __longlong_as_double(static_cast<long long>(g_exp2_frac64[k & 63]));
+  const double t = __longlong_as_double(static_cast<long long>(tab[k & 63]));
   const long long yb =
       __double_as_longlong(__dmul_rn(t, p)) + (static_cast<long long>(k >> 6) << 52);
   const float res = __double2float_rn(__longlong_as_double(yb));
@@ -108,9 +111,46 @@ __device__ __forceinline__ float exp2_cr(float x) {
   return res;
 }
 
+// 2^(i/256), i = 0..255, correctly rounded to double (gen_exp2_t256_table.py).
+static __device__ const unsigned long long g_exp2_t256[Q3_EXP2_T256_N] = Q3_EXP2_T256_INIT;
+
+// exp2_cr_fast: the same correctly rounded result with fewer double operations,
+// for throughput-bound callers (the prefill attention evaluates ~2e9 exps per
+// layer; measured 10 % more exps per second than exp2_cr_t).  Latency-bound
+// callers (the decode kernels) keep exp2_cr_t, whose chain is shorter there.  x = k/256 + r with k = rint(256 x) and
+// |r| <= 2^-9, both exact in float32 (the rint by the 1.5 * 2^23 shifter);
+// 2^x = 2^(k >> 8) * T * 2^r with T = 2^((k & 255)/256) from the table, and
+// T * 2^r = T + (T r) * (ln2 + r (ln2^2/2 + r (ln2^3/6 + r ln2^4/24))) in
+// double (truncation < 2^-54, the whole evaluation within a few double ulps).
+// The rounding test on the double's 29 bits below float32 precision is
+// exp2_cr_t's; flagged inputs and x outside [-125, 128) take exp2_cr_t.  The
+// float32 result is scaled by 2^(k >> 8) through its exponent field (exact:
+// the result is normal, or +inf when it rounds to 2^128).  Checked identical
+// to exp2_cr_t on every float32 input (q3_exp2_selfcheck).
+__device__ __forceinline__ float exp2_cr_fast(float x) {
+  if (!(x >= -125.0f && x < 128.0f)) return exp2_cr_t(x, g_exp2_frac64);
+  const float u = __fadd_rn(__fmul_rn(x, 256.0f), 12582912.0f);
+  const float kf = __fsub_rn(u, 12582912.0f);
+  const int k = __float_as_int(u) - 0x4B400000;
+  const double r = static_cast<double>(__fmaf_rn(kf, -0.00390625f, x));   // exact
+  double p = __fma_rn(0.009618129107628477, r, 0.05550410866482158);      // ln2^4/4!, ln2^3/3!
+  p = __fma_rn(p, r, 0.24022650695910072);                                 // ln2^2/2!
+  p = __fma_rn(p, r, 0.6931471805599453);                                  // ln2
+  const double t = __longlong_as_double(static_cast<long long>(g_exp2_t256[k & 255]));
+  const double y = __fma_rn(__dmul_rn(t, r), p, t);
+  const unsigned low = static_cast<unsigned>(__double_as_longlong(y)) & 0x1FFFFFFFu;
+  if (low - ((1u << 28) - 64u) <= 128u) return exp2_cr_t(x, g_exp2_frac64);
+  return __int_as_float(__float_as_int(__double2float_rn(y)) + ((k >> 8) << 23));
+}
+
+__device__ __forceinline__ float exp2_cr(float x) { return exp2_cr_t(x, g_exp2_frac64); }
+
 // exp as amulx(log2e) + aexp2 (ref_qwen3.py:27-29)
 __device__ __forceinline__ float exp_ref(float x) {
   return exp2_cr(__fmul_rn(x, __uint_as_float(kLog2eBits)));
+}
+__device__ __forceinline__ float exp_ref_fast(float x) {
+  return exp2_cr_fast(__fmul_rn(x, __uint_as_float(kLog2eBits)));
 }
 
 // rne(x / scale) saturated to +-127, NaN -> 0 (ref_qwen3.py:69-76)

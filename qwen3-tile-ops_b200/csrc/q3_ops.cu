@@ -375,6 +375,32 @@ extern "C" int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream) 
   return exp_common(x, out, 1, stream);
 }
 
+// every float32 bit pattern b in [lo, hi): exp2_cr_fast(b) against exp2_cr_t(b)
+__global__ void k_exp2_selfcheck(uint32_t lo, uint32_t hi, unsigned long long *count,
+                                 uint32_t *first_bad) {
+  const uint64_t n = static_cast<uint64_t>(hi) - lo;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t b = lo + static_cast<uint32_t>(i);
+    const float x = __uint_as_float(b);
+    const float f = exp2_cr_fast(x);
+    const float d = exp2_cr_t(x, g_exp2_frac64);
+    if (__float_as_uint(f) != __float_as_uint(d)) {
+      atomicAdd(count, 1ull);
+      atomicMin(first_bad, b);
+    }
+  }
+}
+
+extern "C" int q3_exp2_selfcheck(uint32_t lo_bits, uint32_t hi_bits, unsigned long long *count,
+                                 uint32_t *first_bad, void *stream) {
+  if (!count || !first_bad) return Q3_ERR_NULL;
+  if (hi_bits < lo_bits) return Q3_ERR_SHAPE;
+  if (hi_bits == lo_bits) return Q3_OK;
+  k_exp2_selfcheck<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(lo_bits, hi_bits, count, first_bad);
+  return launch_status();
+}
+
 extern "C" int q3_argmax_logits(const q3_view *logits, int32_t *out_id, void *stream) {
   Q3_TRY(check_view(logits, Q3_DT_F32));
   if (!out_id) return Q3_ERR_NULL;

@@ -332,6 +332,22 @@ def test_exp_correctly_rounded(ops):
         same_bits(host(y), O.exp_f32(x))
 
 
+def test_exp2_short_evaluation_exhaustive(q3):
+    """The short evaluation of the correctly rounded exp2 that every kernel
+    uses (256-entry table, degree-4 polynomial) gives the same bits as the
+    longer double-precision one (itself pinned above and to the mpmath
+    hard-case table) on EVERY float32 input in (-151, 128) plus +-0: about
+    2.25e9 inputs."""
+    lib = q3._lib.lib()
+    count = torch.zeros(1, dtype=torch.int64, device="cuda")
+    first = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    for lo, hi in ((0x00000000, 0x43000000), (0x80000000, 0xC3170000)):
+        assert lib.q3_exp2_selfcheck(lo, hi, count.data_ptr(), first.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    bad = int(count.item())
+    assert bad == 0, f"{bad} inputs differ, first bit pattern {int(first.item()) & 0xffffffff:#010x}"
+
+
 # ---------------------------------------------------------------- attention
 def _pool_from_contiguous(k8, ks, v8, vs, kv_heads, table):
     """Scatter contiguous K/V [T][kv_heads*128] into pages following `table`."""
