@@ -248,7 +248,11 @@ int q3_forward_chunk(void *blob, const q3_layout *layout, uint32_t pos,
 /* src/main_big.cpp:332-369 — the greedy loop: reads CTRL [n_prompt, n_gen,
  * max_seq, mode] from the blob (one 16-byte device->host read), then runs
  * every chunk asynchronously, writing each picked id into ids[pos].
- * Returns Q3_ERR_MODE for mode > 1. */
+ * In mode 0 (fused lm_head + argmax) the one-row decode steps after the
+ * prompt run the batched decode kernels with one sequence over the blob's
+ * own cache (same bits as q3_forward_chunk); of the blob's stage buffers the
+ * call then leaves x, s8/ss, o8/os (last layer, last step) and argf/argi, as
+ * the reference's loop does.  Returns Q3_ERR_MODE for mode > 1. */
 int q3_generate(void *blob, const q3_layout *layout, void *workspace,
                 size_t workspace_bytes, void *stream);
 

@@ -491,6 +491,44 @@ extern "C" int q3_tp_decode_step_batch(void *comm, void *blob, const q3_layout *
   return tp_decode(c, bl, L, pool, tables, max_pages, ids, pos, n_seqs, next_ids, w, st);
 }
 
+namespace {
+// sequence 0's stage rows of the last decode step -> the blob's stage buffers
+__global__ void k_decode_stages_to_blob(const float *x, const int8_t *s8, const float *ss,
+                                        const int8_t *o8, const float *os, const float *best,
+                                        const int32_t *id, int H, int I, int QW, int heads,
+                                        float *bx, int8_t *bs8, float *bss, int8_t *bo8,
+                                        float *bos, float *argf, int32_t *argi) {
+  for (int i = threadIdx.x; i < H; i += blockDim.x) bx[i] = x[i];
+  for (int i = threadIdx.x; i < I; i += blockDim.x) bs8[i] = s8[i];
+  for (int i = threadIdx.x; i < QW; i += blockDim.x) bo8[i] = o8[i];
+  for (int i = threadIdx.x; i < I / 256; i += blockDim.x) bss[i] = ss[i];
+  for (int i = threadIdx.x; i < heads; i += blockDim.x) bos[i] = os[i];
+  if (threadIdx.x == 0) {
+    *argf = best[0];
+    *argi = *id;
+  }
+}
+}  // namespace
+
+namespace q3 {
+// After a one-sequence q3_decode_step_batch with this workspace: copy the rows
+// the reference's greedy loop leaves in its blob (x, s8/ss, o8/os of the last
+// layer, the argmax value and index) into the blob's stage buffers.
+int decode_stages_to_blob(const q3_layout &L, void *workspace, void *blob, const int32_t *id,
+                          cudaStream_t st) {
+  const DecodeWs w = carve(L, 1, static_cast<char *>(workspace));
+  char *bl = static_cast<char *>(blob);
+  const int64_t *o = L.off;
+  k_decode_stages_to_blob<<<1, 256, 0, st>>>(
+      w.x, w.s8, w.ss, w.o8, w.os, w.best, id, (int)L.hidden, (int)L.inter,
+      (int)(L.heads * L.head_dim), (int)L.heads, reinterpret_cast<float *>(bl + o[Q3_OFF_X]),
+      reinterpret_cast<int8_t *>(bl + o[Q3_OFF_S8]), reinterpret_cast<float *>(bl + o[Q3_OFF_SS]),
+      reinterpret_cast<int8_t *>(bl + o[Q3_OFF_O8]), reinterpret_cast<float *>(bl + o[Q3_OFF_OS]),
+      reinterpret_cast<float *>(bl + o[Q3_OFF_ARGF]), reinterpret_cast<int32_t *>(bl + o[Q3_OFF_ARGI]));
+  return q3h::launch_status();
+}
+}  // namespace q3
+
 extern "C" size_t q3_decode_workspace_bytes(const q3_layout *L, uint32_t n_seqs) {
   if (!L) return 0;
   return carve(*L, n_seqs, nullptr).total;

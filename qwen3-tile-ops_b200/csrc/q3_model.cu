@@ -7,6 +7,11 @@
 
 #include "q3_common.cuh"
 
+namespace q3 {
+int decode_stages_to_blob(const q3_layout &L, void *workspace, void *blob, const int32_t *id,
+                          cudaStream_t st);
+}
+
 namespace {
 
 constexpr uint32_t kPageTokens = 32;
@@ -40,15 +45,28 @@ __global__ void k_init_best(float *best, int32_t *bidx) {
 
 __global__ void k_copy_id(const int32_t *src, int32_t *dst) { *dst = *src; }
 
+__global__ void k_iota(int32_t *v, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) v[i] = i;
+}
+
+// ptab | argmax keys | positions 0..max_seq-1 | last id | one-sequence decode workspace
 struct Ws {
   uint16_t *ptab;
   void *argmax_ws;
   size_t argmax_bytes;
+  int32_t *positions;
+  int32_t *last_id;
+  void *dec_ws;
+  size_t dec_bytes;
 };
+
+size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
 
 size_t ws_bytes(const q3_layout *L) {
   const size_t pages = L->max_seq / kPageTokens;
-  return 256 * ((pages * 2 + 255) / 256) + 256;
+  return a256(pages * 2) + 256 + a256(4 * static_cast<size_t>(L->max_seq)) + 256 +
+         a256(q3_decode_workspace_bytes(L, 1));
 }
 
 int carve(const q3_layout *L, void *ws, size_t bytes, Ws &w) {
@@ -56,9 +74,18 @@ int carve(const q3_layout *L, void *ws, size_t bytes, Ws &w) {
   if (bytes < ws_bytes(L)) return Q3_ERR_CAPACITY;
   if (reinterpret_cast<uintptr_t>(ws) % 256) return Q3_ERR_ALIGN;
   const size_t pages = L->max_seq / kPageTokens;
-  w.ptab = static_cast<uint16_t *>(ws);
-  w.argmax_ws = static_cast<char *>(ws) + 256 * ((pages * 2 + 255) / 256);
+  char *b = static_cast<char *>(ws);
+  w.ptab = reinterpret_cast<uint16_t *>(b);
+  b += a256(pages * 2);
+  w.argmax_ws = b;
   w.argmax_bytes = 256;
+  b += 256;
+  w.positions = reinterpret_cast<int32_t *>(b);
+  b += a256(4 * static_cast<size_t>(L->max_seq));
+  w.last_id = reinterpret_cast<int32_t *>(b);
+  b += 256;
+  w.dec_ws = b;
+  w.dec_bytes = a256(q3_decode_workspace_bytes(L, 1));
   return Q3_OK;
 }
 
@@ -339,7 +366,21 @@ extern "C" int q3_generate(void *blob, const q3_layout *layout, void *workspace,
   const int pages = layout->max_seq / kPageTokens;
   k_fill_ptab<<<(pages + 127) / 128, 128, 0, st>>>(ws.ptab, pages);
   Q3_TRY(q3h::launch_status());
+  k_iota<<<(layout->max_seq + 255) / 256, 256, 0, st>>>(ws.positions, (int)layout->max_seq);
+  Q3_TRY(q3h::launch_status());
   int32_t *ids = reinterpret_cast<int32_t *>(static_cast<char *>(blob) + layout->off[Q3_OFF_IDS]);
+  // decode steps (one row after the prompt) of the fused mode run the batched
+  // decode kernels with one sequence over the blob's own cache: the cache is a
+  // page pool in the reference's layout and ptab its page table
+  char *kvb = static_cast<char *>(blob) + layout->off[Q3_OFF_KV_BASE];
+  const q3_kv_pool cache{kvb, kvb + layout->off[Q3_OFF_KV_VOFF], kvb + layout->off[Q3_OFF_KV_SOFF],
+                         kvb + layout->off[Q3_OFF_KV_VOFF] + layout->off[Q3_OFF_KV_SOFF],
+                         static_cast<uint64_t>(layout->off[Q3_OFF_KV_STRIDE]),
+                         static_cast<uint64_t>(layout->off[Q3_OFF_KV_STRIDE]),
+                         layout->max_seq / kPageTokens};
+  const bool batched_decode = fused && reinterpret_cast<uintptr_t>(kvb) % 16 == 0 &&
+                              layout->off[Q3_OFF_KV_VOFF] % 16 == 0 &&
+                              layout->off[Q3_OFF_KV_STRIDE] % 16 == 0;
   const int32_t *argi =
       reinterpret_cast<const int32_t *>(static_cast<char *>(blob) + layout->off[Q3_OFF_ARGI]);
   const float *logits0 =
@@ -347,6 +388,17 @@ extern "C" int q3_generate(void *blob, const q3_layout *layout, void *workspace,
   const uint32_t N = layout->seq;
   uint32_t pos = 0;
   while (pos < total) {
+    if (batched_decode && pos >= n_prompt) {
+      // the id picked for the next position goes straight into ids[pos + 1]
+      const bool last = (pos + 1 == total);
+      int32_t *nxt = last ? ws.last_id : ids + pos + 1;
+      Q3_TRY(q3_decode_step_batch(blob, layout, &cache, ws.ptab, layout->max_seq / kPageTokens,
+                                  ids + pos, ws.positions + pos, 1, nxt, ws.dec_ws, ws.dec_bytes,
+                                  st));
+      pos += 1;
+      if (last) Q3_TRY(q3::decode_stages_to_blob(*layout, ws.dec_ws, blob, nxt, st));
+      continue;
+    }
     const uint32_t rows = (pos < n_prompt) ? ((n_prompt - pos < N) ? (n_prompt - pos) : N) : 1;
     const bool need_out = (pos + rows >= n_prompt);
     const int lm_out = need_out ? (fused ? Q3_LM_ARGMAX : Q3_LM_LOGITS) : Q3_LM_NONE;
