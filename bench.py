@@ -447,7 +447,8 @@ def run_ours(args) -> None:
         print(json.dumps(measure_single_sequence(args, q3, lib, dev)), flush=True)
         return
     if args.prefill_only:
-        pf = measure_prefill(args, q3, lib, dev, rank, world, dist)
+        pf = measure_prefill(args, q3, lib, dev, rank, world, dist,
+                             mode="tp" if args.parallel == "tp" else "replicas")
         if dist:
             dist.destroy_process_group()
         if rank == 0:
@@ -498,6 +499,9 @@ def run_ours(args) -> None:
     if not args.no_prefill:
         torch.cuda.empty_cache()
         prefill = measure_prefill(args, q3, lib, dev, rank, world, dist)
+        if world > 1:
+            torch.cuda.empty_cache()
+            prefill["tp"] = measure_prefill(args, q3, lib, dev, rank, world, dist, mode="tp")
     if dist:
         dist.destroy_process_group()
     if rank != 0:
@@ -646,16 +650,24 @@ def prefill_ops(B: int, T: int, layers: int) -> float:
     return float(B) * (T * layers * linear + layers * attn + 2 * H * V)
 
 
-def measure_prefill(args, q3, lib, dev, rank, world, dist) -> dict:
+def measure_prefill(args, q3, lib, dev, rank, world, dist, mode: str = "replicas") -> dict:
+    """One warm-up and one timed batched prefill.  mode "replicas": every rank
+    its own prompts (q3_prefill_batch, no collective); "tp": the SAME prompts
+    split over the ranks (q3_tp_prefill_batch), followed by a bit-exactness
+    check against q3_prefill_batch of the batch on rank 0."""
+    import hashlib
+
     import torch
-    from q3b200 import synthetic
+    from q3b200 import synthetic, tp
     from q3b200.model import Dims
     B, T = args.prefill_seqs, args.prefill_len
+    rseed = rank if mode == "replicas" else 0
     dims = Dims(layers=args.layers, vocab=VOCAB, max_seq=T)
-    bm = synthetic.random_blob_model(dims, seed=4000 + rank, device=dev)
+    bm = synthetic.random_blob_model(dims, seed=4000 + rseed, device=dev)
     pages = B * (T // 32)
-    pool = synthetic.KVPoolTensors(args.layers, pages, 8, device=dev)
-    g = torch.Generator().manual_seed(5000 + rank)
+    shard = tp.shard_of(bm.L, rank, world) if mode == "tp" else tp.shard_of(bm.L, 0, 1)
+    pool = synthetic.KVPoolTensors(args.layers, pages, shard.kv_heads, device=dev)
+    g = torch.Generator().manual_seed(5000 + rseed)
     tables = torch.randperm(pages, generator=g).reshape(B, T // 32).to(torch.int16).to(dev)
     ids = torch.randint(0, VOCAB, (B * T,), generator=g, dtype=torch.int32).to(dev)
     nxt = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -664,11 +676,18 @@ def measure_prefill(args, q3, lib, dev, rank, world, dist) -> dict:
     cpool = pool.c()
     stream = torch.cuda.Stream(device=dev)
 
-    def step():
-        q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
-            bm.blob.data_ptr(), C.byref(bm.L), C.byref(cpool), tables.data_ptr(), T // 32,
-            ids.data_ptr(), B, T, nxt.data_ptr(), ws.data_ptr(), wsb, stream.cuda_stream))
+    comm = tp.TPPrefillComm(bm.L, rank, world, B * T, B) if mode == "tp" else None
 
+    def step():
+        if comm is not None:
+            comm.prefill(bm.blob, bm.L, cpool, tables, T // 32, ids, B, T, nxt, ws, stream)
+        else:
+            q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
+                bm.blob.data_ptr(), C.byref(bm.L), C.byref(cpool), tables.data_ptr(), T // 32,
+                ids.data_ptr(), B, T, nxt.data_ptr(), ws.data_ptr(), wsb, stream.cuda_stream))
+
+    if dist:
+        dist.barrier()
     with torch.cuda.stream(stream):
         step()                                   # warm-up
     torch.cuda.synchronize(dev)
@@ -681,19 +700,75 @@ def measure_prefill(args, q3, lib, dev, rank, world, dist) -> dict:
         e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
+    status = int(lib.q3_device_status())
+    if status != 0:
+        raise RuntimeError(f"device status {status} after the {mode} prefill")
     if dist:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
+    parity = None
+    if comm is not None:
+        def digest(*ts):
+            h = hashlib.sha256()
+            for x in ts:
+                h.update(x.contiguous().cpu().numpy().tobytes())
+            return h.hexdigest()
+        mine = {"ids": digest(nxt), "kv": digest(pool.k, pool.v, pool.ks, pool.vs),
+                "h0": shard.kv_head0, "nh": shard.kv_heads}
+        comm.close()
+        comm = None
+        del pool
+        torch.cuda.empty_cache()
+        every = [None] * world
+        if dist:
+            dist.all_gather_object(every, mine)
+        else:
+            every = [mine]
+        if rank == 0:
+            full = synthetic.KVPoolTensors(args.layers, pages, 8, device=dev)
+            fpool = full.c()
+            ref = torch.zeros(B, dtype=torch.int32, device=dev)
+            q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
+                bm.blob.data_ptr(), C.byref(bm.L), C.byref(fpool), tables.data_ptr(), T // 32,
+                ids.data_ptr(), B, T, ref.data_ptr(), ws.data_ptr(), wsb, stream.cuda_stream))
+            torch.cuda.synchronize(dev)
+
+            def cols(e):
+                a, b = e["h0"], e["h0"] + e["nh"]
+                return digest(full.k[..., a * 128:b * 128], full.v[..., a * 128:b * 128],
+                              full.ks[..., a:b], full.vs[..., a:b])
+            parity = {"ids_equal": all(e["ids"] == digest(ref) for e in every),
+                      "kv_equal": all(e["kv"] == cols(e) for e in every),
+                      "status_clean": int(lib.q3_device_status()) == 0,
+                      "against": "q3_prefill_batch on one GPU, whole pool", "seqs": B, "T": T}
+            del full
+            torch.cuda.empty_cache()
+        if dist:
+            dist.barrier()
     ops = prefill_ops(B, T, args.layers)
     peak = 4500.0   # nominal dense int8 TOPS per B200 (no measured int8 peak on this pool)
-    return {"metric": "prefill tokens/s (config 5)", "value": round(world * B * T / (ms * 1e-3), 1),
-            "unit": "tokens/s", "ms_per_step": round(ms, 2), "steps": 1, "warmup": 1,
-            "config": {"workload": f"config 5: {B} x {T}-token prompts, causal, {args.layers} layers, "
-                                   f"vocab {VOCAB}, greedy next token", "parallelism": f"replicas x{world}"},
-            "roofline": {"bound": "tensor", "achieved": round(ops / (ms * 1e-3) / 1e12, 2),
-                         "peak": peak, "unit": "TOPS (int8)", "frac": round(ops / (ms * 1e-3) / 1e12 / peak, 4),
-                         "ops_per_step": ops, "peak_source": "nominal dense int8 (no measured int8 peak)"}}
+    n_units = (1 if mode == "tp" else world) * B * T
+    out = {"metric": "prefill tokens/s (config 5)", "value": round(n_units / (ms * 1e-3), 1),
+           "unit": "tokens/s", "ms_per_step": round(ms, 2), "steps": 1, "warmup": 1,
+           "config": {"workload": f"config 5: {B} x {T}-token prompts, causal, {args.layers} layers, "
+                                  f"vocab {VOCAB}, greedy next token",
+                      "parallelism": (f"tp{world}: heads, MLP groups, residual columns and "
+                                      "vocabulary split over the ranks, all-gathers over NVLink")
+                      if mode == "tp" else f"replicas x{world}"},
+           "scaling": "strong" if mode == "tp" else "weak"}
+    if mode == "tp":
+        out["tp_parity"] = parity
+        out["roofline"] = {"bound": "tensor", "achieved": round(ops / (ms * 1e-3) / 1e12, 2),
+                           "peak": peak * world, "unit": "TOPS (int8, all GPUs)",
+                           "frac": round(ops / (ms * 1e-3) / 1e12 / (peak * world), 4),
+                           "ops_per_step": ops}
+    else:
+        out["roofline"] = {"bound": "tensor", "achieved": round(ops / (ms * 1e-3) / 1e12, 2),
+                           "peak": peak, "unit": "TOPS (int8)",
+                           "frac": round(ops / (ms * 1e-3) / 1e12 / peak, 4),
+                           "ops_per_step": ops, "peak_source": "nominal dense int8 (no measured int8 peak)"}
+    return out
 
 
 # ---------------------------------------------------------------------------

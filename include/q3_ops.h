@@ -465,6 +465,38 @@ int q3_tp_decode_step_batch(void *comm, void *blob, const q3_layout *layout,
                             uint32_t n_seqs, int32_t *next_ids, void *workspace,
                             size_t workspace_bytes, void *stream);
 
+/* Tensor-parallel batched prefill (config 5 at 2/4/8 GPUs): the layer chain
+ * of q3_prefill_batch split over the ranks, bit-identical to it.  Rank r owns
+ * the q/KV heads and MLP groups of its shard (q3_tp_shard_of), the residual
+ * columns [r*H/world, (r+1)*H/world) and its vocabulary rows.  Per layer:
+ * RMSNorm + quant of the full residual on every rank; V, K and Q GEMMs and
+ * causal attention for the rank's heads (its pool holds only its KV heads);
+ * all-gather of the attention output o8/os; the O GEMM for the rank's residual
+ * columns (every K group summed in the reference's order, group_gemm.h:194-214);
+ * all-gather of x; RMSNorm + quant; gate/up SwiGLU for the rank's groups;
+ * all-gather of s8/ss; down for the rank's columns; all-gather of x.  The last
+ * rows' lm_head runs over the rank's vocabulary rows and the (max, first
+ * index) keys are exchanged, as in the decode step.  Every element is computed
+ * by one rank with the single-GPU arithmetic, so no sum changes order.
+ *
+ * The communicator holds the exchanged buffers of up to max_rows = n_seqs*T
+ * rows and max_seqs sequences (about max_rows * 7.2 KB at the Qwen3-0.6B
+ * shape) in a region every rank maps (CUDA IPC); create / connect / reset /
+ * destroy work like the decode communicator's.  Exchanges are copies into the
+ * other ranks' regions over NVLink, ordered by system-scope counters; a wait
+ * gives up after wait_ns (2 s by default), sets device status bit 20 and
+ * returns.  The workspace is q3_prefill_workspace_bytes(layout, n_seqs, T). */
+int q3_tp_prefill_comm_create(const q3_layout *layout, int32_t rank, int32_t world,
+                              uint32_t max_rows, uint32_t max_seqs, void **comm, void *handle);
+int q3_tp_prefill_comm_connect(void *comm, const void *handles);
+int q3_tp_prefill_comm_reset(void *comm, void *stream);
+int q3_tp_prefill_comm_set_wait_ns(void *comm, uint64_t ns);
+int q3_tp_prefill_comm_destroy(void *comm);
+int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layout,
+                        const q3_kv_pool *pool, const uint16_t *tables, uint32_t max_pages,
+                        const int32_t *ids, uint32_t n_seqs, uint32_t T, int32_t *next_ids,
+                        void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- value ops (include/tile.h exp_/exp2 semantics; tests/guest/value_ops.cpp)
  * out[i] = exp(x[i]) as the path computes it: exp2(f32(x * log2e))
  * (tools/ref_qwen3.py:27-29), or out[i] = exp2(x[i]); both correctly rounded

@@ -14,6 +14,7 @@
 #include "q3_attention.h"
 #include "q3_common.cuh"
 #include "q3_gemm.h"
+#include "q3_tp.h"
 
 namespace {
 
@@ -269,4 +270,194 @@ extern "C" int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv
   Q3_TRY(q3_rmsnorm_rows(&xl, &nf, &hl, inv_h, s));
   Q3_TRY(q3_quant_rows_heads(&hl, &h8l, &hsl, 256, s));
   return q3_gemm_nt_group_argmax(&h8l, &hsl, &lm, &lm_s, w.best, next_ids, 256, w.keys, 8 * B, s);
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-parallel prefill: the same batched prefill with the layer split over
+// the ranks of a q3::PfComm, bit-identical to q3_prefill_batch on one GPU.
+// Rank r owns the KV heads and q heads of its shard (q3_tp_shard_of), the
+// MLP groups of its shard, a slice of H / world residual columns and its
+// vocabulary rows.  Per layer, every rank:
+//   RMSNorm + quant of the full residual x (replicated, same bits everywhere);
+//   V, K (head norm/rope/quant) and Q GEMMs for its heads only, its K/V into
+//   its own page pool, causal attention over its heads -> its o8/os columns;
+//   all-gather of o8/os;
+//   O for its residual columns, every K group summed in the reference's
+//   order by the one GEMM (ref_qwen3.py:152-157) -> its x columns; all-gather;
+//   RMSNorm + quant (replicated); gate/up SwiGLU for its MLP groups -> its
+//   s8/ss columns; all-gather; down for its x columns; all-gather.
+// Every output element is computed by exactly one rank with the single-GPU
+// arithmetic, so no sum changes order.  The exchanges copy each rank's
+// columns into every other rank's region over NVLink (CUDA IPC) and signal
+// with system-scope counters (q3_tp.cu); the last rows' lm_head runs over
+// the rank's vocabulary rows and the (max, first index) keys are exchanged.
+// ---------------------------------------------------------------------------
+extern "C" int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layout,
+                                   const q3_kv_pool *pool, const uint16_t *tables,
+                                   uint32_t max_pages, const int32_t *ids, uint32_t n_seqs,
+                                   uint32_t T, int32_t *next_ids, void *workspace,
+                                   size_t workspace_bytes, void *stream) {
+  if (!comm || !blob || !layout || !pool || !tables || !ids || !next_ids || !workspace)
+    return Q3_ERR_NULL;
+  q3::PfComm &c = *static_cast<q3::PfComm *>(comm);
+  const q3_layout &L = *layout;
+  if (L.head_dim != 128 || L.hidden % 256 || L.inter % 256 || L.max_seq % kPT ||
+      L.hidden != c.hidden || L.heads != c.heads || L.inter != c.inter)
+    return Q3_ERR_SHAPE;
+  if (n_seqs == 0 || T == 0) return Q3_OK;
+  for (int q = 0; q < c.world; ++q)
+    if (!c.peer[q]) return Q3_ERR_NULL;   // not connected
+  if (T > L.max_seq || (size_t)(T + kPT - 1) / kPT > max_pages) return Q3_ERR_CAPACITY;
+  if ((size_t)n_seqs * T > c.max_rows || n_seqs > c.max_seqs) return Q3_ERR_CAPACITY;
+  if ((size_t)n_seqs * T > 0x7fffffffu / L.inter) return Q3_ERR_CAPACITY;
+  if (workspace_bytes < q3_prefill_workspace_bytes(layout, n_seqs, T)) return Q3_ERR_CAPACITY;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256) return Q3_ERR_ALIGN;
+  if (!pool->k || !pool->v || !pool->ks || !pool->vs || pool->num_pages == 0) return Q3_ERR_NULL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void *s = st;
+  const int64_t *o = L.off;
+  const q3_tp_shard &sh = c.shard[c.rank];
+  const uint32_t B = n_seqs, H = L.hidden, HD = L.head_dim, QW = L.heads * HD, I = L.inter,
+                 V = L.vocab, HALF = HD / 2, HEADS = L.heads, G = I / 256;
+  const uint32_t QH = sh.q_heads, KVH = sh.kv_heads, QWl = QH * HD, KWl = KVH * HD;
+  const uint32_t c0 = c.col0[c.rank], NC = c.cols[c.rank];
+  const uint32_t g0 = sh.mlp_group0, NG = sh.mlp_groups;
+  const uint32_t M = B * T;
+  char *bl = static_cast<char *>(blob);
+  PrefillWs w = carve(L, M, B, static_cast<char *>(workspace));
+  char *R = c.local;
+  int8_t *o8f = reinterpret_cast<int8_t *>(R + c.off_o8);
+  float *osf = reinterpret_cast<float *>(R + c.off_os);
+  float *xf = reinterpret_cast<float *>(R + c.off_x);
+  int8_t *s8f = reinterpret_cast<int8_t *>(R + c.off_s8);
+  float *ssf = reinterpret_cast<float *>(R + c.off_ss);
+
+  k_prefill_rope_rows<<<M, 64, 0, st>>>(reinterpret_cast<const float *>(bl + o[Q3_OFF_COS]),
+                                        reinterpret_cast<const float *>(bl + o[Q3_OFF_SIN]), HALF,
+                                        T, w.cos, w.sin);
+  Q3_TRY(q3h::launch_status());
+
+  const q3_view x = v2(xf, M, H, Q3_DT_F32), h = v2(w.h, M, H, Q3_DT_F32);
+  const q3_view h8 = v2(w.h8, M, H, Q3_DT_I8), hs = v2(w.hs, M, H / 256, Q3_DT_F32);
+  const q3_view q8 = v2(w.q8, M, QWl, Q3_DT_I8), qs = v2(w.qs, M, QH, Q3_DT_F32);
+  const q3_view k8 = v2(w.k8, M, KWl, Q3_DT_I8), ks = v2(w.ks, M, KVH, Q3_DT_F32);
+  const q3_view v8 = v2(w.v8, M, KWl, Q3_DT_I8), vs = v2(w.vs, M, KVH, Q3_DT_F32);
+  const q3_view o8 = v2(o8f, M, QW, Q3_DT_I8), os = v2(osf, M, HEADS, Q3_DT_F32);
+  const q3_view s8 = v2(s8f, M, I, Q3_DT_I8), ss = v2(ssf, M, G, Q3_DT_F32);
+  // this rank's columns of the exchanged buffers
+  q3_view xc = v2(xf + c0, M, NC, Q3_DT_F32);
+  xc.row_bytes = static_cast<int32_t>(4 * H);
+  q3_view s8c = v2(s8f + g0 * 256, M, NG * 256, Q3_DT_I8);
+  s8c.row_bytes = static_cast<int32_t>(I);
+  q3_view ssc = v2(ssf + g0, M, NG, Q3_DT_F32);
+  ssc.row_bytes = static_cast<int32_t>(4 * G);
+  const q3_view cosv = v2(w.cos, M, HALF, Q3_DT_F32), sinv = v2(w.sin, M, HALF, Q3_DT_F32);
+  const q3_view idv = v2(const_cast<int32_t *>(ids), M, 1, Q3_DT_I32);
+  const q3_view emb = v2(bl + o[Q3_OFF_EMB], V, H, Q3_DT_I8);
+  const q3_view emb_s = v2(bl + o[Q3_OFF_EMB] + (int64_t)V * H, V, 1, Q3_DT_F32);
+  const q3_view lm = v2(bl + o[Q3_OFF_LM] + (int64_t)sh.vocab0 * H, sh.vocab_rows, H, Q3_DT_I8);
+  const q3_view lm_s = v2(bl + o[Q3_OFF_LM] + (int64_t)V * H + (int64_t)sh.vocab0 * 4,
+                          sh.vocab_rows, 1, Q3_DT_F32);
+  const q3_view nf = v2(bl + o[Q3_OFF_NF], H, 1, Q3_DT_F32);
+  const float inv_h = 1.0f / static_cast<float>(H), inv_hd = 1.0f / static_cast<float>(HD);
+  const q3::PfSeg seg_o8{c.off_o8, sh.q_head0 * HD, QWl, QW};
+  const q3::PfSeg seg_os{c.off_os, sh.q_head0 * 4, QH * 4, HEADS * 4};
+  const q3::PfSeg seg_x{c.off_x, c0 * 4, NC * 4, H * 4};
+  const q3::PfSeg seg_s8{c.off_s8, g0 * 256, NG * 256, I};
+  const q3::PfSeg seg_ss{c.off_ss, g0 * 4, NG * 4, G * 4};
+
+  {
+    const q3_view n1_0 = v2(bl + o[Q3_OFF_N1], H, 1, Q3_DT_F32);
+    Q3_TRY(q3_embedding_rmsnorm_rows(&emb, &emb_s, &idv, &x, &n1_0, &h, inv_h, s));
+  }
+  for (uint32_t Li = 0; Li < L.layers; ++Li) {
+    char *lw = bl + o[Q3_OFF_LQ] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERW_STRIDE];
+    char *ln = bl + o[Q3_OFF_N1] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERN_STRIDE];
+    // rows [r0, r0 + r) of a weight matrix (K = c columns) and of its scales
+    auto W = [&](int key, uint32_t r0, uint32_t r, uint32_t cc) {
+      return v2(lw + (o[key] - o[Q3_OFF_LQ]) + static_cast<int64_t>(r0) * cc, r, cc, Q3_DT_I8);
+    };
+    auto S = [&](int key, uint32_t r0, uint32_t r) {
+      return v2(lw + (o[key] - o[Q3_OFF_LQ]) + static_cast<int64_t>(r0) * 4, r, 1, Q3_DT_F32);
+    };
+    const q3_view wq = W(Q3_OFF_LQ, sh.q_head0 * HD, QWl, H), wqs = S(Q3_OFF_LQ_SCALE, sh.q_head0 * HD, QWl);
+    const q3_view wk = W(Q3_OFF_LK, sh.kv_head0 * HD, KWl, H), wks = S(Q3_OFF_LK_SCALE, sh.kv_head0 * HD, KWl);
+    const q3_view wv = W(Q3_OFF_LV, sh.kv_head0 * HD, KWl, H), wvs = S(Q3_OFF_LV_SCALE, sh.kv_head0 * HD, KWl);
+    const q3_view wo = W(Q3_OFF_LO, c0, NC, QW), wos = S(Q3_OFF_LO_SCALE, c0, NC);
+    const q3_view wg = W(Q3_OFF_LG, g0 * 256, NG * 256, H), wgs = S(Q3_OFF_LG_SCALE, g0 * 256, NG * 256);
+    const q3_view wu = W(Q3_OFF_LU, g0 * 256, NG * 256, H), wus = S(Q3_OFF_LU_SCALE, g0 * 256, NG * 256);
+    const q3_view wd = W(Q3_OFF_LD, c0, NC, I), wds = S(Q3_OFF_LD_SCALE, c0, NC);
+    const q3_view n1 = v2(ln, H, 1, Q3_DT_F32);
+    const q3_view nq = v2(ln + (o[Q3_OFF_NQ] - o[Q3_OFF_N1]), HD, 1, Q3_DT_F32);
+    const q3_view nk = v2(ln + (o[Q3_OFF_NK] - o[Q3_OFF_N1]), HD, 1, Q3_DT_F32);
+    const q3_view n2 = v2(ln + (o[Q3_OFF_N2] - o[Q3_OFF_N1]), H, 1, Q3_DT_F32);
+    char *pk = static_cast<char *>(pool->k) + Li * pool->layer_stride;
+    char *pv = static_cast<char *>(pool->v) + Li * pool->layer_stride;
+    char *pks = static_cast<char *>(pool->ks) + Li * pool->scale_layer_stride;
+    char *pvs = static_cast<char *>(pool->vs) + Li * pool->scale_layer_stride;
+
+    if (Li != 0) Q3_TRY(q3_rmsnorm_rows(&x, &n1, &h, inv_h, s));
+    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wv, &wvs, nullptr, 256, nullptr, &v8, &vs, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wk, &wks, nullptr, 256, nullptr, &k8, &ks, &nk,
+                                  &cosv, &sinv, inv_hd, s));
+    k_prefill_scatter<<<M, 64, 0, st>>>(w.k8, w.v8, w.ks, w.vs, tables, max_pages, (int)T, pk, pv,
+                                        pks, pvs, KWl, KVH);
+    Q3_TRY(q3h::launch_status());
+    Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wq, &wqs, nullptr, 256, nullptr, &q8, &qs, &nq, &cosv,
+                                  &sinv, inv_hd, s));
+    {
+      q3::PrefillAttnArgs a{};
+      a.qs = reinterpret_cast<const char *>(w.qs);
+      a.qs_rb = 4 * QH;
+      a.o8 = reinterpret_cast<char *>(o8f + sh.q_head0 * HD);
+      a.o_rb = QW;
+      a.os = reinterpret_cast<char *>(osf + sh.q_head0);
+      a.os_rb = 4 * HEADS;
+      a.ks = pks;
+      a.vs = pvs;
+      a.table = tables;
+      a.table_stride = max_pages;
+      a.scale_page_bytes = kPT * 4 * KVH;
+      a.scale_row_bytes = 4 * KVH;
+      a.num_pages = pool->num_pages;
+      a.heads = (int)QH;
+      a.kv_heads = (int)KVH;
+      a.T = (int)T;
+      a.qk_scale = kInvSqrt128;
+      Q3_TRY(q3::attention_prefill_launch(a, w.q8, QWl, (int)M, pk, pv, kPT * KWl, KWl, (int)B, st));
+    }
+    {
+      const q3::PfSeg sg[2] = {seg_o8, seg_os};
+      Q3_TRY(q3::pf_push(c, q3::PF_O, sg, 2, M, st));
+      Q3_TRY(q3::pf_wait(c, q3::PF_O, st));
+    }
+    Q3_TRY(q3_gemm_nt_group_store(&o8, &os, &wo, &wos, nullptr, 128, &xc, nullptr, nullptr, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+    Q3_TRY(q3::pf_push(c, q3::PF_XO, &seg_x, 1, M, st));
+    Q3_TRY(q3::pf_wait(c, q3::PF_XO, st));
+    Q3_TRY(q3_rmsnorm_rows(&x, &n2, &h, inv_h, s));
+    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    Q3_TRY(q3_gemm_gate_up_swiglu_quant(&h8, &hs, &wg, &wgs, &wu, &wus, &s8c, &ssc, 256, s));
+    {
+      const q3::PfSeg sg[2] = {seg_s8, seg_ss};
+      Q3_TRY(q3::pf_push(c, q3::PF_S, sg, 2, M, st));
+      Q3_TRY(q3::pf_wait(c, q3::PF_S, st));
+    }
+    Q3_TRY(q3_gemm_nt_group_store(&s8, &ss, &wd, &wds, nullptr, 256, &xc, nullptr, nullptr, nullptr,
+                                  nullptr, nullptr, 0.0f, s));
+    Q3_TRY(q3::pf_push(c, q3::PF_XD, &seg_x, 1, M, st));
+    Q3_TRY(q3::pf_wait(c, q3::PF_XD, st));
+  }
+  // last row of every sequence: final norm + quant (replicated), lm_head over
+  // this rank's vocabulary rows, then the key exchange
+  k_prefill_last_rows<<<B, 256, 0, st>>>(xf, (int)T, (int)H, w.xl, w.best, next_ids);
+  Q3_TRY(q3h::launch_status());
+  const q3_view xl = v2(w.xl, B, H, Q3_DT_F32), hl = v2(w.hl, B, H, Q3_DT_F32);
+  const q3_view h8l = v2(w.h8l, B, H, Q3_DT_I8), hsl = v2(w.hsl, B, H / 256, Q3_DT_F32);
+  Q3_TRY(q3_rmsnorm_rows(&xl, &nf, &hl, inv_h, s));
+  Q3_TRY(q3_quant_rows_heads(&hl, &h8l, &hsl, 256, s));
+  Q3_TRY(q3_gemm_nt_group_argmax(&h8l, &hsl, &lm, &lm_s, w.best, next_ids, 256, w.keys, 8 * B, s));
+  return q3::pf_argmax_exchange(c, w.best, next_ids, sh.vocab0, (int)B, st);
 }

@@ -154,7 +154,160 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 __global__ void k_tp_expect_add(unsigned *expect, unsigned count) { *expect += count; }
 
+// ---- prefill exchanges
+struct PfPushArgs {
+  const char *src;                  // this rank's region
+  char *dst[kTpMaxRanks];           // every rank's region as mapped here
+  unsigned *sig[kTpMaxRanks];       // rank q's counter of (exchange, this rank)
+  PfSeg seg[2];
+  int nseg, world, me;
+  uint32_t rows;
+};
+
+// rows are spread over the CTAs; a row's segment goes to every other rank in
+// 16-byte words when the segment allows it, else in 4-byte words.  Each CTA
+// then fences its stores at system scope, passes a barrier, and one thread
+// adds 1 (release, system scope) to this rank's counter at every rank.
+__global__ void __launch_bounds__(256) k_pf_push(PfPushArgs a) {
+  for (int si = 0; si < a.nseg; ++si) {
+    const PfSeg sg = a.seg[si];
+    const bool v16 = (sg.offset % 16 == 0) && (sg.width % 16 == 0) && (sg.row_bytes % 16 == 0) &&
+                     (sg.base % 16 == 0);
+    const uint32_t words = v16 ? sg.width / 16 : sg.width / 4;
+    const size_t total = static_cast<size_t>(a.rows) * words;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+      const size_t r = i / words, w = i % words;
+      const size_t off = sg.base + r * sg.row_bytes + sg.offset + w * (v16 ? 16 : 4);
+      if (v16) {
+        const int4 v = __ldcg(reinterpret_cast<const int4 *>(a.src + off));
+        for (int q = 0; q < a.world; ++q)
+          if (q != a.me) *reinterpret_cast<int4 *>(a.dst[q] + off) = v;
+      } else {
+        const int v = __ldcg(reinterpret_cast<const int *>(a.src + off));
+        for (int q = 0; q < a.world; ++q)
+          if (q != a.me) *reinterpret_cast<int *>(a.dst[q] + off) = v;
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int q = 0; q < a.world; ++q) sys_signal(a.sig[q]);
+}
+
+__global__ void k_pf_wait(const unsigned *sig, int world, unsigned target, unsigned long long wait_ns) {
+  const int q = threadIdx.x;
+  if (q < world && !wait_count(sig + q, target, wait_ns)) atomicOr(&g_tp_error, kErrTpWait);
+}
+
+struct PfKeyArgs {
+  const float *best;
+  int32_t *idx;                                // in: local index; out: the greedy id
+  uint32_t v0;
+  int B, world, me, max_seqs;
+  unsigned long long *keys_dst[kTpMaxRanks];   // rank q's key buffer [ranks][max_seqs]
+  unsigned *sig_dst[kTpMaxRanks];              // rank q's counter of (PF_KEYS, me)
+  const unsigned long long *keys;              // this rank's key buffer
+  const unsigned *sig;                         // this rank's counters of PF_KEYS
+  unsigned target;
+  unsigned long long wait_ns;
+};
+
+// (max, first index) of every rank's vocabulary slice as one key (monotone
+// value << 32 | ~global index): the largest key is the first maximum of the
+// whole row, as np.argmax picks it (ref_qwen3.py:447-464).  One CTA, thread i =
+// sequence i.
+__global__ void __launch_bounds__(256) k_pf_argmax_exchange(PfKeyArgs a) {
+  const int i = threadIdx.x;
+  if (i < a.B) {
+    const float v = __fadd_rn(a.best[i], 0.0f);
+    const unsigned b = __float_as_uint(v);
+    const unsigned key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    const unsigned long long k = (static_cast<unsigned long long>(key) << 32) |
+                                 (0xffffffffu - (static_cast<unsigned>(a.idx[i]) + a.v0));
+    for (int q = 0; q < a.world; ++q) a.keys_dst[q][a.me * a.max_seqs + i] = k;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (i == 0)
+    for (int q = 0; q < a.world; ++q) sys_signal(a.sig_dst[q]);
+  if (i < a.world && !wait_count(a.sig + i, a.target, a.wait_ns)) atomicOr(&g_tp_error, kErrTpWait);
+  __syncthreads();
+  if (i < a.B) {
+    unsigned long long best = 0ull;
+    for (int q = 0; q < a.world; ++q) {
+      const unsigned long long k = __ldcg(a.keys + q * a.max_seqs + i);
+      best = k > best ? k : best;
+    }
+    a.idx[i] = static_cast<int32_t>(0xffffffffu - static_cast<unsigned>(best & 0xffffffffu));
+  }
+}
+
 }  // namespace
+
+unsigned *pf_sig(const PfComm &c, int q, int ex, int producer) {
+  return reinterpret_cast<unsigned *>(c.peer[q] + c.off_sig) + ex * kTpMaxRanks + producer;
+}
+
+int pf_push(PfComm &c, int ex, const PfSeg *segs, int nseg, uint32_t rows, cudaStream_t s) {
+  if (nseg < 1 || nseg > 2) return Q3_ERR_SHAPE;
+  PfPushArgs a{};
+  a.src = c.local;
+  for (int q = 0; q < c.world; ++q) {
+    a.dst[q] = c.peer[q];
+    a.sig[q] = pf_sig(c, q, ex, c.rank);
+  }
+  for (int i = 0; i < nseg; ++i) {
+    if (segs[i].width % 4 || segs[i].offset % 4 || segs[i].row_bytes % 4 || segs[i].base % 4)
+      return Q3_ERR_ALIGN;
+    a.seg[i] = segs[i];
+  }
+  a.nseg = nseg;
+  a.world = c.world;
+  a.me = c.rank;
+  a.rows = rows;
+  c.gen[ex] += 1;
+  q3h::timer_begin(q3h::TIMER_EXCHANGE, s);
+  k_pf_push<<<kPfPushCtas, 256, 0, s>>>(a);
+  const int st = q3h::launch_status();
+  q3h::timer_end(q3h::TIMER_EXCHANGE, s);
+  return st;
+}
+
+int pf_wait(const PfComm &c, int ex, cudaStream_t s) {
+  q3h::timer_begin(q3h::TIMER_EXCHANGE, s);
+  k_pf_wait<<<1, 32, 0, s>>>(pf_sig(c, c.rank, ex, 0), c.world, c.gen[ex] * kPfPushCtas, c.wait_ns);
+  const int st = q3h::launch_status();
+  q3h::timer_end(q3h::TIMER_EXCHANGE, s);
+  return st;
+}
+
+int pf_argmax_exchange(PfComm &c, const float *best, int32_t *idx, uint32_t v0, int B, cudaStream_t s) {
+  if (B < 1 || B > 256 || static_cast<uint32_t>(B) > c.max_seqs) return Q3_ERR_SHAPE;
+  PfKeyArgs a{};
+  a.best = best;
+  a.idx = idx;
+  a.v0 = v0;
+  a.B = B;
+  a.world = c.world;
+  a.me = c.rank;
+  a.max_seqs = static_cast<int>(c.max_seqs);
+  for (int q = 0; q < c.world; ++q) {
+    a.keys_dst[q] = reinterpret_cast<unsigned long long *>(c.peer[q] + c.off_keys);
+    a.sig_dst[q] = pf_sig(c, q, PF_KEYS, c.rank);
+  }
+  a.keys = reinterpret_cast<const unsigned long long *>(c.local + c.off_keys);
+  a.sig = pf_sig(c, c.rank, PF_KEYS, 0);
+  c.gen[PF_KEYS] += 1;
+  a.target = c.gen[PF_KEYS];
+  a.wait_ns = c.wait_ns;
+  q3h::timer_begin(q3h::TIMER_EXCHANGE, s);
+  k_pf_argmax_exchange<<<1, 256, 0, s>>>(a);
+  const int st = q3h::launch_status();
+  q3h::timer_end(q3h::TIMER_EXCHANGE, s);
+  return st;
+}
 
 int tp_reduce_norm(const TpReduceArgs &a, cudaStream_t s) {
   if (a.H != 1024 || a.B < 1 || a.slots < 1 || a.slots > kTpMaxSlots || a.world < 1 ||
@@ -319,6 +472,107 @@ extern "C" int q3_tp_comm_inject_missing_signals(void *comm, int32_t buf, int32_
   q3::k_tp_expect_add<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(
       q3::tp_expect(*c, buf) + producer, count);
   return q3h::launch_status();
+}
+
+// ---- tensor-parallel prefill communicator
+extern "C" int q3_tp_prefill_comm_create(const q3_layout *L, int32_t rank, int32_t world,
+                                         uint32_t max_rows, uint32_t max_seqs, void **comm,
+                                         void *handle) {
+  if (!L || !comm || !handle) return Q3_ERR_NULL;
+  *comm = nullptr;
+  if (world < 1 || world > q3::kTpMaxRanks || rank < 0 || rank >= world) return Q3_ERR_SHAPE;
+  if (max_rows < 1 || max_seqs < 1 || max_seqs > 256 || L->head_dim != 128 ||
+      L->hidden % (128u * static_cast<uint32_t>(world)) || L->inter % 256)
+    return Q3_ERR_SHAPE;
+  q3::PfComm *c = new (std::nothrow) q3::PfComm{};
+  if (!c) return Q3_ERR_CAPACITY;
+  for (int q = 0; q < world; ++q) {
+    const int st = q3_tp_shard_of(L, q, world, &c->shard[q]);
+    if (st != Q3_OK) {
+      delete c;
+      return st;
+    }
+    c->cols[q] = L->hidden / static_cast<uint32_t>(world);
+    c->col0[q] = static_cast<uint32_t>(q) * c->cols[q];
+  }
+  c->rank = rank;
+  c->world = world;
+  c->max_rows = max_rows;
+  c->max_seqs = max_seqs;
+  c->hidden = L->hidden;
+  c->heads = L->heads;
+  c->inter = L->inter;
+  c->wait_ns = q3::kTpDefaultWaitNs;
+  const size_t M = max_rows, QW = static_cast<size_t>(L->heads) * 128;
+  size_t off = 4096;                                   // counters
+  c->off_sig = 0;
+  c->off_o8 = off;   off = q3::align256(off + M * QW);
+  c->off_os = off;   off = q3::align256(off + M * L->heads * 4);
+  c->off_x = off;    off = q3::align256(off + M * L->hidden * 4);
+  c->off_s8 = off;   off = q3::align256(off + M * L->inter);
+  c->off_ss = off;   off = q3::align256(off + M * (L->inter / 256) * 4);
+  c->off_keys = off; off = q3::align256(off + static_cast<size_t>(q3::kTpMaxRanks) * max_seqs * 8);
+  c->bytes = off;
+  cudaError_t e = cudaMalloc(&c->local, c->bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->local, 0, 4096);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t *>(handle), c->local);
+  if (e != cudaSuccess) {
+    if (c->local) cudaFree(c->local);
+    delete c;
+    q3h::set_cuda_error(e);
+    return Q3_ERR_CUDA;
+  }
+  c->peer[rank] = c->local;
+  *comm = c;
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_prefill_comm_connect(void *comm, const void *handles) {
+  if (!comm || !handles) return Q3_ERR_NULL;
+  q3::PfComm *c = static_cast<q3::PfComm *>(comm);
+  const cudaIpcMemHandle_t *h = static_cast<const cudaIpcMemHandle_t *>(handles);
+  for (int q = 0; q < c->world; ++q) {
+    if (q == c->rank || c->opened[q]) continue;
+    void *p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h[q], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      q3h::set_cuda_error(e);
+      return Q3_ERR_CUDA;
+    }
+    c->peer[q] = static_cast<char *>(p);
+    c->opened[q] = true;
+  }
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_prefill_comm_reset(void *comm, void *stream) {
+  if (!comm) return Q3_ERR_NULL;
+  q3::PfComm *c = static_cast<q3::PfComm *>(comm);
+  const cudaError_t e = cudaMemsetAsync(c->local, 0, 4096, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    q3h::set_cuda_error(e);
+    return Q3_ERR_CUDA;
+  }
+  for (int i = 0; i < q3::PF_NEX; ++i) c->gen[i] = 0;
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_prefill_comm_set_wait_ns(void *comm, uint64_t ns) {
+  if (!comm) return Q3_ERR_NULL;
+  if (ns < 1000000ull || ns > 60000000000ull) return Q3_ERR_SHAPE;
+  static_cast<q3::PfComm *>(comm)->wait_ns = ns;
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_prefill_comm_destroy(void *comm) {
+  if (!comm) return Q3_OK;
+  q3::PfComm *c = static_cast<q3::PfComm *>(comm);
+  for (int q = 0; q < c->world; ++q)
+    if (c->opened[q]) cudaIpcCloseMemHandle(c->peer[q]);
+  if (c->local) cudaFree(c->local);
+  delete c;
+  return Q3_OK;
 }
 
 extern "C" int q3_tp_comm_destroy(void *comm) {

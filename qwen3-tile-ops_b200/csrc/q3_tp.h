@@ -62,4 +62,39 @@ int tp_argmax_exchange(const TpComm &c, const float *best, const int32_t *bidx, 
 
 int tp_device_status_take();
 
+// ---- tensor-parallel prefill (q3_tp_prefill_batch) --------------------------
+// Exchanges of one prefill layer, all all-gathers: the attention output o8/os
+// of each rank's q heads, the residual columns x after O and after down, the
+// SwiGLU output s8/ss of each rank's MLP groups; then the argmax keys.
+enum PfEx { PF_O = 0, PF_XO = 1, PF_S = 2, PF_XD = 3, PF_KEYS = 4, PF_NEX = 5 };
+constexpr int kPfPushCtas = 264;     // CTAs of every push (all ranks use the same count)
+
+struct PfComm {
+  int rank, world;
+  uint32_t max_rows, max_seqs, hidden, heads, inter;
+  char *local;                    // this rank's region (cudaMalloc)
+  char *peer[kTpMaxRanks];
+  bool opened[kTpMaxRanks];
+  size_t bytes, off_sig, off_o8, off_os, off_x, off_s8, off_ss, off_keys;
+  unsigned gen[PF_NEX];           // rounds of each exchange so far (host count)
+  unsigned long long wait_ns;
+  q3_tp_shard shard[kTpMaxRanks];
+  uint32_t col0[kTpMaxRanks], cols[kTpMaxRanks];   // residual columns of each rank
+};
+
+// a row slice [offset, offset + width) bytes of rows 0..rows-1 of a buffer with
+// row stride row_bytes that every rank holds at the same region offset
+struct PfSeg {
+  size_t base;                    // region offset of the buffer
+  uint32_t offset, width, row_bytes;
+};
+// copy this rank's segments into every other rank's region, then signal
+// exchange `ex` at every rank (this one included); wait_pf blocks the stream
+// until every rank's round `gen` of `ex` has arrived here
+int pf_push(PfComm &c, int ex, const PfSeg *segs, int nseg, uint32_t rows, cudaStream_t s);
+int pf_wait(const PfComm &c, int ex, cudaStream_t s);
+// every rank's (best, index in its vocabulary slice) of each sequence -> the greedy id
+int pf_argmax_exchange(PfComm &c, const float *best, int32_t *idx_then_ids, uint32_t v0, int B,
+                       cudaStream_t s);
+
 }  // namespace q3

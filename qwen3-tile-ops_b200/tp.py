@@ -59,9 +59,21 @@ def _bind():
     h.q3_tp_comm_set_wait_ns.argtypes = [C.c_void_p, C.c_uint64]
     h.q3_tp_comm_inject_missing_signals.argtypes = [C.c_void_p, C.c_int32, C.c_int32, C.c_uint32,
                                                     C.c_void_p]
+    h.q3_tp_prefill_comm_create.argtypes = [C.POINTER(Layout), C.c_int32, C.c_int32, C.c_uint32,
+                                            C.c_uint32, C.POINTER(C.c_void_p), C.c_void_p]
+    h.q3_tp_prefill_comm_connect.argtypes = [C.c_void_p, C.c_void_p]
+    h.q3_tp_prefill_comm_reset.argtypes = [C.c_void_p, C.c_void_p]
+    h.q3_tp_prefill_comm_set_wait_ns.argtypes = [C.c_void_p, C.c_uint64]
+    h.q3_tp_prefill_comm_destroy.argtypes = [C.c_void_p]
+    h.q3_tp_prefill_batch.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(Layout), C.c_void_p,
+                                      C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32, C.c_uint32,
+                                      C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
     for name in ("q3_tp_shard_of", "q3_tp_comm_create", "q3_tp_comm_connect", "q3_tp_comm_reset",
                  "q3_tp_comm_destroy", "q3_tp_decode_step_batch", "q3_tp_comm_set_wait_ns",
-                 "q3_tp_comm_inject_missing_signals"):
+                 "q3_tp_comm_inject_missing_signals", "q3_tp_prefill_comm_create",
+                 "q3_tp_prefill_comm_connect", "q3_tp_prefill_comm_reset",
+                 "q3_tp_prefill_comm_set_wait_ns", "q3_tp_prefill_comm_destroy",
+                 "q3_tp_prefill_batch"):
         getattr(h, name).restype = C.c_int
     h._q3_tp_bound = True
     return h
@@ -144,4 +156,74 @@ class TPComm:
             self._barrier()
             torch.cuda.synchronize()
             check("q3_tp_comm_destroy", _bind().q3_tp_comm_destroy(self.ptr))
+            self.ptr = C.c_void_p()
+
+
+def _gather_handles(handle, hb: int, world: int, group) -> "C.Array":
+    handles = (C.c_ubyte * (hb * world))()
+    if world == 1:
+        C.memmove(handles, handle, hb)
+        return handles
+    import torch.distributed as dist
+    dev = torch.device("cuda", torch.cuda.current_device()) \
+        if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=dev)
+    every = torch.empty(hb * world, dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(every, mine, group=group)
+    C.memmove(handles, bytes(every.cpu().tolist()), hb * world)
+    return handles
+
+
+class TPPrefillComm:
+    """One rank's communicator of the tensor-parallel prefill
+    (``q3_tp_prefill_batch``): the exchanged o8/os, x and s8/ss buffers of up
+    to ``max_rows`` prompt rows, mapped by every rank.  Collective over
+    ``group`` (default: the default process group)."""
+
+    def __init__(self, layout: Layout, rank: int, world: int, max_rows: int, max_seqs: int,
+                 group=None):
+        h = _bind()
+        self.layout, self.rank, self.world, self.group = layout, rank, world, group
+        self.shard = shard_of(layout, rank, world)
+        hb = h.q3_tp_handle_bytes()
+        handle = (C.c_ubyte * hb)()
+        self.ptr = C.c_void_p()
+        check("q3_tp_prefill_comm_create",
+              h.q3_tp_prefill_comm_create(C.byref(layout), rank, world, max_rows, max_seqs,
+                                          C.byref(self.ptr), handle))
+        handles = _gather_handles(handle, hb, world, group)
+        check("q3_tp_prefill_comm_connect", h.q3_tp_prefill_comm_connect(self.ptr, handles))
+        self._barrier()
+
+    def _barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier(group=self.group)
+
+    def prefill(self, blob: torch.Tensor, layout: Layout, pool, tables: torch.Tensor,
+                max_pages: int, ids: torch.Tensor, n_seqs: int, T: int, next_ids: torch.Tensor,
+                ws: torch.Tensor, stream) -> None:
+        """Enqueue this rank's share of one batched prefill (``pool`` = KVPool
+        of this rank's KV heads); every rank passes the same ids and tables."""
+        check("q3_tp_prefill_batch", _bind().q3_tp_prefill_batch(
+            self.ptr, blob.data_ptr(), C.byref(layout), C.byref(pool), tables.data_ptr(),
+            max_pages, ids.data_ptr(), n_seqs, T, next_ids.data_ptr(), ws.data_ptr(),
+            ws.numel(), stream.cuda_stream))
+
+    def set_wait_ns(self, ns: int) -> None:
+        check("q3_tp_prefill_comm_set_wait_ns",
+              _bind().q3_tp_prefill_comm_set_wait_ns(self.ptr, int(ns)))
+
+    def reset(self) -> None:
+        """Zero every rank's counters (no prefill may be in flight)."""
+        self._barrier()
+        check("q3_tp_prefill_comm_reset", _bind().q3_tp_prefill_comm_reset(self.ptr, None))
+        torch.cuda.synchronize()
+        self._barrier()
+
+    def close(self) -> None:
+        if self.ptr:
+            self._barrier()
+            torch.cuda.synchronize()
+            check("q3_tp_prefill_comm_destroy", _bind().q3_tp_prefill_comm_destroy(self.ptr))
             self.ptr = C.c_void_p()

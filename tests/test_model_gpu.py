@@ -198,9 +198,11 @@ def test_decode_step_batch(q3, layers, vocab, lens, tp_world1):
 
 
 # ---------------------------------------------------------------- batched prefill
-def _prefill_case(q3, layers, vocab, B, T, seed=0):
+def _prefill_case(q3, layers, vocab, B, T, seed=0, tp_world1=False):
     """Prefill B prompts of T tokens on the oracle (32-row chunks) and in ONE
-    batched GPU prefill into a shared page pool under shuffled page tables."""
+    batched GPU prefill into a shared page pool under shuffled page tables.
+    ``tp_world1``: through the tensor-parallel entry point with a one-rank
+    communicator (its exchange kernels run, with no peers)."""
     shape = synth.Shape(layers=layers, vocab=vocab, max_seq=(T + 31) // 32 * 32)
     w = synth.build_model(shape)
     rng = np.random.default_rng(seed)
@@ -235,19 +237,28 @@ def _prefill_case(q3, layers, vocab, B, T, seed=0):
     lib = q3._lib.lib()
     wsb = lib.q3_prefill_workspace_bytes(C.byref(bm.L), B, T)
     ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
-    q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
-        bm.blob.data_ptr(), C.byref(bm.L), C.byref(pool), tab.data_ptr(), max_pages,
-        ids_d.data_ptr(), B, T, nxt.data_ptr(), ws.data_ptr(), wsb,
-        torch.cuda.current_stream().cuda_stream))
+    if tp_world1:
+        from q3b200 import tp
+        comm = tp.TPPrefillComm(bm.L, 0, 1, B * T, B)
+        comm.prefill(bm.blob, bm.L, pool, tab, max_pages, ids_d, B, T, nxt, ws,
+                     torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        comm.close()
+    else:
+        q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
+            bm.blob.data_ptr(), C.byref(bm.L), C.byref(pool), tab.data_ptr(), max_pages,
+            ids_d.data_ptr(), B, T, nxt.data_ptr(), ws.data_ptr(), wsb,
+            torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     assert q3._lib.lib().q3_device_status() == 0
     return (nxt.cpu().numpy(), want_ids, {k: v.cpu().numpy() for k, v in d.items()}, tables,
             want_kv)
 
 
+@pytest.mark.parametrize("tp_world1", [False, True], ids=["single", "tp1"])
 @pytest.mark.parametrize("layers,vocab,B,T", [(1, 1024, 3, 70), (2, 4096, 2, 128), (1, 1024, 2, 300)])
-def test_prefill_batch(q3, layers, vocab, B, T):
-    got, want, pool, tables, kvs = _prefill_case(q3, layers, vocab, B, T)
+def test_prefill_batch(q3, layers, vocab, B, T, tp_world1):
+    got, want, pool, tables, kvs = _prefill_case(q3, layers, vocab, B, T, tp_world1=tp_world1)
     assert list(got) == want
     for s in range(B):                    # every prompt row of every layer, un-paged
         for L in range(layers):

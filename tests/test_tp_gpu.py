@@ -206,3 +206,119 @@ def test_tp_wait_timeout_then_reset(q3, buf):
         assert nxt.cpu().tolist() == want
     finally:
         comm.close()
+
+
+PB, PT, PLAYERS = 3, 150, 2
+
+
+def _run_prefill_rank(rank, world, port, out_dir):
+    import ctypes as C
+    import datetime
+    import os
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(repo))
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    comm = None
+    try:
+        import __graft_entry__ as ge
+        q3 = ge.load_package()
+        from q3b200 import synthetic, tp
+        from q3b200.model import Dims
+        lib = q3._lib.lib()
+        dev = torch.device("cuda", rank)
+        max_seq = ((PT + 31) // 32) * 32
+        dims = Dims(layers=PLAYERS, vocab=151936, max_seq=max_seq)
+        bm = synthetic.random_blob_model(dims, seed=41, device=dev)
+        sh = tp.shard_of(bm.L, rank, world)
+        max_pages = max_seq // 32
+        g = torch.Generator().manual_seed(43)
+        tables = torch.randperm(PB * max_pages, generator=g).reshape(PB, max_pages).to(torch.int16)
+        tab = tables.to(dev)
+        ids = torch.randint(0, 151936, (PB * PT,), generator=g, dtype=torch.int32).to(dev)
+        wsb = lib.q3_prefill_workspace_bytes(C.byref(bm.L), PB, PT)
+        stream = torch.cuda.Stream(device=dev)
+
+        def rows_of(pool):
+            out = []
+            for s in range(PB):
+                for t in range(PT):
+                    p = int(tables[s, t // 32]) & 0xFFFF
+                    out.append(torch.cat([pool.k[:, p, t % 32].flatten(), pool.v[:, p, t % 32].flatten(),
+                                          pool.ks[:, p, t % 32].flatten().view(torch.int8),
+                                          pool.vs[:, p, t % 32].flatten().view(torch.int8)]).cpu().numpy())
+            return np.stack(out)
+
+        pool = synthetic.KVPoolTensors(PLAYERS, PB * max_pages, sh.kv_heads, device=dev)
+        comm = tp.TPPrefillComm(bm.L, rank, world, PB * PT, PB)
+        ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+        nxt = torch.full((PB,), -1, dtype=torch.int32, device=dev)
+        dist.barrier()
+        with torch.cuda.stream(stream):
+            for _ in range(2):                 # twice: the counters carry over between calls
+                comm.prefill(bm.blob, bm.L, pool.c(), tab, max_pages, ids, PB, PT, nxt, ws, stream)
+        torch.cuda.synchronize(dev)
+        res = {"ids": nxt.cpu().numpy(), "status": np.asarray(lib.q3_device_status()),
+               "kv": rows_of(pool), "kv_head0": np.asarray(sh.kv_head0),
+               "kv_heads": np.asarray(sh.kv_heads)}
+        dist.barrier()
+        comm.close()
+        comm = None
+        if rank == 0:
+            del pool
+            full = synthetic.KVPoolTensors(PLAYERS, PB * max_pages, 8, device=dev)
+            ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+            ref = torch.full((PB,), -1, dtype=torch.int32, device=dev)
+            q3._lib.check("q3_prefill_batch", lib.q3_prefill_batch(
+                bm.blob.data_ptr(), C.byref(bm.L), C.byref(full.c()), tab.data_ptr(), max_pages,
+                ids.data_ptr(), PB, PT, ref.data_ptr(), ws.data_ptr(), wsb, stream.cuda_stream))
+            torch.cuda.synchronize(dev)
+            res.update(ref_ids=ref.cpu().numpy(), ref_pk=full.k.cpu().numpy(),
+                       ref_pv=full.v.cpu().numpy(), ref_pks=full.ks.cpu().numpy(),
+                       ref_pvs=full.vs.cpu().numpy(), tables=tables.numpy())
+        np.savez(Path(out_dir) / f"prefill_rank{rank}.npz", **res)
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_prefill_matches_single_gpu(q3, tmp_path, world):
+    """Tensor-parallel batched prefill (3 prompts of 150 tokens, 2 layers, vocab
+    151936) on 2/4/8 GPUs against q3_prefill_batch on one GPU: the greedy next
+    ids and every prompt row's K/V (+ scales) of every layer in each rank's
+    heads, bit for bit.  Layer 1's K/V depend on the residual stream after layer
+    0, so they also pin the exchanged o8, x and s8 columns."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_run_prefill_rank, args=(world, port, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    r0 = np.load(tmp_path / "prefill_rank0.npz")
+    tables = r0["tables"]
+    for r in range(world):
+        d = np.load(tmp_path / f"prefill_rank{r}.npz")
+        assert int(d["status"]) == 0, f"rank {r}: device status {int(d['status'])}"
+        np.testing.assert_array_equal(d["ids"], r0["ref_ids"])
+        h0, nh = int(d["kv_head0"]), int(d["kv_heads"])
+        want = []
+        for s in range(PB):
+            for t in range(PT):
+                p = int(tables[s, t // 32]) & 0xFFFF
+                want.append(np.concatenate([
+                    r0["ref_pk"][:, p, t % 32, h0 * 128:(h0 + nh) * 128].ravel(),
+                    r0["ref_pv"][:, p, t % 32, h0 * 128:(h0 + nh) * 128].ravel(),
+                    r0["ref_pks"][:, p, t % 32, h0:h0 + nh].ravel().view(np.int8),
+                    r0["ref_pvs"][:, p, t % 32, h0:h0 + nh].ravel().view(np.int8)]))
+        np.testing.assert_array_equal(d["kv"], np.stack(want))
