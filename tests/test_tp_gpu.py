@@ -252,8 +252,8 @@ def _run_prefill_rank(rank, world, port, out_dir):
                 for t in range(PT):
                     p = int(tables[s, t // 32]) & 0xFFFF
                     out.append(torch.cat([pool.k[:, p, t % 32].flatten(), pool.v[:, p, t % 32].flatten(),
-                                          pool.ks[:, p, t % 32].flatten().view(torch.int8),
-                                          pool.vs[:, p, t % 32].flatten().view(torch.int8)]).cpu().numpy())
+                                          pool.ks[:, p, t % 32].flatten().contiguous().view(torch.int8),
+                                          pool.vs[:, p, t % 32].flatten().contiguous().view(torch.int8)]).cpu().numpy())
             return np.stack(out)
 
         pool = synthetic.KVPoolTensors(PLAYERS, PB * max_pages, sh.kv_heads, device=dev)
