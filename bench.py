@@ -42,9 +42,9 @@ SEQS, CTX, LAYERS, VOCAB = 64, 2048, 28, 151936
 KV_BYTES_PER_TOKEN_LAYER = 2 * 1024 + 2 * 8 * 4   # K+V int8 rows + f32 per-head scales
 LAYER_WEIGHT_BYTES = 15777792                       # int8 weights + f32 row scales of one layer
 LM_HEAD_BYTES = 151936 * 1024 + 151936 * 4          # int8 lm_head + f32 row scales
-# DRAM bytes (read + write) of one k_attention_decode launch at ctx 2048, 64 seqs, from
-# one ncu capture of this bench (--layers 2 --no-graph); the profile summary gives it
-ATT_TRAFFIC_BYTES = 281348352 + 4959744
+# DRAM bytes (read + write) of one k_attention_decode launch at ctx 2048, 64 seqs: the
+# mean of two launches of one ncu capture of this bench (--layers 2 --no-graph)
+ATT_TRAFFIC_BYTES = 281230464 + 5382272
 
 
 def parse():
