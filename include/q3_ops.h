@@ -452,6 +452,19 @@ int q3_tp_comm_destroy(void *comm);
  * (timeout -> status bit 20 -> q3_tp_comm_reset -> clean step) without a
  * peer process or a GPU fault. */
 int q3_tp_comm_set_wait_ns(void *comm, uint64_t ns);
+
+/* Comparison variant of the decode step's O / down reductions
+ * (src/main_big.cpp:255,261 reduction points): mode 1 sums each rank's own
+ * group partials in order, then sums the ranks' results with ncclAllReduce
+ * (NCCL's ring/tree order, so the residual stream matches the exact path only
+ * within float32 rounding, and greedy ids can differ where two logits tie
+ * within it); mode 0 (default) is the exact ordered exchange.  The first
+ * switch to mode 1 is collective: every rank passes the same 128-byte NCCL
+ * unique id, made on one rank by q3_tp_nccl_unique_id and sent to the others
+ * by the host.  NCCL is loaded from the process (libnccl.so.2) at that point;
+ * nothing else in the library uses it. */
+int q3_tp_nccl_unique_id(void *out128);
+int q3_tp_comm_set_reduction(void *comm, int32_t mode, const void *nccl_unique_id);
 int q3_tp_comm_inject_missing_signals(void *comm, int32_t buf, int32_t producer,
                                       uint32_t count, void *stream);
 

@@ -309,7 +309,11 @@ __global__ void __launch_bounds__(THREADS, 4)
       if (warp < count) {
         const float mj0 = fmaxf(mp0, sm.bm[slot][warp][0]), mj1 = fmaxf(mp1, sm.bm[slot][warp][1]);
         // lane 0: corr of head 0, lane 1: corr of head 1
-        const float cx = exp_ref(lane == 1 ? __fsub_rn(mp1, mj1) : __fsub_rn(mp0, mj0));
+        // exp(m_prev - m_new) is exp(0) = 1 exactly when the running maximum of
+        // both heads stayed (the common case after the first blocks)
+        const float cx = (mp0 == mj0 && mp1 == mj1)
+                             ? 1.0f
+                             : exp_ref(lane == 1 ? __fsub_rn(mp1, mj1) : __fsub_rn(mp0, mj0));
         const float pr0 = exp_ref(__fsub_rn(s0, mj0)), pr1 = exp_ref(__fsub_rn(s1, mj1));
         const float ps0 = warp_tree_sum(pr0), ps1 = warp_tree_sum(pr1);
         const float pv0 = (t < kv_len) ? __fmul_rn(pr0, vs) : 0.0f;
@@ -369,8 +373,26 @@ __global__ void __launch_bounds__(THREADS, 4)
 }  // namespace dec
 
 // ---------------------------------------------------------------- host side
+// The split form's CTAs each stream at most 4 key groups in two phases (K,
+// then V) and hand the recurrence state down the cluster; measured on one B200
+// at 2112 keys it wins only while the pairs cannot fill the GPU: 64 pairs
+// 27.6 us against 36.8 for the single-CTA kernel, 128 pairs 48 against 37.
+constexpr long kSplitMaxPairs = 96;
+
+int attention_decode_split_cluster(uint32_t max_pages);
+int attention_decode_split_launch(const DecodeAttnArgs &p, const void *k_pool, const void *v_pool,
+                                  uint32_t num_pages, int kv_heads, int n_seqs, int cluster,
+                                  cudaStream_t s, bool pdl);
+
 int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const void *v_pool,
                             uint32_t num_pages, int kv_heads, int n_seqs, cudaStream_t s, bool pdl) {
+  // few pairs (tensor parallelism, small batches): split each pair's key range
+  // over a cluster (q3_attention_decode_split.cu)
+  if (static_cast<long>(n_seqs) * kv_heads <= kSplitMaxPairs) {
+    const int cl = attention_decode_split_cluster(static_cast<uint32_t>(p.table_stride));
+    if (cl > 1)
+      return attention_decode_split_launch(p, k_pool, v_pool, num_pages, kv_heads, n_seqs, cl, s, pdl);
+  }
   if (p.row_bytes % 16 || p.page_bytes % 16 || reinterpret_cast<uintptr_t>(k_pool) % 16 ||
       reinterpret_cast<uintptr_t>(v_pool) % 16)
     return Q3_ERR_ALIGN;
@@ -402,6 +424,7 @@ int gemm_device_status_take();
 int dgemm_device_status_take();
 int pattn_device_status_take();
 int tp_device_status_take();
+int dsplit_device_status_take();
 }
 
 extern "C" int q3_device_status(void) {
@@ -419,5 +442,8 @@ extern "C" int q3_device_status(void) {
   const int tp = q3::tp_device_status_take();
   if (tp < 0) return -1;
   v |= static_cast<unsigned int>(tp);
+  const int ds = q3::dsplit_device_status_take();
+  if (ds < 0) return -1;
+  v |= static_cast<unsigned int>(ds);
   return static_cast<int>(v) | g;
 }

@@ -387,9 +387,19 @@ int tp_decode(const q3::TpComm &c, char *bl, const q3_layout &L, const q3_kv_poo
       a.as_rb = as_rb;
       a.ws[0] = wscale;
       a.H = (int)H;
+      a.expect = q3::tp_expect(c, buf);
+      if (c.reduce_nccl) {
+        // comparison variant: this rank's group partials stay local (slots
+        // 0..), counted on the producer-0 counter, summed and all-reduced below
+        a.ndst = 1;
+        a.slot0 = 0;
+        a.dst[0] = reinterpret_cast<float *>(c.local + (buf == q3::TP_O ? c.off_orecv : c.off_drecv));
+        a.sig[0] = q3::tp_sig(c, c.rank, buf, 0);
+        a.inc[0] = q3::dgemm_part_ctas((int)H, (int)(buf == q3::TP_O ? sh.q_heads : sh.mlp_groups));
+        return a;
+      }
       a.ndst = c.world;
       a.slot0 = slot0;
-      a.expect = q3::tp_expect(c, buf);
       for (int q = 0; q < c.world; ++q) {
         a.dst[q] = reinterpret_cast<float *>(c.peer[q] + (buf == q3::TP_O ? c.off_orecv : c.off_drecv));
         a.sig[q] = q3::tp_sig(c, q, buf, c.rank);
@@ -405,6 +415,14 @@ int tp_decode(const q3::TpComm &c, char *bl, const q3_layout &L, const q3_kv_poo
       r.sig = q3::tp_sig(c, c.rank, buf, 0);
       r.expect = q3::tp_expect(c, buf);
       r.world = c.world;
+      if (c.reduce_nccl) {
+        const int own = (int)(buf == q3::TP_O ? sh.q_heads : sh.mlp_groups);
+        float *red = reinterpret_cast<float *>(c.local + c.off_nccl);
+        Q3_TRY(q3::tp_nccl_reduce(c, r.recv, own, (int)B, (int)H, red, st));
+        r.recv = red;
+        r.slots = 1;
+        r.world = 0;                   // complete already: nothing to wait for
+      }
       r.x = w.x;
       r.w = nw;
       r.inv = inv_h;

@@ -15,6 +15,7 @@
 // reuse a buffer only after every rank has consumed its previous contents:
 // the next write into `buf` comes after the writer waited for data that each
 // reader produces only after its own consumer of `buf` finished (stream order).
+#include <dlfcn.h>
 #include <string.h>
 
 #include <new>
@@ -153,6 +154,48 @@ __global__ void __launch_bounds__(64) k_tp_argmax_exchange(TpArgmaxArgs a) {
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 __global__ void k_tp_expect_add(unsigned *expect, unsigned count) { *expect += count; }
+
+// out[m][t] = ((0 + recv[0][m][t]) + recv[1][m][t]) + ... (slot order)
+__global__ void k_tp_sum_slots(const float *recv, int slots, int B, int H, float *out) {
+  const size_t n = static_cast<size_t>(B) * H;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    float acc = 0.0f;
+    for (int sl = 0; sl < slots; ++sl) acc = __fadd_rn(acc, __ldcg(recv + sl * n + i));
+    out[i] = acc;
+  }
+}
+
+// ---- NCCL, loaded at run time from the process (the copy torch loaded), so
+// the library itself does not depend on it.  Only the comparison variant uses it.
+struct NcclUid { char internal[128]; };
+using NcclGetUid = int (*)(NcclUid *);
+using NcclInit = int (*)(void **, int, NcclUid, int);
+using NcclAllReduce = int (*)(const void *, void *, size_t, int, int, void *, cudaStream_t);
+using NcclDestroy = int (*)(void *);
+constexpr int kNcclFloat32 = 7, kNcclSum = 0;
+struct NcclApi {
+  NcclGetUid get_uid = nullptr;
+  NcclInit init = nullptr;
+  NcclAllReduce all_reduce = nullptr;
+  NcclDestroy destroy = nullptr;
+};
+const NcclApi *nccl_api() {
+  static NcclApi api;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
+    if (h) {
+      api.get_uid = reinterpret_cast<NcclGetUid>(dlsym(h, "ncclGetUniqueId"));
+      api.init = reinterpret_cast<NcclInit>(dlsym(h, "ncclCommInitRank"));
+      api.all_reduce = reinterpret_cast<NcclAllReduce>(dlsym(h, "ncclAllReduce"));
+      api.destroy = reinterpret_cast<NcclDestroy>(dlsym(h, "ncclCommDestroy"));
+    }
+  }
+  return (api.get_uid && api.init && api.all_reduce && api.destroy) ? &api : nullptr;
+}
 
 // ---- prefill exchanges
 struct PfPushArgs {
@@ -309,8 +352,25 @@ int pf_argmax_exchange(PfComm &c, const float *best, int32_t *idx, uint32_t v0, 
   return st;
 }
 
+int tp_nccl_reduce(const TpComm &c, const float *recv, int slots, int B, int H, float *out,
+                   cudaStream_t s) {
+  const NcclApi *api = nccl_api();
+  if (!api || !c.nccl) return Q3_ERR_NULL;
+  q3h::timer_begin(q3h::TIMER_EXCHANGE, s);
+  k_tp_sum_slots<<<64, 256, 0, s>>>(recv, slots, B, H, out);
+  int st = q3h::launch_status();
+  if (st == Q3_OK && api->all_reduce(out, out, static_cast<size_t>(B) * H, kNcclFloat32, kNcclSum,
+                                     c.nccl, s) != 0) {
+    q3h::set_error_message("ncclAllReduce failed");
+    st = Q3_ERR_CUDA;
+  }
+  q3h::timer_end(q3h::TIMER_EXCHANGE, s);
+  return st;
+}
+
 int tp_reduce_norm(const TpReduceArgs &a, cudaStream_t s) {
-  if (a.H != 1024 || a.B < 1 || a.slots < 1 || a.slots > kTpMaxSlots || a.world < 1 ||
+  // world 0: the partials are already complete (no counters to wait for)
+  if (a.H != 1024 || a.B < 1 || a.slots < 1 || a.slots > kTpMaxSlots || a.world < 0 ||
       a.world > kTpMaxRanks)
     return Q3_ERR_SHAPE;
   q3h::timer_begin(q3h::TIMER_EXCHANGE, s);
@@ -411,7 +471,8 @@ extern "C" int q3_tp_comm_create(const q3_layout *L, int32_t rank, int32_t world
   c->off_orecv = 512;
   c->off_drecv = q3::align256(c->off_orecv + c->heads * slot);
   c->off_keys = q3::align256(c->off_drecv + c->mlp_groups * slot);
-  c->bytes = q3::align256(c->off_keys + static_cast<size_t>(q3::kTpMaxRanks) * max_seqs * 8);
+  c->off_nccl = q3::align256(c->off_keys + static_cast<size_t>(q3::kTpMaxRanks) * max_seqs * 8);
+  c->bytes = q3::align256(c->off_nccl + slot);
   cudaError_t e = cudaMalloc(&c->local, c->bytes);
   if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->bytes);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -575,9 +636,58 @@ extern "C" int q3_tp_prefill_comm_destroy(void *comm) {
   return Q3_OK;
 }
 
+extern "C" int q3_tp_nccl_unique_id(void *out) {
+  if (!out) return Q3_ERR_NULL;
+  const q3::NcclApi *api = q3::nccl_api();
+  if (!api) {
+    q3h::set_error_message("libnccl.so.2 is not loadable in this process");
+    return Q3_ERR_CUDA;
+  }
+  q3::NcclUid uid;
+  if (api->get_uid(&uid) != 0) {
+    q3h::set_error_message("ncclGetUniqueId failed");
+    return Q3_ERR_CUDA;
+  }
+  memcpy(out, &uid, sizeof uid);
+  return Q3_OK;
+}
+
+extern "C" int q3_tp_comm_set_reduction(void *comm, int32_t mode, const void *nccl_unique_id) {
+  if (!comm) return Q3_ERR_NULL;
+  TpComm *c = static_cast<TpComm *>(comm);
+  if (mode == 0) {
+    c->reduce_nccl = 0;
+    return Q3_OK;
+  }
+  if (mode != 1) return Q3_ERR_MODE;
+  if (!c->nccl) {
+    if (!nccl_unique_id) return Q3_ERR_NULL;
+    const q3::NcclApi *api = q3::nccl_api();
+    if (!api) {
+      q3h::set_error_message("libnccl.so.2 is not loadable in this process");
+      return Q3_ERR_CUDA;
+    }
+    q3::NcclUid uid;
+    memcpy(&uid, nccl_unique_id, sizeof uid);
+    void *nc = nullptr;
+    if (api->init(&nc, c->world, uid, c->rank) != 0 || !nc) {   // collective over the ranks
+      q3h::set_error_message("ncclCommInitRank failed");
+      return Q3_ERR_CUDA;
+    }
+    c->nccl = nc;
+  }
+  c->reduce_nccl = 1;
+  return Q3_OK;
+}
+
 extern "C" int q3_tp_comm_destroy(void *comm) {
   if (!comm) return Q3_OK;
   TpComm *c = static_cast<TpComm *>(comm);
+  if (c->nccl) {
+    const q3::NcclApi *api = q3::nccl_api();
+    if (api) api->destroy(c->nccl);
+    c->nccl = nullptr;
+  }
   for (int q = 0; q < c->world; ++q)
     if (c->opened[q]) cudaIpcCloseMemHandle(c->peer[q]);
   if (c->local) cudaFree(c->local);

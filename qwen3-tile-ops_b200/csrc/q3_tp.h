@@ -23,10 +23,18 @@ struct TpComm {
   char *peer[kTpMaxRanks];        // every rank's region as mapped here (peer[rank] = local)
   bool opened[kTpMaxRanks];       // peer[q] came from cudaIpcOpenMemHandle
   size_t bytes;
-  size_t off_sig, off_expect, off_orecv, off_drecv, off_keys;
+  size_t off_sig, off_expect, off_orecv, off_drecv, off_keys, off_nccl;
   unsigned long long wait_ns;     // limit of every bounded wait on the peers' signals
   q3_tp_shard shard[kTpMaxRanks];
+  int reduce_nccl;                // O/down reductions by ncclAllReduce (comparison variant)
+  void *nccl;                     // ncclComm_t of the variant
 };
+
+// the comparison variant's reduction: this rank's group partials (slots
+// 0..slots-1 of its receive buffer) summed in order, then summed over the
+// ranks by ncclAllReduce (ring/tree order: not the reference's order)
+int tp_nccl_reduce(const TpComm &c, const float *recv, int slots, int B, int H, float *out,
+                   cudaStream_t s);
 
 constexpr unsigned long long kTpDefaultWaitNs = 2000000000ull;
 

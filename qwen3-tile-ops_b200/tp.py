@@ -59,6 +59,10 @@ def _bind():
     h.q3_tp_comm_set_wait_ns.argtypes = [C.c_void_p, C.c_uint64]
     h.q3_tp_comm_inject_missing_signals.argtypes = [C.c_void_p, C.c_int32, C.c_int32, C.c_uint32,
                                                     C.c_void_p]
+    h.q3_tp_nccl_unique_id.argtypes = [C.c_void_p]
+    h.q3_tp_comm_set_reduction.argtypes = [C.c_void_p, C.c_int32, C.c_void_p]
+    h.q3_tp_nccl_unique_id.restype = C.c_int
+    h.q3_tp_comm_set_reduction.restype = C.c_int
     h.q3_tp_prefill_comm_create.argtypes = [C.POINTER(Layout), C.c_int32, C.c_int32, C.c_uint32,
                                             C.c_uint32, C.POINTER(C.c_void_p), C.c_void_p]
     h.q3_tp_prefill_comm_connect.argtypes = [C.c_void_p, C.c_void_p]
@@ -137,6 +141,26 @@ class TPComm:
         check("q3_tp_comm_reset", _bind().q3_tp_comm_reset(self.ptr, None))
         torch.cuda.synchronize()
         self._barrier()
+
+    def use_nccl(self, on: bool = True) -> None:
+        """Switch the O / down reductions to the ncclAllReduce comparison
+        variant (``on``) or back to the exact ordered exchange.  The first
+        switch on is collective: rank 0 makes the NCCL id and the process group
+        carries it to the others."""
+        h = _bind()
+        uid = None
+        if on:
+            raw = (C.c_ubyte * 128)()
+            if self.rank == 0:
+                check("q3_tp_nccl_unique_id", h.q3_tp_nccl_unique_id(raw))
+            if self.world > 1:
+                import torch.distributed as dist
+                box = [bytes(raw)]
+                dist.broadcast_object_list(box, src=0, group=self.group)
+                C.memmove(raw, box[0], 128)
+            uid = raw
+        check("q3_tp_comm_set_reduction",
+              h.q3_tp_comm_set_reduction(self.ptr, 1 if on else 0, uid))
 
     def set_wait_ns(self, ns: int) -> None:
         """How long this rank's kernels wait for a peer's signal before they

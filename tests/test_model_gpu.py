@@ -112,7 +112,7 @@ def test_config3_full_shape_generate(q3):
 
 
 # ---------------------------------------------------------------- batched decode
-def _decode_case(q3, layers, vocab, lens, seed=0, tp_world1=False):
+def _decode_case(q3, layers, vocab, lens, seed=0, tp_world1=False, nccl=False):
     """Prefill each sequence on the oracle, load its KV into a shared page
     pool under a shuffled page table, run ONE batched decode step on the GPU
     and the oracle per sequence; return both.  ``tp_world1``: the step runs
@@ -167,6 +167,8 @@ def _decode_case(q3, layers, vocab, lens, seed=0, tp_world1=False):
     if tp_world1:
         from q3b200 import tp
         comm = tp.TPComm(bm.L, 0, 1, B)
+        if nccl:
+            comm.use_nccl()
         comm.decode_step(bm.blob, bm.L, pool, tab, max_pages, ids_d, pos_d, B, nxt, ws,
                          torch.cuda.current_stream())
         torch.cuda.synchronize()
@@ -182,11 +184,15 @@ def _decode_case(q3, layers, vocab, lens, seed=0, tp_world1=False):
             want_kv)
 
 
-@pytest.mark.parametrize("tp_world1", [False, True], ids=["single", "tp1"])
+@pytest.mark.parametrize("variant", ["single", "tp1", "tp1-nccl"])
 @pytest.mark.parametrize("layers,vocab,lens", [(1, 1024, [5, 40, 64, 33]),
                                                (2, 4096, [100, 1, 31, 32, 250])])
-def test_decode_step_batch(q3, layers, vocab, lens, tp_world1):
-    got, want, pool, tables, kvs = _decode_case(q3, layers, vocab, lens, tp_world1=tp_world1)
+def test_decode_step_batch(q3, layers, vocab, lens, variant):
+    """"tp1-nccl": the ncclAllReduce reduction variant with one rank, where the
+    in-order sum of the rank's groups is the whole sum, so it must be exact."""
+    got, want, pool, tables, kvs = _decode_case(q3, layers, vocab, lens,
+                                                tp_world1=variant != "single",
+                                                nccl=variant == "tp1-nccl")
     assert list(got) == want
     for s, n in enumerate(lens):          # the new K/V row of every layer
         p, sl = tables[s, n // 32], n % 32

@@ -322,3 +322,95 @@ def test_tp_prefill_matches_single_gpu(q3, tmp_path, world):
                     r0["ref_pks"][:, p, t % 32, h0:h0 + nh].ravel().view(np.int8),
                     r0["ref_pvs"][:, p, t % 32, h0:h0 + nh].ravel().view(np.int8)]))
         np.testing.assert_array_equal(d["kv"], np.stack(want))
+
+
+def _run_nccl_rank(rank, world, port, out_dir):
+    import ctypes as C
+    import datetime
+    import os
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(repo))
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    comm = None
+    try:
+        import __graft_entry__ as ge
+        q3 = ge.load_package()
+        from q3b200 import synthetic, tp
+        from q3b200.model import Dims
+        lib = q3._lib.lib()
+        dev = torch.device("cuda", rank)
+        max_seq = ((CTX + 1 + 31) // 32) * 32
+        dims = Dims(layers=1, vocab=151936, max_seq=max_seq)
+        bm = synthetic.random_blob_model(dims, seed=51, device=dev)
+        sh = tp.shard_of(bm.L, rank, world)
+        max_pages = max_seq // 32
+        g = torch.Generator().manual_seed(53)
+        tab = torch.randperm(B * max_pages, generator=g).reshape(B, max_pages).to(torch.int16).to(dev)
+        ids = torch.randint(0, 151936, (B,), generator=g, dtype=torch.int32).to(dev)
+        pos = torch.randint(CTX - 200, CTX, (B,), generator=g, dtype=torch.int32).to(dev)
+        wsb = lib.q3_decode_workspace_bytes(C.byref(bm.L), B)
+        stream = torch.cuda.Stream(device=dev)
+        comm = tp.TPComm(bm.L, rank, world, B)
+        out = {}
+        for name in ("exact", "nccl"):
+            pool = synthetic.KVPoolTensors(1, B * max_pages, sh.kv_heads, device=dev)
+            pool.fill_random(seed=52, head0=sh.kv_head0, total_heads=8)
+            if name == "nccl":
+                comm.use_nccl()
+            ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+            nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+            dist.barrier()
+            with torch.cuda.stream(stream):
+                comm.decode_step(bm.blob, bm.L, pool.c(), tab, max_pages, ids, pos, B, nxt, ws,
+                                 stream)
+            torch.cuda.synchronize(dev)
+            out[name + "_ids"] = nxt.cpu().numpy()
+            out[name + "_x"] = ws[:B * 1024 * 4].cpu().numpy().view(np.float32).copy()
+        out["status"] = np.asarray(lib.q3_device_status())
+        dist.barrier()
+        np.savez(Path(out_dir) / f"nccl_rank{rank}.npz", **out)
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_tp_nccl_variant_close_to_exact(q3, tmp_path):
+    """The ncclAllReduce form of the O / down reductions on 2 GPUs (48
+    sequences, one layer, one step) against the exact ordered exchange.  The
+    variant adds the ranks' partial sums in NCCL's order, so x differs in the
+    last bits, and where that moves a value across an int8 rounding tie the
+    requantised input of the next GEMM differs by one step.  Held to the
+    tolerance of float32 stages with that allowance: at least 99.9 % of the
+    residual elements within 1e-3 relative (floor 1e-3 absolute), the norm of
+    the difference within 1e-3 of the norm of x, and at least 90 % of the
+    greedy ids equal; every rank holds the same ids and x."""
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_run_nccl_rank, args=(world, port, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    r0 = np.load(tmp_path / "nccl_rank0.npz")
+    for r in range(world):
+        d = np.load(tmp_path / f"nccl_rank{r}.npz")
+        assert int(d["status"]) == 0
+        np.testing.assert_array_equal(d["exact_ids"], r0["exact_ids"])
+        np.testing.assert_array_equal(d["nccl_ids"], r0["nccl_ids"])
+        xe, xn = d["exact_x"].astype(np.float64), d["nccl_x"].astype(np.float64)
+        close = np.abs(xn - xe) <= 1e-3 * np.maximum(np.abs(xe), 1e-3)
+        rel = np.linalg.norm(xn - xe) / np.linalg.norm(xe)
+        agree = float(np.mean(d["nccl_ids"] == d["exact_ids"]))
+        msg = f"rank {r}: close {close.mean():.5f}, rel norm {rel:.2e}, ids agree {agree:.3f}"
+        assert close.mean() >= 0.999 and rel <= 1e-3 and agree >= 0.9, msg
