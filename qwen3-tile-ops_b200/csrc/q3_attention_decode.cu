@@ -63,7 +63,9 @@ struct Smem {
   alignas(1024) int8_t pq[2][1024];       // no swizzle: [16-key chunk][8 rows][16 B]
   uint16_t tab[TAB_CACHE];                // this sequence's page table (first TAB_CACHE entries)
   float bm[2][NCW][2];                    // block maxima
-  float corr[2][2][4], psum[2][2][4], pmax[2][2][4];   // [slot][head][block]
+  alignas(16) float corr[2][2][4];        // [slot][head][block]
+  alignas(16) float psum[2][2][4];
+  alignas(16) float pmax[2][2][4];
   float red[NCW][2];
   unsigned long long kfull[2], kempty[2], vfull, vempty;
   unsigned long long qk_done[2], pv_done[2], pq_ready[2], bm_ready[2], mma_final;
@@ -257,15 +259,21 @@ __global__ void __launch_bounds__(THREADS, 4)
                      "=r"(v[6]), "=r"(v[7])
                    : "r"(lane_base + 32 + 16 * slot));
       tmem_wait_ld();
+      float cv[2][4], sv[2][4], mv[2][4];   // the block terms, one vector load each
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        *reinterpret_cast<float4 *>(cv[h]) = *reinterpret_cast<const float4 *>(sm.corr[slot][h]);
+        *reinterpret_cast<float4 *>(sv[h]) = *reinterpret_cast<const float4 *>(sm.psum[slot][h]);
+        *reinterpret_cast<float4 *>(mv[h]) = *reinterpret_cast<const float4 *>(sm.pmax[slot][h]);
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (q < count) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const float c = sm.corr[slot][h][q];
-            den[h] = __fadd_rn(__fmul_rn(den[h], c), sm.psum[slot][h][q]);
-            res[h] = __fadd_rn(__fmul_rn(res[h], c),
-                               __fmul_rn(i2f_small(v[2 * q + h]), sm.pmax[slot][h][q]));
+            den[h] = __fadd_rn(__fmul_rn(den[h], cv[h][q]), sv[h][q]);
+            res[h] = __fadd_rn(__fmul_rn(res[h], cv[h][q]),
+                               __fmul_rn(i2f_small(v[2 * q + h]), mv[h][q]));
           }
         }
       }
