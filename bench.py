@@ -741,10 +741,22 @@ def measure_prefill(args, q3, lib, dev, rank, world, dist, mode: str = "replicas
     status = int(lib.q3_device_status())
     if status != 0:
         raise RuntimeError(f"device status {status} after the {mode} prefill")
+    fam_ms = None
+    if mode == "tp":
+        # one eager prefill per kernel family with events around its launches
+        # (events serialise the launches; the sums are the families' own times)
+        fam_ms = {}
+        for name in ("attention", "gemm", "exchange"):
+            if dist:
+                dist.barrier()
+            fam_ms[name] = sum(family_times(lib, name, step, stream, dev, capacity=1024))
     if dist:
-        t = torch.tensor([ms], device=dev)
+        vals = [ms] + ([fam_ms[k] for k in ("attention", "gemm", "exchange")] if fam_ms else [])
+        t = torch.tensor(vals, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
+        if fam_ms:
+            fam_ms = {k: round(float(v), 2) for k, v in zip(("attention", "gemm", "exchange"), t[1:])}
     parity = None
     if comm is not None:
         def digest(*ts):
@@ -797,6 +809,7 @@ def measure_prefill(args, q3, lib, dev, rank, world, dist, mode: str = "replicas
            "scaling": "strong" if mode == "tp" else "weak"}
     if mode == "tp":
         out["tp_parity"] = parity
+        out["kernel_ms_per_step"] = fam_ms
         out["roofline"] = {"bound": "tensor", "achieved": round(ops / (ms * 1e-3) / 1e12, 2),
                            "peak": peak * world, "unit": "TOPS (int8, all GPUs)",
                            "frac": round(ops / (ms * 1e-3) / 1e12 / (peak * world), 4),
