@@ -292,6 +292,87 @@ extern "C" int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv
 // with system-scope counters (q3_tp.cu); the last rows' lm_head runs over
 // the rank's vocabulary rows and the (max, first index) keys are exchanged.
 // ---------------------------------------------------------------------------
+namespace {
+
+using q3::kEps;
+using q3::kInv127;
+using q3::quant1;
+using q3::rsqrt_ref;
+using q3::warp_tree_max;
+using q3::warp_tree_sum;
+
+// RMSNorm + per-256 quant (rmsnorm.h:34-81, quant.h:89-138) of a residual
+// stream whose columns [c0, c0 + nc) are this rank's, in three steps with an
+// all-gather after each (the reference's arithmetic, split at its exchange
+// points):
+//   1. the tree sum of x^2 of each of this rank's 32-column blocks;
+//   2. with every block sum: ss summed over the blocks in order, r, h = (x r) w
+//      for this rank's columns, and the maximum of |h| per 128 columns;
+//   3. with every maximum: the scale of each 256-column group (every rank
+//      computes all of them) and the int8 codes of this rank's columns.
+// One warp per (row, 32-column block) in step 1, per (row, 128-column chunk)
+// in steps 2 and 3.
+__global__ void k_pf_block_sums(const float *x, int M, int H, int c0, int nc, float *bsum) {
+  const int nbl = nc / 32;
+  const long wi = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wi >= static_cast<long>(M) * nbl) return;
+  const int m = static_cast<int>(wi / nbl), b = c0 / 32 + static_cast<int>(wi % nbl);
+  const float v = x[static_cast<size_t>(m) * H + 32 * b + lane];
+  const float t = warp_tree_sum(__fmul_rn(v, v));
+  if (lane == 0) bsum[static_cast<size_t>(m) * (H / 32) + b] = t;
+}
+
+__global__ void k_pf_norm_amax(const float *x, const float *bsum, const float *w, float inv, int M,
+                               int H, int c0, int nc, float *hc, float *amax) {
+  const int nch = nc / 128;
+  const long wi = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wi >= static_cast<long>(M) * nch) return;
+  const int m = static_cast<int>(wi / nch), ch = static_cast<int>(wi % nch);
+  const float *bs = bsum + static_cast<size_t>(m) * (H / 32);
+  float ss = 0.0f;
+  for (int b = 0; b < H / 32; ++b) ss = __fadd_rn(ss, bs[b]);    // blocks in order
+  ss = __fmul_rn(ss, inv);
+  ss = __fadd_rn(ss, kEps);
+  const float r = rsqrt_ref(ss);
+  float mx = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int col = c0 + 128 * ch + 32 * k + lane;
+    const float h = __fmul_rn(__fmul_rn(x[static_cast<size_t>(m) * H + col], r), w[col]);
+    hc[static_cast<size_t>(m) * nc + (col - c0)] = h;
+    mx = fmaxf(mx, fabsf(h));
+  }
+  mx = warp_tree_max(mx);
+  if (lane == 0) amax[static_cast<size_t>(m) * (H / 128) + (c0 / 128 + ch)] = mx;
+}
+
+__global__ void k_pf_quant_cols(const float *hc, const float *amax, int M, int H, int c0, int nc,
+                                int8_t *h8, float *hs) {
+  const int nch = nc / 128;
+  const long wi = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wi >= static_cast<long>(M) * nch) return;
+  const int m = static_cast<int>(wi / nch), ch = static_cast<int>(wi % nch);
+  const float *am = amax + static_cast<size_t>(m) * (H / 128);
+  const int gc = (c0 / 128 + ch) / 2;                                 // this chunk's 256-group
+  const float scale = __fmul_rn(fmaxf(am[2 * gc], am[2 * gc + 1]), kInv127);
+  if (ch == 0 && lane < H / 256)                                     // every group's scale
+    hs[static_cast<size_t>(m) * (H / 256) + lane] =
+        __fmul_rn(fmaxf(am[2 * lane], am[2 * lane + 1]), kInv127);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int col = c0 + 128 * ch + 32 * k + lane;
+    h8[static_cast<size_t>(m) * H + col] =
+        static_cast<int8_t>(quant1(hc[static_cast<size_t>(m) * nc + (col - c0)], scale));
+  }
+}
+
+inline unsigned warps_grid(long warps) { return static_cast<unsigned>((warps * 32 + 255) / 256); }
+
+}  // namespace
+
 extern "C" int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layout,
                                    const q3_kv_pool *pool, const uint16_t *tables,
                                    uint32_t max_pages, const int32_t *ids, uint32_t n_seqs,
@@ -331,6 +412,9 @@ extern "C" int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layo
   float *xf = reinterpret_cast<float *>(R + c.off_x);
   int8_t *s8f = reinterpret_cast<int8_t *>(R + c.off_s8);
   float *ssf = reinterpret_cast<float *>(R + c.off_ss);
+  int8_t *h8f = reinterpret_cast<int8_t *>(R + c.off_h8);
+  float *bsumf = reinterpret_cast<float *>(R + c.off_bsum);
+  float *amaxf = reinterpret_cast<float *>(R + c.off_amax);
 
   k_prefill_rope_rows<<<M, 64, 0, st>>>(reinterpret_cast<const float *>(bl + o[Q3_OFF_COS]),
                                         reinterpret_cast<const float *>(bl + o[Q3_OFF_SIN]), HALF,
@@ -338,7 +422,7 @@ extern "C" int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layo
   Q3_TRY(q3h::launch_status());
 
   const q3_view x = v2(xf, M, H, Q3_DT_F32), h = v2(w.h, M, H, Q3_DT_F32);
-  const q3_view h8 = v2(w.h8, M, H, Q3_DT_I8), hs = v2(w.hs, M, H / 256, Q3_DT_F32);
+  const q3_view h8 = v2(h8f, M, H, Q3_DT_I8), hs = v2(w.hs, M, H / 256, Q3_DT_F32);
   const q3_view q8 = v2(w.q8, M, QWl, Q3_DT_I8), qs = v2(w.qs, M, QH, Q3_DT_F32);
   const q3_view k8 = v2(w.k8, M, KWl, Q3_DT_I8), ks = v2(w.ks, M, KVH, Q3_DT_F32);
   const q3_view v8 = v2(w.v8, M, KWl, Q3_DT_I8), vs = v2(w.vs, M, KVH, Q3_DT_F32);
@@ -362,8 +446,28 @@ extern "C" int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layo
   const float inv_h = 1.0f / static_cast<float>(H), inv_hd = 1.0f / static_cast<float>(HD);
   const q3::PfSeg seg_o8{c.off_o8, sh.q_head0 * HD, QWl, QW};
   const q3::PfSeg seg_os{c.off_os, sh.q_head0 * 4, QH * 4, HEADS * 4};
-  const q3::PfSeg seg_x{c.off_x, c0 * 4, NC * 4, H * 4};
   const q3::PfSeg seg_s8{c.off_s8, g0 * 256, NG * 256, I};
+  const q3::PfSeg seg_bsum{c.off_bsum, c0 / 32 * 4, NC / 32 * 4, H / 32 * 4};
+  const q3::PfSeg seg_amax{c.off_amax, c0 / 128 * 4, NC / 128 * 4, H / 128 * 4};
+  const q3::PfSeg seg_h8{c.off_h8, c0, NC, H};
+  // RMSNorm(nw) + quant of the column-sharded residual into h8 (all columns) / hs
+  auto sharded_norm = [&](const float *nw) -> int {
+    k_pf_block_sums<<<warps_grid((long)M * (NC / 32)), 256, 0, st>>>(xf, (int)M, (int)H, (int)c0,
+                                                                     (int)NC, bsumf);
+    Q3_TRY(q3h::launch_status());
+    Q3_TRY(q3::pf_push(c, q3::PF_NB, &seg_bsum, 1, M, st));
+    Q3_TRY(q3::pf_wait(c, q3::PF_NB, st));
+    k_pf_norm_amax<<<warps_grid((long)M * (NC / 128)), 256, 0, st>>>(
+        xf, bsumf, nw, 1.0f / static_cast<float>(H), (int)M, (int)H, (int)c0, (int)NC, w.h, amaxf);
+    Q3_TRY(q3h::launch_status());
+    Q3_TRY(q3::pf_push(c, q3::PF_NA, &seg_amax, 1, M, st));
+    Q3_TRY(q3::pf_wait(c, q3::PF_NA, st));
+    k_pf_quant_cols<<<warps_grid((long)M * (NC / 128)), 256, 0, st>>>(w.h, amaxf, (int)M, (int)H,
+                                                                      (int)c0, (int)NC, h8f, w.hs);
+    Q3_TRY(q3h::launch_status());
+    Q3_TRY(q3::pf_push(c, q3::PF_NH, &seg_h8, 1, M, st));
+    return q3::pf_wait(c, q3::PF_NH, st);
+  };
   const q3::PfSeg seg_ss{c.off_ss, g0 * 4, NG * 4, G * 4};
 
   {
@@ -396,8 +500,10 @@ extern "C" int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layo
     char *pks = static_cast<char *>(pool->ks) + Li * pool->scale_layer_stride;
     char *pvs = static_cast<char *>(pool->vs) + Li * pool->scale_layer_stride;
 
-    if (Li != 0) Q3_TRY(q3_rmsnorm_rows(&x, &n1, &h, inv_h, s));
-    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    // layer 0: x is the embedding, whole on every rank (h from the embedding
+    // step); later layers: the column-sharded residual
+    if (Li == 0) Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    else Q3_TRY(sharded_norm(reinterpret_cast<const float *>(ln)));
     Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wv, &wvs, nullptr, 256, nullptr, &v8, &vs, nullptr,
                                   nullptr, nullptr, 0.0f, s));
     Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wk, &wks, nullptr, 256, nullptr, &k8, &ks, &nk,
@@ -435,10 +541,7 @@ extern "C" int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layo
     }
     Q3_TRY(q3_gemm_nt_group_store(&o8, &os, &wo, &wos, nullptr, 128, &xc, nullptr, nullptr, nullptr,
                                   nullptr, nullptr, 0.0f, s));
-    Q3_TRY(q3::pf_push(c, q3::PF_XO, &seg_x, 1, M, st));
-    Q3_TRY(q3::pf_wait(c, q3::PF_XO, st));
-    Q3_TRY(q3_rmsnorm_rows(&x, &n2, &h, inv_h, s));
-    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    Q3_TRY(sharded_norm(reinterpret_cast<const float *>(n2.data)));
     Q3_TRY(q3_gemm_gate_up_swiglu_quant(&h8, &hs, &wg, &wgs, &wu, &wus, &s8c, &ssc, 256, s));
     {
       const q3::PfSeg sg[2] = {seg_s8, seg_ss};
@@ -447,11 +550,14 @@ extern "C" int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layo
     }
     Q3_TRY(q3_gemm_nt_group_store(&s8, &ss, &wd, &wds, nullptr, 256, &xc, nullptr, nullptr, nullptr,
                                   nullptr, nullptr, 0.0f, s));
-    Q3_TRY(q3::pf_push(c, q3::PF_XD, &seg_x, 1, M, st));
-    Q3_TRY(q3::pf_wait(c, q3::PF_XD, st));
   }
-  // last row of every sequence: final norm + quant (replicated), lm_head over
-  // this rank's vocabulary rows, then the key exchange
+  // last row of every sequence: its residual columns gathered, final norm +
+  // quant (replicated), lm_head over this rank's vocabulary rows, key exchange
+  {
+    const q3::PfSeg seg_xl{c.off_x + static_cast<size_t>(T - 1) * H * 4, c0 * 4, NC * 4, T * H * 4};
+    Q3_TRY(q3::pf_push(c, q3::PF_XL, &seg_xl, 1, B, st));
+    Q3_TRY(q3::pf_wait(c, q3::PF_XL, st));
+  }
   k_prefill_last_rows<<<B, 256, 0, st>>>(xf, (int)T, (int)H, w.xl, w.best, next_ids);
   Q3_TRY(q3h::launch_status());
   const q3_view xl = v2(w.xl, B, H, Q3_DT_F32), hl = v2(w.hl, B, H, Q3_DT_F32);

@@ -573,6 +573,9 @@ extern "C" int q3_tp_prefill_comm_create(const q3_layout *L, int32_t rank, int32
   c->off_s8 = off;   off = q3::align256(off + M * L->inter);
   c->off_ss = off;   off = q3::align256(off + M * (L->inter / 256) * 4);
   c->off_keys = off; off = q3::align256(off + static_cast<size_t>(q3::kTpMaxRanks) * max_seqs * 8);
+  c->off_h8 = off;   off = q3::align256(off + M * L->hidden);
+  c->off_bsum = off; off = q3::align256(off + M * (L->hidden / 32) * 4);
+  c->off_amax = off; off = q3::align256(off + M * (L->hidden / 128) * 4);
   c->bytes = off;
   cudaError_t e = cudaMalloc(&c->local, c->bytes);
   if (e == cudaSuccess) e = cudaMemset(c->local, 0, 4096);

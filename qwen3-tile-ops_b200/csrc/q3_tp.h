@@ -71,10 +71,12 @@ int tp_argmax_exchange(const TpComm &c, const float *best, const int32_t *bidx, 
 int tp_device_status_take();
 
 // ---- tensor-parallel prefill (q3_tp_prefill_batch) --------------------------
-// Exchanges of one prefill layer, all all-gathers: the attention output o8/os
-// of each rank's q heads, the residual columns x after O and after down, the
-// SwiGLU output s8/ss of each rank's MLP groups; then the argmax keys.
-enum PfEx { PF_O = 0, PF_XO = 1, PF_S = 2, PF_XD = 3, PF_KEYS = 4, PF_NEX = 5 };
+// Exchanges of the prefill, all all-gathers: the attention output o8/os of
+// each rank's q heads and the SwiGLU output s8/ss of its MLP groups; for each
+// RMSNorm of the column-sharded residual, the 32-column block sums of x^2,
+// the 128-column maxima of |h| and the quantised h8 of each rank's columns;
+// the last rows' residual columns; the argmax keys.
+enum PfEx { PF_O = 0, PF_S = 1, PF_NB = 2, PF_NA = 3, PF_NH = 4, PF_XL = 5, PF_KEYS = 6, PF_NEX = 7 };
 constexpr int kPfPushCtas = 264;     // CTAs of every push (all ranks use the same count)
 
 struct PfComm {
@@ -84,6 +86,7 @@ struct PfComm {
   char *peer[kTpMaxRanks];
   bool opened[kTpMaxRanks];
   size_t bytes, off_sig, off_o8, off_os, off_x, off_s8, off_ss, off_keys;
+  size_t off_h8, off_bsum, off_amax;   // [rows][H] i8, [rows][H/32] f32, [rows][H/128] f32
   unsigned gen[PF_NEX];           // rounds of each exchange so far (host count)
   unsigned long long wait_ns;
   q3_tp_shard shard[kTpMaxRanks];
