@@ -429,6 +429,7 @@ int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const v
 
 namespace q3 {
 int gemm_device_status_take();
+int gemm2_device_status_take();
 int dgemm_device_status_take();
 int pattn_device_status_take();
 int tp_device_status_take();
@@ -441,6 +442,9 @@ extern "C" int q3_device_status(void) {
   if (v) cudaMemcpyToSymbol(q3::g_device_error, &zero, sizeof zero);
   const int g = q3::gemm_device_status_take();
   if (g < 0) return -1;
+  const int g2 = q3::gemm2_device_status_take();
+  if (g2 < 0) return -1;
+  v |= static_cast<unsigned int>(g2);
   const int dg = q3::dgemm_device_status_take();
   if (dg < 0) return -1;
   v |= static_cast<unsigned int>(dg);

@@ -44,6 +44,9 @@ struct GemmArgs {
 };
 
 int gemm_simt(const GemmArgs &p, cudaStream_t s);
+// CTA-pair tensor-core path for many-row GEMMs (q3_gemm_tc2.cu)
+bool gemm_pair_eligible(const GemmArgs &p);
+int gemm_pair(const GemmArgs &p, cudaStream_t s);
 int gemm_tc(const GemmArgs &p, cudaStream_t s);
 bool gemm_tc_eligible(const GemmArgs &p);
 int argmax_begin(const GemmArgs &p, cudaStream_t s);

@@ -557,6 +557,7 @@ bool gemm_tc_eligible(const GemmArgs &p) {
 }
 
 int gemm_tc(const GemmArgs &p, cudaStream_t s) {
+  if (gemm_pair_eligible(p)) return gemm_pair(p, s);
   switch (p.mode) {
     // wider token tiles cut the weight traffic per MAC; SwiGLU stages 256
     // features per token and keeps 64, and so do the few-row GEMMs

@@ -165,8 +165,9 @@ def test_lm_head_argmax(ops, m):
 
 
 # ---- the per-group GEMM microbench shapes (prefill-size GEMMs) ------------------
-# M beyond 64 takes the wide token tiles; 700 leaves a ragged last tile.
-@pytest.mark.parametrize("m", [512, 700, 4096])
+# M beyond 64 takes the wide token tiles; 700 leaves a ragged last tile; from
+# 1024 rows the CTA-pair kernel runs (1100: a ragged last 256-token tile).
+@pytest.mark.parametrize("m", [512, 700, 1100, 4096])
 @pytest.mark.parametrize("k,n,g", [(1024, 2048, 256), (2048, 1024, 128), (3072, 1024, 256)])
 def test_gemm_config2_store_add(ops, m, k, n, g):
     rng = np.random.default_rng(m + k + n)
@@ -181,7 +182,7 @@ def test_gemm_config2_store_add(ops, m, k, n, g):
     same_bits(host(x), (x0 + ref).astype(F))
 
 
-@pytest.mark.parametrize("m", [512, 700])
+@pytest.mark.parametrize("m", [512, 700, 1100, 4096])
 def test_gate_up_swiglu_config2(ops, m):
     rng = np.random.default_rng(100 + m)
     a, as_, wg, wgs = _rand_gemm(rng, m, 1024, 3072, 256)
@@ -197,7 +198,7 @@ def test_gate_up_swiglu_config2(ops, m):
     same_bits(host(ss), refs)
 
 
-@pytest.mark.parametrize("m", [200, 700])
+@pytest.mark.parametrize("m", [200, 700, 1100, 2048])
 def test_gemm_head_epilogues_wide_tiles(ops, m):
     from oracle import synth
     rng = np.random.default_rng(200 + m)
