@@ -495,14 +495,17 @@ def test_paged_kv_scatter_and_batch(ops):
 
 # ---------------------------------------------------------------- decode batch
 @pytest.mark.parametrize("lens", [[1, 31, 32, 33, 100], [2049, 300, 64, 4100, 5],
-                                  [2112] * 8, [1, 200, 520, 700, 33]])
+                                  [2112] * 8, [1, 200, 520, 700, 33],
+                                  [2112] * 16, [2100 + 3 * i for i in range(32)],
+                                  [2112] * 40])
 def test_attention_decode_batch(ops, q3, lens):
     """One decode row per sequence over a shared pool with shuffled per-sequence
     tables.  Few (sequence, head) pairs with more than 4 key groups take the
     key-split kernel: [2112] * 8 runs clusters of 5 CTAs (the carry-in and the
-    recurrence chain), the last case clusters of 2 in which short sequences
+    recurrence chain), the fourth case clusters of 2 in which short sequences
     leave CTAs without keys; 4100 keys exceed the split form and the first
-    case needs no split: both take the single-CTA kernel."""
+    case needs no split: both take the single-CTA kernel, and so do the
+    128-, 256- (the TP-2 shape) and 320-pair cases."""
     rng = np.random.default_rng(sum(lens))
     heads, kvh, kw = 16, 8, 1024
     B = len(lens)
