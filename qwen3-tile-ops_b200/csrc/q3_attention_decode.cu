@@ -55,9 +55,10 @@ constexpr unsigned kErrWait = 8u;       // a pipeline wait timed out
 constexpr uint32_t ID_QK = idesc_i8(16);          // A = keys (K-major), B = q rows
 constexpr uint32_t ID_PV = idesc_i8(16, true);    // A = V (MN-major), B = pq rows
 
+template <int VS>   // V ring slots: 1, or 2 when fewer CTAs share an SM
 struct Smem {
   alignas(1024) int8_t kbuf[2][4][4096];  // K pages of a group, 128-byte swizzled rows
-  alignas(1024) int8_t vbuf[4][4096];     // V pages of a group
+  alignas(1024) int8_t vbuf[VS][4][4096]; // V pages of a group
   // B operands, 8 rows each; rows 8..15 of N = 16 alias rows 0..7 (stride offset 0)
   alignas(1024) int8_t qt[1024];          // 128-byte swizzled: rows 0,1 = q heads
   alignas(1024) int8_t pq[2][1024];       // no swizzle: [16-key chunk][8 rows][16 B]
@@ -67,7 +68,7 @@ struct Smem {
   alignas(16) float psum[2][2][4];
   alignas(16) float pmax[2][2][4];
   float red[NCW][2];
-  unsigned long long kfull[2], kempty[2], vfull, vempty;
+  unsigned long long kfull[2], kempty[2], vfull[VS], vempty[VS];
   unsigned long long qk_done[2], pv_done[2], pq_ready[2], bm_ready[2], mma_final;
   uint32_t tmem_base;
   int abort;
@@ -85,22 +86,25 @@ __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;
 __device__ __forceinline__ void softmax_sync() {   // the 4 softmax warps only
   asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
 }
-__device__ __forceinline__ bool wait_or_abort(unsigned long long *b, uint32_t par, Smem &sm) {
+template <class S>
+__device__ __forceinline__ bool wait_or_abort(unsigned long long *b, uint32_t par, S &sm) {
   if (mbar_wait(b, par, &sm.abort)) return true;
   if (!*reinterpret_cast<volatile int *>(&sm.abort)) atomicOr(&g_device_error, kErrWait);
   *reinterpret_cast<volatile int *>(&sm.abort) = 1;
   return false;
 }
 
-__device__ __forceinline__ uint32_t page_of(const Smem &sm, const uint16_t *table, int j) {
+template <class S>
+__device__ __forceinline__ uint32_t page_of(const S &sm, const uint16_t *table, int j) {
   return j < TAB_CACHE ? sm.tab[j] : table[j];
 }
 
-__global__ void __launch_bounds__(THREADS, 4)
+template <int VS>
+__global__ void __launch_bounds__(THREADS, VS == 1 ? 4 : 3)
     k_attention_decode(const char *__restrict__ kpool, const char *__restrict__ vpool,
                        DecodeAttnArgs p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  Smem &sm = *reinterpret_cast<Smem *>(
+  Smem<VS> &sm = *reinterpret_cast<Smem<VS> *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
   const int kvh = blockIdx.x, seq = blockIdx.y;
@@ -137,8 +141,10 @@ __global__ void __launch_bounds__(THREADS, 4)
       mbar_init(&sm.pq_ready[i], NCW * 32);
       mbar_init(&sm.bm_ready[i], NCW);
     }
-    mbar_init(&sm.vfull, 32);
-    mbar_init(&sm.vempty, 1);
+    for (int i = 0; i < VS; ++i) {
+      mbar_init(&sm.vfull[i], 32);
+      mbar_init(&sm.vempty[i], 1);
+    }
     mbar_init(&sm.mma_final, 1);
     sm.abort = 0;
     mbar_init_fence();
@@ -169,9 +175,10 @@ __global__ void __launch_bounds__(THREADS, 4)
         full = &sm.kfull[slot];
         dst = sm.kbuf[slot];
       } else {
-        if (g >= 1 && !wait_or_abort(&sm.vempty, (g - 1) & 1, sm)) break;
-        full = &sm.vfull;
-        dst = sm.vbuf;
+        const int vslot = g % VS;
+        if (g >= VS && !wait_or_abort(&sm.vempty[vslot], ((g / VS) - 1) & 1, sm)) break;
+        full = &sm.vfull[vslot];
+        dst = sm.vbuf[vslot];
       }
       const char *pool = isv ? vpool : kpool;
       const int first = 4 * g, count = min(4, nb - first);
@@ -213,16 +220,16 @@ __global__ void __launch_bounds__(THREADS, 4)
       for (int g = 0; g < G && ok; ++g) {
         if (g + 1 < G && !(ok = issue_qk(g + 1))) break;
         const int slot = g & 1;
-        if (!(ok = wait_or_abort(&sm.vfull, g & 1, sm))) break;
+        if (!(ok = wait_or_abort(&sm.vfull[g % VS], (g / VS) & 1, sm))) break;
         if (!(ok = wait_or_abort(&sm.pq_ready[slot], (g >> 1) & 1, sm))) break;
         fence_after();
         const int count = min(4, nb - 4 * g);
-        const uint32_t a0 = su32(sm.vbuf[0]), b0 = su32(sm.pq[slot]);
+        const uint32_t a0 = su32(sm.vbuf[g % VS][0]), b0 = su32(sm.pq[slot]);
         for (int q = 0; q < count; ++q)          // k-step q = block q's 32 keys
           mma_i8(tmem + 32 + 16 * slot, sdesc_sw128(a0 + q * 4096), sdesc_plain(b0 + q * 256, 128, 0),
                  ID_PV, q != 0);
         mma_commit(&sm.pv_done[slot]);
-        mma_commit(&sm.vempty);
+        mma_commit(&sm.vempty[g % VS]);
       }
       mma_commit(&sm.mma_final);                   // every MMA issued above has completed
       mbar_wait(&sm.mma_final, 0, nullptr);        // bounded
@@ -392,6 +399,26 @@ int attention_decode_split_launch(const DecodeAttnArgs &p, const void *k_pool, c
                                   uint32_t num_pages, int kv_heads, int n_seqs, int cluster,
                                   cudaStream_t s, bool pdl);
 
+template <int VS>
+static size_t smem_of() { return sizeof(dec::Smem<VS>) + 1024; }   // + alignment slack
+
+template <int VS>
+static int launch_decode(bool pdl, dim3 grid, size_t smem, cudaStream_t s, const void *k_pool,
+                         const void *v_pool, const DecodeAttnArgs &a) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(dec::k_attention_decode<VS>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  if (attr_err != cudaSuccess) {
+    q3h::set_cuda_error(attr_err);
+    return Q3_ERR_CUDA;
+  }
+  return q3h::launch_ex(pdl, dec::k_attention_decode<VS>, grid, dim3(dec::THREADS), smem, s,
+                        static_cast<const char *>(k_pool), static_cast<const char *>(v_pool), a);
+}
+
 int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const void *v_pool,
                             uint32_t num_pages, int kv_heads, int n_seqs, cudaStream_t s, bool pdl) {
   // few pairs (tensor parallelism, small batches): split each pair's key range
@@ -404,23 +431,15 @@ int attention_decode_launch(const DecodeAttnArgs &p, const void *k_pool, const v
   if (p.row_bytes % 16 || p.page_bytes % 16 || reinterpret_cast<uintptr_t>(k_pool) % 16 ||
       reinterpret_cast<uintptr_t>(v_pool) % 16)
     return Q3_ERR_ALIGN;
-  const size_t smem = sizeof(dec::Smem) + 1024;   // + alignment slack
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(dec::k_attention_decode,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  });
-  if (attr_err != cudaSuccess) {
-    q3h::set_cuda_error(attr_err);
-    return Q3_ERR_CUDA;
-  }
   DecodeAttnArgs a = p;
   a.num_pages = num_pages;
   dim3 grid(kv_heads, n_seqs);
+  // with at most 3 CTAs per SM (pairs <= 3 x SMs) a CTA has room for a second
+  // V slot: the V copy of group g+1 then runs while the P.V of group g waits
+  const bool two_v = static_cast<long>(n_seqs) * kv_heads <= 3L * q3h::sm_count();
   q3h::timer_begin(q3h::TIMER_ATTENTION, s);
-  const int st = q3h::launch_ex(pdl, dec::k_attention_decode, grid, dim3(dec::THREADS), smem, s,
-                                static_cast<const char *>(k_pool), static_cast<const char *>(v_pool), a);
+  const int st = two_v ? launch_decode<2>(pdl, grid, smem_of<2>(), s, k_pool, v_pool, a)
+                       : launch_decode<1>(pdl, grid, smem_of<1>(), s, k_pool, v_pool, a);
   q3h::timer_end(q3h::TIMER_ATTENTION, s);
   return st;
 }

@@ -214,6 +214,19 @@ void set_error_message(const char *msg);   // text returned by q3_last_cuda_erro
 int launch_argmax_row(const float *row, int n, int32_t *out_id, cudaStream_t s);
 void count_launch();
 
+// Streaming multiprocessors of the current device (cached per device).
+inline int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
 // Every kernel launch of the library is followed by this check (it also
 // counts the launch for q3_launch_count).
 inline int launch_status() {
