@@ -76,6 +76,7 @@ struct Smem {
   alignas(16) float xsum[2][ROWS][KP];
   alignas(16) float xam[2][ROWS][KP];
   float xout[KP][ROWS];
+  unsigned long long t256[Q3_EXP2_T256_N];           // exp2 table (per-lane indices)
   unsigned long long q_full, kv_full[NST], kv_empty[NST];
   unsigned long long s_full[2], s_free[2], p_full[2], o_full, o_free, final_done;
   uint32_t tmem_base;
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     sm.abort = 0;
     mbar_init_fence();
   }
+  for (int i = tid; i < Q3_EXP2_T256_N; i += THREADS) sm.t256[i] = g_exp2_t256[i];
   if (warp == MMA_WARP) tmem_alloc<TMEM_COLS>(&sm.tmem_base);
   fence_before();
   __syncthreads();
@@ -267,11 +269,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float bmax = fmaxf(fmaxf(xm.x, xm.y), fmaxf(xm.z, xm.w));
       const float mn = fmaxf(m, bmax);
       // exp(m - mn) is exp(0) = 1 exactly when the running maximum did not move
-      const float corr = (mn == m) ? 1.0f : exp_ref_fast(__fsub_rn(m, mn));
+      const float corr = (mn == m) ? 1.0f : exp_ref_fast_t(__fsub_rn(m, mn), sm.t256);
       float pv[KPK];
       float am = 0.0f;
 #pragma unroll
-      for (int i = 0; i < KPK; ++i) s[i] = exp_ref_fast(__fsub_rn(s[i], mn));   // p
+      for (int i = 0; i < KPK; ++i) s[i] = exp_ref_fast_t(__fsub_rn(s[i], mn), sm.t256);   // p
       const float ps = tree8_sum(s);
       *reinterpret_cast<float4 *>(&vsv[0]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt]);
       *reinterpret_cast<float4 *>(&vsv[4]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt + 4]);

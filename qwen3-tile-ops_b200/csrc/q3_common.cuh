@@ -127,7 +127,9 @@ static __device__ const unsigned long long g_exp2_t256[Q3_EXP2_T256_N] = Q3_EXP2
 // float32 result is scaled by 2^(k >> 8) through its exponent field (exact:
 // the result is normal, or +inf when it rounds to 2^128).  Checked identical
 // to exp2_cr_t on every float32 input (q3_exp2_selfcheck).
-__device__ __forceinline__ float exp2_cr_fast(float x) {
+// `tab` is g_exp2_t256 or a copy of it in shared memory (the index varies per
+// lane: a shared copy serves a warp's lookups without the L1 tag traffic).
+__device__ __forceinline__ float exp2_cr_fast_t(float x, const unsigned long long *tab) {
   if (!(x >= -125.0f && x < 128.0f)) return exp2_cr_t(x, g_exp2_frac64);
   const float u = __fadd_rn(__fmul_rn(x, 256.0f), 12582912.0f);
   const float kf = __fsub_rn(u, 12582912.0f);
@@ -136,12 +138,14 @@ __device__ __forceinline__ float exp2_cr_fast(float x) {
   double p = __fma_rn(0.009618129107628477, r, 0.05550410866482158);      // ln2^4/4!, ln2^3/3!
   p = __fma_rn(p, r, 0.24022650695910072);                                 // ln2^2/2!
   p = __fma_rn(p, r, 0.6931471805599453);                                  // ln2
-  const double t = __longlong_as_double(static_cast<long long>(g_exp2_t256[k & 255]));
+  const double t = __longlong_as_double(static_cast<long long>(tab[k & 255]));
   const double y = __fma_rn(__dmul_rn(t, r), p, t);
   const unsigned low = static_cast<unsigned>(__double_as_longlong(y)) & 0x1FFFFFFFu;
   if (low - ((1u << 28) - 64u) <= 128u) return exp2_cr_t(x, g_exp2_frac64);
   return __int_as_float(__float_as_int(__double2float_rn(y)) + ((k >> 8) << 23));
 }
+
+__device__ __forceinline__ float exp2_cr_fast(float x) { return exp2_cr_fast_t(x, g_exp2_t256); }
 
 __device__ __forceinline__ float exp2_cr(float x) { return exp2_cr_t(x, g_exp2_frac64); }
 
@@ -151,6 +155,9 @@ __device__ __forceinline__ float exp_ref(float x) {
 }
 __device__ __forceinline__ float exp_ref_fast(float x) {
   return exp2_cr_fast(__fmul_rn(x, __uint_as_float(kLog2eBits)));
+}
+__device__ __forceinline__ float exp_ref_fast_t(float x, const unsigned long long *tab) {
+  return exp2_cr_fast_t(__fmul_rn(x, __uint_as_float(kLog2eBits)), tab);
 }
 
 // rne(x / scale) saturated to +-127, NaN -> 0 (ref_qwen3.py:69-76)
