@@ -366,10 +366,7 @@ __global__ void __launch_bounds__(THREADS, VS == 1 ? 4 : 3)
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     o[h] = __fmul_rn(res[h], __fdiv_rn(1.0f, den[h]));
-    float m = fabsf(o[h]);
-#pragma unroll
-    for (int k = 1; k < 32; k <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, k));
-    mx[h] = m;
+    mx[h] = warp_tree_max(fabsf(o[h]));
   }
   if (lane == 0) { sm.red[warp][0] = mx[0]; sm.red[warp][1] = mx[1]; }
   softmax_sync();

@@ -178,21 +178,23 @@ __device__ __forceinline__ float rsqrt_ref(float x) {
 // max as np.where(b > a, b, a) (ref_qwen3.py:57-58)
 __device__ __forceinline__ float max_ref(float a, float b) { return b > a ? b : a; }
 
-// Warp adjacent-pair reduction trees (ref_qwen3.py:41-63): a butterfly over
+// Warp adjacent-pair reduction tree (ref_qwen3.py:41-63): a butterfly over
 // lanes 1,2,4,8,16 pairs exactly the reference's tree when absent lanes hold
-// the identity (0 for sums, -inf for maxima); every lane gets the result.
+// the identity (0); every lane gets the result.
 __device__ __forceinline__ float warp_tree_sum(float v) {
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+// Maximum over the warp (every lane gets it) in one redux.sync (the sm_100a
+// float form).  A maximum does not depend on the order of comparisons: callers
+// take maxima of magnitudes, or of scores whose maximum only enters as
+// exp(s - m) and m == m' tests, where the sign of a zero maximum cannot show.
+// NaN inputs are passed over, as by fmaxf.
 __device__ __forceinline__ float warp_tree_max(float v) {
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float w = __shfl_xor_sync(0xffffffffu, v, o);
-    v = fmaxf(v, w);
-  }
-  return v;
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
 }
 
 // Programmatic dependent launch: let the next kernel of the stream start its
