@@ -398,6 +398,10 @@ int attention_decode_split_launch(const DecodeAttnArgs &p, const void *k_pool, c
 
 template <int VS>
 static size_t smem_of() { return sizeof(dec::Smem<VS>) + 1024; }   // + alignment slack
+// 4 (one V slot) or 3 (two) CTAs per SM: 228 KB of shared memory, 1 KB of it
+// reserved per CTA
+static_assert(sizeof(dec::Smem<1>) + 1024 <= 228 * 1024 / 4 - 1024, "4 CTAs per SM");
+static_assert(sizeof(dec::Smem<2>) + 1024 <= 228 * 1024 / 3 - 1024, "3 CTAs per SM");
 
 template <int VS>
 static int launch_decode(bool pdl, dim3 grid, size_t smem, cudaStream_t s, const void *k_pool,
