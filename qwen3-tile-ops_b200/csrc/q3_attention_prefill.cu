@@ -83,8 +83,9 @@ struct Smem {
   int abort;
 };
 
-__device__ __forceinline__ void rows_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
+// the four warps (parts) of one TMEM lane quadrant, which share its 32 rows
+__device__ __forceinline__ void rows_sync(int qd) {
+  asm volatile("bar.sync %0, %1;" ::"r"(2 + qd), "n"(KP * 32) : "memory");
 }
 __device__ __forceinline__ bool wait_or_abort(unsigned long long *b, uint32_t par, int *abort) {
   if (mbar_wait(b, par, abort)) return true;
@@ -264,7 +265,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         bm = fmaxf(bm, s[i]);
       }
       sm.xmax[slot][r][pt] = bm;
-      rows_sync();
+      rows_sync(qd);
       const float4 xm = *reinterpret_cast<const float4 *>(sm.xmax[slot][r]);
       const float bmax = fmaxf(fmaxf(xm.x, xm.y), fmaxf(xm.z, xm.w));
       const float mn = fmaxf(m, bmax);
@@ -285,7 +286,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       sm.xsum[slot][r][pt] = ps;
       sm.xam[slot][r][pt] = am;
-      rows_sync();
+      rows_sync(qd);
       // the two top levels of the 32-key tree: (s0 + s1) + (s2 + s3)
       const float4 xs = *reinterpret_cast<const float4 *>(sm.xsum[slot][r]);
       const float psum = __fadd_rn(__fadd_rn(xs.x, xs.y), __fadd_rn(xs.z, xs.w));
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mx = fmaxf(mx, fabsf(res[d]));
     }
     sm.xout[pt][r] = mx;
-    rows_sync();
+    rows_sync(qd);
     float omx = sm.xout[0][r];
 #pragma unroll
     for (int q = 1; q < KP; ++q) omx = fmaxf(omx, sm.xout[q][r]);
