@@ -107,6 +107,70 @@ __global__ void k_prefill_scatter(const int8_t *k8, const int8_t *v8, const floa
 }
 
 // x row s*T + T-1 -> xl[s]; best[s] = -3e38, next_ids[s] = 0 (argmax state)
+using q3::kEps;
+using q3::kInv127;
+using q3::quant1;
+using q3::rsqrt_ref;
+using q3::warp_tree_max;
+
+// RMSNorm (kernels/rmsnorm.h:34-81) and the per-256-column int8 quantisation
+// (kernels/quant.h:89-138) of 1024-column rows in one pass, without the f32
+// rows in between: one warp per row, lane l holding columns 4l .. 4l+3 of
+// each 128-column chunk (float4 loads, packed int8 stores).  A 32-column
+// block's tree of squares is the in-lane (v0+v1)+(v2+v3) followed by the
+// butterfly over its 8 lanes (offsets 1, 2, 4): the reference's adjacent-pair
+// tree; the 32 block sums are added in column order.  Bit-identical to
+// q3_rmsnorm_rows followed by q3_quant_rows_heads with group 256.
+__global__ void k_norm_quant_1024(const float *__restrict__ x, const float *__restrict__ w,
+                                  float inv, int rows, int8_t *h8, float *hs) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(row) * 1024);
+  float4 v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = xr[32 * k + lane];
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float t = __fadd_rn(__fadd_rn(__fmul_rn(v[k].x, v[k].x), __fmul_rn(v[k].y, v[k].y)),
+                        __fadd_rn(__fmul_rn(v[k].z, v[k].z), __fmul_rn(v[k].w, v[k].w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, t, 8 * q));
+  }
+  ss = __fadd_rn(__fmul_rn(ss, inv), kEps);
+  const float r = rsqrt_ref(ss);
+  const float4 *wr = reinterpret_cast<const float4 *>(w);
+  int8_t *qrow = h8 + static_cast<size_t>(row) * 1024;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {                    // 256-column groups = chunk pairs
+    float hv[8];
+    float am = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int k = 2 * g + c;
+      const float4 wv = wr[32 * k + lane];
+      hv[4 * c + 0] = __fmul_rn(__fmul_rn(v[k].x, r), wv.x);
+      hv[4 * c + 1] = __fmul_rn(__fmul_rn(v[k].y, r), wv.y);
+      hv[4 * c + 2] = __fmul_rn(__fmul_rn(v[k].z, r), wv.z);
+      hv[4 * c + 3] = __fmul_rn(__fmul_rn(v[k].w, r), wv.w);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(hv[i]));
+    const float scale = __fmul_rn(warp_tree_max(am), kInv127);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint32_t b0 = static_cast<uint8_t>(quant1(hv[4 * c + 0], scale));
+      const uint32_t b1 = static_cast<uint8_t>(quant1(hv[4 * c + 1], scale));
+      const uint32_t b2 = static_cast<uint8_t>(quant1(hv[4 * c + 2], scale));
+      const uint32_t b3 = static_cast<uint8_t>(quant1(hv[4 * c + 3], scale));
+      reinterpret_cast<uint32_t *>(qrow + 128 * (2 * g + c))[lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+    if (lane == 0) hs[static_cast<size_t>(row) * 4 + g] = scale;
+  }
+}
+
 __global__ void k_prefill_last_rows(const float *x, int T, int H, float *xl, float *best,
                                     int32_t *next_ids) {
   const int s = blockIdx.x;
@@ -172,6 +236,16 @@ extern "C" int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv
     const q3_view n1_0 = v2(bl + o[Q3_OFF_N1], H, 1, Q3_DT_F32);
     Q3_TRY(q3_embedding_rmsnorm_rows(&emb, &emb_s, &idv, &x, &n1_0, &h, inv_h, s));
   }
+  // RMSNorm + quant of x into h8/hs: one pass for 1024-column rows, else the
+  // two row operators through h
+  auto norm_quant = [&](const float *nw, const q3_view &xv, const q3_view &nv) -> int {
+    if (H == 1024) {
+      k_norm_quant_1024<<<(M + 7) / 8, 256, 0, st>>>(w.x, nw, inv_h, (int)M, w.h8, w.hs);
+      return q3h::launch_status();
+    }
+    Q3_TRY(q3_rmsnorm_rows(&xv, &nv, &h, inv_h, s));
+    return q3_quant_rows_heads(&h, &h8, &hs, 256, s);
+  };
   for (uint32_t Li = 0; Li < L.layers; ++Li) {
     char *lw = bl + o[Q3_OFF_LQ] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERW_STRIDE];
     char *ln = bl + o[Q3_OFF_N1] + static_cast<int64_t>(Li) * o[Q3_OFF_LAYERN_STRIDE];
@@ -193,8 +267,8 @@ extern "C" int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv
     char *pks = static_cast<char *>(pool->ks) + Li * pool->scale_layer_stride;
     char *pvs = static_cast<char *>(pool->vs) + Li * pool->scale_layer_stride;
 
-    if (Li != 0) Q3_TRY(q3_rmsnorm_rows(&x, &n1, &h, inv_h, s));
-    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    if (Li != 0) Q3_TRY(norm_quant(reinterpret_cast<const float *>(ln), x, n1));
+    else Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
     Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wv, &wvs, nullptr, 256, nullptr, &v8, &vs, nullptr,
                                   nullptr, nullptr, 0.0f, s));
     Q3_TRY(q3_gemm_nt_group_store(&h8, &hs, &wk, &wks, nullptr, 256, nullptr, &k8, &ks, &nk,
@@ -256,8 +330,7 @@ extern "C" int q3_prefill_batch(void *blob, const q3_layout *layout, const q3_kv
     }
     Q3_TRY(q3_gemm_nt_group_store(&o8, &os, &wo, &wos, nullptr, 128, &x, nullptr, nullptr, nullptr,
                                   nullptr, nullptr, 0.0f, s));
-    Q3_TRY(q3_rmsnorm_rows(&x, &n2, &h, inv_h, s));
-    Q3_TRY(q3_quant_rows_heads(&h, &h8, &hs, 256, s));
+    Q3_TRY(norm_quant(reinterpret_cast<const float *>(ln + (o[Q3_OFF_N2] - o[Q3_OFF_N1])), x, n2));
     Q3_TRY(q3_gemm_gate_up_swiglu_quant(&h8, &hs, &wg, &wgs, &wu, &wus, &s8, &ss, 256, s));
     Q3_TRY(q3_gemm_nt_group_store(&s8, &ss, &wd, &wds, nullptr, 256, &x, nullptr, nullptr, nullptr,
                                   nullptr, nullptr, 0.0f, s));
