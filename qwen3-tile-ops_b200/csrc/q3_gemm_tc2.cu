@@ -362,6 +362,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         scales_m0 = m0;
       }
       const int n = r0 + f;
+      if (MODE == EPI_ADD) {
+        // the residual rows this warp adds to after the groups: into L2 now, so
+        // the epilogue's loads do not wait on DRAM (one 128-byte line per row)
+        const char *seg = p.out + static_cast<long>(r0 + (warp & 3) * 32) * 4;
+#pragma unroll
+        for (int i = lane; i < HT; i += 32)
+          if (c0 + i < mvalid)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(seg + (long)(m0 + c0 + i) * p.out_rb));
+      }
       float bs[NACC];
       bs[0] = p.b_scale[n];
       float accf[NACC][HT];
