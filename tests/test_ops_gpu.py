@@ -182,6 +182,21 @@ def test_gemm_config2_store_add(ops, m, k, n, g):
     same_bits(host(x), (x0 + ref).astype(F))
 
 
+# The CTA-pair kernel's residual shapes of the tensor-parallel prefill (the O and
+# down GEMMs of one rank at 2 and 4 GPUs: 512 or 256 output columns, one or two
+# pair tiles) and a token count one past a 192-token tile boundary.
+@pytest.mark.parametrize("m,k,n,g", [(1025, 2048, 256, 128), (1151, 3072, 512, 256),
+                                     (1344, 2048, 512, 128)])
+def test_gemm_pair_residual_shapes(ops, m, k, n, g):
+    rng = np.random.default_rng(m + 3 * n)
+    a, as_, w, ws = _rand_gemm(rng, m, k, n, g)
+    ref = O.gemm_group(a, as_, w, ws, g)
+    x0 = rng.standard_normal((m, n)).astype(F)
+    x = dev(x0)
+    ops.gemm_nt_group_store(dev(a), dev(as_), dev(w), dev(ws), None, g, add=x)
+    same_bits(host(x), (x0 + ref).astype(F))
+
+
 @pytest.mark.parametrize("m", [512, 700, 1100, 4096])
 def test_gate_up_swiglu_config2(ops, m):
     rng = np.random.default_rng(100 + m)
