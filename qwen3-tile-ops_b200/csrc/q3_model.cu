@@ -45,6 +45,21 @@ __global__ void k_init_best(float *best, int32_t *bidx) {
 
 __global__ void k_copy_id(const int32_t *src, int32_t *dst) { *dst = *src; }
 
+// graph-replayed greedy decode: the step reads its id and position from
+// fixed words (cur_id, cur_pos) and leaves the picked id in next_id; this
+// kernel then stores it at ids[pos + 1] and moves the words on by one token
+__global__ void k_gen_advance(const int32_t *next_id, int32_t *cur_id, int32_t *cur_pos,
+                              int32_t *ids) {
+  const int32_t pos = *cur_pos, id = *next_id;
+  ids[pos + 1] = id;
+  *cur_id = id;
+  *cur_pos = pos + 1;
+}
+__global__ void k_gen_start(const int32_t *id, int32_t pos, int32_t *cur_id, int32_t *cur_pos) {
+  *cur_id = *id;
+  *cur_pos = pos;
+}
+
 __global__ void k_iota(int32_t *v, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) v[i] = i;
@@ -343,6 +358,79 @@ extern "C" int q3_forward_chunk(void *blob, const q3_layout *layout, uint32_t po
   return forward_chunk_impl(blob, layout, ws, pos, rows, lm_out, optimize_tail, st);
 }
 
+namespace {
+constexpr int kGraphUnavailable = -1000;   // capture not possible: run the steps eagerly
+
+// A private capture stream per thread and device (the caller's stream may be
+// the legacy default stream, which cannot be captured).
+cudaStream_t capture_stream() {
+  thread_local cudaStream_t per_dev[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!per_dev[dev] && cudaStreamCreateWithFlags(&per_dev[dev], cudaStreamNonBlocking) != cudaSuccess)
+    per_dev[dev] = nullptr;
+  return per_dev[dev];
+}
+
+// The n_gen decode steps of q3_generate (positions n_prompt .. n_prompt + n_gen - 1,
+// ids[n_prompt] already picked): step 0 eagerly, steps 1 .. n_gen - 2 as replays of
+// one captured step, the last step eagerly into last_id + the stage rows.
+int generate_by_graph(void *blob, const q3_layout *layout, const q3_kv_pool &cache, const Ws &ws,
+                      int32_t *ids, uint32_t n_prompt, uint32_t n_gen, cudaStream_t st) {
+  cudaStreamCaptureStatus cs_st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs_st) != cudaSuccess || cs_st != cudaStreamCaptureStatusNone)
+    return kGraphUnavailable;      // the caller is capturing: no nested capture
+  cudaStream_t cs = capture_stream();
+  if (!cs) return kGraphUnavailable;
+  const uint32_t max_pages = layout->max_seq / kPageTokens;
+  int32_t *cur_id = ws.last_id + 1, *cur_pos = ws.last_id + 2, *next_id = ws.last_id + 3;
+  auto step = [&](int32_t *nxt, cudaStream_t s) {
+    return q3_decode_step_batch(blob, layout, &cache, ws.ptab, max_pages, cur_id, cur_pos, 1, nxt,
+                                ws.dec_ws, ws.dec_bytes, s);
+  };
+  k_gen_start<<<1, 1, 0, st>>>(ids + n_prompt, static_cast<int32_t>(n_prompt), cur_id, cur_pos);
+  Q3_TRY(q3h::launch_status());
+  Q3_TRY(step(next_id, st));                                   // step 0
+  k_gen_advance<<<1, 1, 0, st>>>(next_id, cur_id, cur_pos, ids);
+  Q3_TRY(q3h::launch_status());
+  // steps 1 .. n_gen - 2: replays of one captured step (eagerly if capture fails)
+  cudaGraphExec_t ge = nullptr;
+  if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+    int rc = step(next_id, cs);
+    if (rc == Q3_OK) {
+      k_gen_advance<<<1, 1, 0, cs>>>(next_id, cur_id, cur_pos, ids);
+      rc = q3h::launch_status();
+    }
+    cudaGraph_t g = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(cs, &g);
+    if (rc != Q3_OK) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (ec == cudaSuccess && g && cudaGraphInstantiate(&ge, g, 0) != cudaSuccess) ge = nullptr;
+    if (g) cudaGraphDestroy(g);
+  }
+  cudaGetLastError();             // a failed capture leaves nothing behind
+  if (ge) {
+    cudaError_t e = cudaSuccess;
+    for (uint32_t i = 1; i + 1 < n_gen && e == cudaSuccess; ++i) e = cudaGraphLaunch(ge, st);
+    cudaGraphExecDestroy(ge);     // freed once the launches above complete
+    if (e != cudaSuccess) {
+      q3h::set_cuda_error(e);
+      return Q3_ERR_CUDA;
+    }
+  } else {
+    for (uint32_t i = 1; i + 1 < n_gen; ++i) {
+      Q3_TRY(step(next_id, st));
+      k_gen_advance<<<1, 1, 0, st>>>(next_id, cur_id, cur_pos, ids);
+      Q3_TRY(q3h::launch_status());
+    }
+  }
+  Q3_TRY(step(ws.last_id, st));                                // the last step
+  return q3::decode_stages_to_blob(*layout, ws.dec_ws, blob, ws.last_id, st);
+}
+}  // namespace
+
 extern "C" int q3_generate(void *blob, const q3_layout *layout, void *workspace,
                            size_t workspace_bytes, void *stream) {
   if (!blob) return Q3_ERR_NULL;
@@ -388,6 +476,14 @@ extern "C" int q3_generate(void *blob, const q3_layout *layout, void *workspace,
   const uint32_t N = layout->seq;
   uint32_t pos = 0;
   while (pos < total) {
+    // four or more decode steps: the first runs eagerly (it also sets up the
+    // kernels' attributes), the middle ones replay one captured step, the last
+    // runs eagerly and copies the stage rows back to the blob
+    if (batched_decode && pos == n_prompt && n_gen >= 4) {
+      const int st_rc = generate_by_graph(blob, layout, cache, ws, ids, n_prompt, n_gen, st);
+      if (st_rc == Q3_OK) break;
+      if (st_rc != kGraphUnavailable) return st_rc;
+    }
     if (batched_decode && pos >= n_prompt) {
       // the id picked for the next position goes straight into ids[pos + 1]
       const bool last = (pos + 1 == total);
