@@ -210,6 +210,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_after();
     fence_proxy_async();               // operands (async proxy) -> partials (generic stores)
     if (ok) {
+      if (c0 < p.M) {                  // (token columns of no row: nothing to keep)
       float *part = reinterpret_cast<float *>(sm.region);
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 #pragma unroll
@@ -225,6 +226,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int i = 0; i < 32; ++i)
             dst[(c0 + i) * 128] = __fmul_rn(__fmul_rn(i2f_small(v[i]), wsv[a]), sm.as[c0 + i][gl]);
         }
+      }
       }
     } else if (lane == 0) {
       atomicOr(&g_dgemm_error, kErrTimeout);
@@ -264,12 +266,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   // ---------------------------------------------- every partial of the cluster is in smem
   fence_proxy_async();                                  // partial stores -> bulk copies
-  if (tid == 0) mbar_expect_tx(&sm.rcv_full, C::RCV);  // the slices this CTA will receive
+  constexpr int TPC = NTOK / NC;                        // tokens reduced by each CTA
+  const int rank = crx + TPCL * gs;
+  // rows of token slice r that exist (a few-row step sends and receives only those)
+  auto slice_rows = [&](int r) { return max(0, min(TPC, p.M - r * TPC)); };
+  if (tid == 0)                                         // the slices this CTA will receive
+    mbar_expect_tx(&sm.rcv_full, static_cast<unsigned>(NC * GPC * NACC * slice_rows(rank) * 128 * 4));
   fence_before();
   cluster_sync();
   fence_after();
-  constexpr int TPC = NTOK / NC;                        // tokens reduced by each CTA
-  const int rank = crx + TPCL * gs;
   // Push: slice r (tokens r*TPC ..) of each of my partials [gl][a] goes to CTA r,
   // into its receive buffer at [group][acc][my tile][TPC][128].
   if (warp == EPI_WARPS) {
@@ -277,10 +282,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     constexpr int NCOPY = GPC * NACC * NC;
     for (int c = lane; c < NCOPY; c += 32) {
       const int r = c % NC, a = (c / NC) % NACC, gl = c / (NC * NACC);
+      const int rows = slice_rows(r);
+      if (rows == 0) continue;
       const int g = gs * GPC + gl;
       const uint32_t src = part0 + static_cast<uint32_t>((((gl * NACC + a) * NTOK + r * TPC) * 128) * 4);
       const uint32_t dst = rcv0 + static_cast<uint32_t>(((((g * NACC + a) * TPCL + crx) * TPC) * 128) * 4);
-      push_to_peer(map_peer(dst, r), src, TPC * 128 * 4, map_peer(su32(&sm.rcv_full), r));
+      push_to_peer(map_peer(dst, r), src, static_cast<uint32_t>(rows * 128 * 4),
+                   map_peer(su32(&sm.rcv_full), r));
     }
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // my sources are read
