@@ -345,13 +345,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float v = __fadd_rn(accf[0][i], 0.0f);   // -0 -> +0: equal maxima compare equal
           const unsigned b = __float_as_uint(v);
           const unsigned key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-          unsigned long long k =
-              (static_cast<unsigned long long>(key) << 32) | (0xffffffffu - static_cast<unsigned>(n));
-#pragma unroll
-          for (int o = 16; o; o >>= 1) {
-            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
-            k = k2 > k ? k2 : k;
-          }
+          // the 64-bit maximum over the warp in two 32-bit reductions: the
+          // largest value key, then the largest ~index among the lanes holding it
+          const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+          const unsigned imax =
+              __reduce_max_sync(0xffffffffu, key == kmax ? 0xffffffffu - static_cast<unsigned>(n) : 0u);
+          const unsigned long long k = (static_cast<unsigned long long>(kmax) << 32) | imax;
           if (lane == 0 && c0 + i < mvalid) {
             if (cta_keys) atomicMax(&sm.akey[c0 + i], k);
             else atomicMax(p.arg_keys + m0 + c0 + i, k);
