@@ -517,10 +517,11 @@ int q3_tp_prefill_batch(void *comm, void *blob, const q3_layout *layout,
 int q3_exp_rows(const q3_view *x, const q3_view *out, void *stream);
 int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream);
 
-/* No counterpart in the reference: self-check of the two device evaluations
- * of the correctly rounded exp2 (the short one every kernel uses and the
- * longer double-precision one it falls back to near rounding midpoints).  Every float32 bit pattern in
- * [lo_bits, hi_bits) is evaluated both ways; *count (device, caller-zeroed)
+/* No counterpart in the reference: self-check of the device evaluations of
+ * the correctly rounded exp2 (the short one, also in its batched branch-free
+ * form, against the longer double-precision one it falls back to near rounding
+ * midpoints).  Every float32 bit pattern in [lo_bits, hi_bits) is evaluated
+ * each way; *count (device, caller-zeroed)
  * gains the number of results that differ and *first_bad (device, caller-set
  * to 0xffffffff) the smallest differing bit pattern. */
 int q3_exp2_selfcheck(uint32_t lo_bits, uint32_t hi_bits, unsigned long long *count,

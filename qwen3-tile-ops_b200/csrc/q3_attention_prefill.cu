@@ -274,7 +274,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       float pv[KPK];
       float am = 0.0f;
 #pragma unroll
-      for (int i = 0; i < KPK; ++i) s[i] = exp_ref_fast_t(__fsub_rn(s[i], mn), sm.t256);   // p
+      for (int i = 0; i < KPK; ++i) s[i] = __fsub_rn(s[i], mn);
+      exp_ref_fast_n(s, sm.t256);                                             // p
       const float ps = tree8_sum(s);
       *reinterpret_cast<float4 *>(&vsv[0]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt]);
       *reinterpret_cast<float4 *>(&vsv[4]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt + 4]);

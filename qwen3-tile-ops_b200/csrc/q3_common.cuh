@@ -145,6 +145,44 @@ __device__ __forceinline__ float exp2_cr_fast_t(float x, const unsigned long lon
   return __int_as_float(__float_as_int(__double2float_rn(y)) + ((k >> 8) << 23));
 }
 
+// exp2_cr_fast_t of N values at once: every value takes the common path without
+// a branch (so the N evaluations interleave: one chain after another would
+// leave the double pipes waiting), inputs below -151 give 0 there as well, and
+// the rare rest -- x in [-151, -125), x >= 128 or NaN, or a double result near
+// a float32 rounding midpoint -- is redone by exp2_cr_t afterwards.  Same
+// results as exp2_cr_fast_t value by value.
+template <int N>
+__device__ __forceinline__ void exp2_cr_fast_n(const float (&x)[N], float (&y)[N],
+                                               const unsigned long long *tab) {
+  unsigned redo = 0;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const float xi = x[i];
+    const bool in = xi >= -125.0f && xi < 128.0f;
+    const float xc = in ? xi : 0.0f;                      // keeps the arithmetic finite
+    const float u = __fadd_rn(__fmul_rn(xc, 256.0f), 12582912.0f);
+    const float kf = __fsub_rn(u, 12582912.0f);
+    const int k = __float_as_int(u) - 0x4B400000;
+    const double r = static_cast<double>(__fmaf_rn(kf, -0.00390625f, xc));   // exact
+    double p = __fma_rn(0.009618129107628477, r, 0.05550410866482158);
+    p = __fma_rn(p, r, 0.24022650695910072);
+    p = __fma_rn(p, r, 0.6931471805599453);
+    const double t = __longlong_as_double(static_cast<long long>(tab[k & 255]));
+    const double yd = __fma_rn(__dmul_rn(t, r), p, t);
+    const unsigned low = static_cast<unsigned>(__double_as_longlong(yd)) & 0x1FFFFFFFu;
+    const bool hard = low - ((1u << 28) - 64u) <= 128u;
+    const float fy = __int_as_float(__float_as_int(__double2float_rn(yd)) + ((k >> 8) << 23));
+    const bool zero = xi < -151.0f;
+    y[i] = zero ? 0.0f : fy;
+    if (in ? hard : !zero) redo |= 1u << i;
+  }
+  if (redo) {
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (redo >> i & 1u) y[i] = exp2_cr_t(x[i], g_exp2_frac64);
+  }
+}
+
 __device__ __forceinline__ float exp2_cr_fast(float x) { return exp2_cr_fast_t(x, g_exp2_t256); }
 
 __device__ __forceinline__ float exp2_cr(float x) { return exp2_cr_t(x, g_exp2_frac64); }
@@ -158,6 +196,14 @@ __device__ __forceinline__ float exp_ref_fast(float x) {
 }
 __device__ __forceinline__ float exp_ref_fast_t(float x, const unsigned long long *tab) {
   return exp2_cr_fast_t(__fmul_rn(x, __uint_as_float(kLog2eBits)), tab);
+}
+// exp(v[i]) in place for N values (exp_ref_fast_t value by value)
+template <int N>
+__device__ __forceinline__ void exp_ref_fast_n(float (&v)[N], const unsigned long long *tab) {
+  float x[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) x[i] = __fmul_rn(v[i], __uint_as_float(kLog2eBits));
+  exp2_cr_fast_n(x, v, tab);
 }
 
 // rne(x / scale) saturated to +-127, NaN -> 0 (ref_qwen3.py:69-76)

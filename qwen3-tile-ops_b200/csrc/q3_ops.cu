@@ -385,7 +385,12 @@ __global__ void k_exp2_selfcheck(uint32_t lo, uint32_t hi, unsigned long long *c
     const float x = __uint_as_float(b);
     const float f = exp2_cr_fast(x);
     const float d = exp2_cr_t(x, g_exp2_frac64);
-    if (__float_as_uint(f) != __float_as_uint(d)) {
+    // the batched form too: x as element 0 of 8 neighbouring bit patterns
+    float xs[8], ys[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xs[j] = __uint_as_float(b ^ static_cast<uint32_t>(j));
+    exp2_cr_fast_n(xs, ys, g_exp2_t256);
+    if (__float_as_uint(f) != __float_as_uint(d) || __float_as_uint(ys[0]) != __float_as_uint(d)) {
       atomicAdd(count, 1ull);
       atomicMin(first_bad, b);
     }
