@@ -361,14 +361,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         // and continue with one warp per token (features l, l+32, l+64, l+96 per lane)
         if (MODE == EPI_SWIGLU) {
           // silu(g)*u (ref_qwen3.py:194-200), element by element, then staged
+          // exp(-g) of the thread's HT tokens in one batch (throughput-bound
+          // here: one exp per gate output; the short exp2, branch-free)
+          float en[HT];
+#pragma unroll
+          for (int i = 0; i < HT; ++i) en[i] = __fmul_rn(accf[0][i], -1.0f);
+          exp_ref_fast_n(en, g_exp2_t256);
 #pragma unroll
           for (int i = 0; i < HT; ++i) {
             float sw = 0.0f;
             if (c0 + i < mvalid) {
               const float gt = accf[0][i];
-              // throughput-bound here (one exp per gate output): the short exp2
-              float e = exp_ref_fast(__fmul_rn(gt, -1.0f));
-              e = __fadd_rn(e, 1.0f);
+              float e = __fadd_rn(en[i], 1.0f);
               e = __fdiv_rn(1.0f, e);
               sw = __fmul_rn(__fmul_rn(gt, e), accf[C::NACC - 1][i]);
             }
