@@ -114,10 +114,10 @@ __device__ __forceinline__ float exp2_cr_t(float x, const unsigned long long *ta
 // 2^(i/256), i = 0..255, correctly rounded to double (gen_exp2_t256_table.py).
 static __device__ const unsigned long long g_exp2_t256[Q3_EXP2_T256_N] = Q3_EXP2_T256_INIT;
 
-// exp2_cr_fast: the same correctly rounded result with fewer double operations,
-// for throughput-bound callers (the prefill attention evaluates ~2e9 exps per
-// layer; measured 10 % more exps per second than exp2_cr_t).  Latency-bound
-// callers (the decode kernels) keep exp2_cr_t, whose chain is shorter there.  x = k/256 + r with k = rint(256 x) and
+// exp2_cr_fast: the same correctly rounded result with fewer double operations
+// (the prefill attention evaluates ~2e9 exps per layer; measured 10 % more
+// exps per second than exp2_cr_t).  Callers evaluate it in batches through
+// exp2_cr_fast_n where they can: a single evaluation is one long chain.  x = k/256 + r with k = rint(256 x) and
 // |r| <= 2^-9, both exact in float32 (the rint by the 1.5 * 2^23 shifter);
 // 2^x = 2^(k >> 8) * T * 2^r with T = 2^((k & 255)/256) from the table, and
 // T * 2^r = T + (T r) * (ln2 + r (ln2^2/2 + r (ln2^3/6 + r ln2^4/24))) in

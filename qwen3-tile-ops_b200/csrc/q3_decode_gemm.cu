@@ -408,12 +408,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         float sw[8];
         float mx = 0.0f;
+        float en[8];                   // exp(-g) of the lane's 8 features in one batch
+#pragma unroll
+        for (int i = 0; i < 8; ++i) en[i] = __fmul_rn(gv[i / 4][i % 4], -1.0f);
+        exp_ref_fast_n(en, g_exp2_t256);
 #pragma unroll
         for (int tt = 0; tt < 2; ++tt) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            float e = exp_ref(__fmul_rn(gv[tt][k], -1.0f));
-            e = __fadd_rn(e, 1.0f);
+            float e = __fadd_rn(en[tt * 4 + k], 1.0f);
             e = __fdiv_rn(1.0f, e);
             sw[tt * 4 + k] = __fmul_rn(__fmul_rn(gv[tt][k], e), uv[tt][k]);
             mx = fmaxf(mx, fabsf(sw[tt * 4 + k]));
