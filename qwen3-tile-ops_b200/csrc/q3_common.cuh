@@ -209,11 +209,10 @@ __device__ __forceinline__ void exp_ref_fast_n(float (&v)[N], const unsigned lon
 // rne(x / scale) saturated to +-127, NaN -> 0 (ref_qwen3.py:69-76)
 __device__ __forceinline__ int quant1(float x, float scale) {
   const float q = __fdiv_rn(x, scale);
-  if (q != q) return 0;
   int v = __float2int_rn(q);
   v = v > 127 ? 127 : v;
   v = v < -127 ? -127 : v;
-  return v;
+  return q != q ? 0 : v;                 // (selects, no branch)
 }
 
 // 1/sqrt with two roundings (ref_qwen3.py:37-38)
