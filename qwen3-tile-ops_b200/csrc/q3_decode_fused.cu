@@ -24,9 +24,19 @@ __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
   pdl_wait();
   __shared__ float gmax[4][8];
   const int m = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const float *bs = a.bsum + static_cast<size_t>(m) * (a.H / 32);
+  // the 32 block sums (H == 1024) loaded at once, then added in block order
+  const float4 *bs = reinterpret_cast<const float4 *>(a.bsum + static_cast<size_t>(m) * 32);
+  float4 b4[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b4[i] = bs[i];
   float ss = 0.0f;
-  for (int b = 0; b < a.H / 32; ++b) ss = __fadd_rn(ss, bs[b]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    ss = __fadd_rn(ss, b4[i].x);
+    ss = __fadd_rn(ss, b4[i].y);
+    ss = __fadd_rn(ss, b4[i].z);
+    ss = __fadd_rn(ss, b4[i].w);
+  }
   ss = __fadd_rn(__fmul_rn(ss, a.inv), kEps);
   const float r = rsqrt_ref(ss);
   float hv[4];
