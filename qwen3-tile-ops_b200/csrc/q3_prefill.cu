@@ -405,7 +405,20 @@ __global__ void k_pf_norm_amax(const float *x, const float *bsum, const float *w
   const int m = static_cast<int>(wi / nch), ch = static_cast<int>(wi % nch);
   const float *bs = bsum + static_cast<size_t>(m) * (H / 32);
   float ss = 0.0f;
-  for (int b = 0; b < H / 32; ++b) ss = __fadd_rn(ss, bs[b]);    // blocks in order
+  if (H == 1024) {                                   // 32 block sums loaded at once
+    float4 b4[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b4[i] = reinterpret_cast<const float4 *>(bs)[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ss = __fadd_rn(ss, b4[i].x);
+      ss = __fadd_rn(ss, b4[i].y);
+      ss = __fadd_rn(ss, b4[i].z);
+      ss = __fadd_rn(ss, b4[i].w);
+    }
+  } else {
+    for (int b = 0; b < H / 32; ++b) ss = __fadd_rn(ss, bs[b]);  // blocks in order
+  }
   ss = __fmul_rn(ss, inv);
   ss = __fadd_rn(ss, kEps);
   const float r = rsqrt_ref(ss);

@@ -64,7 +64,7 @@ __device__ __forceinline__ void sys_signal(unsigned *ctr) {
 __global__ void __launch_bounds__(1024) k_tp_reduce_norm(TpReduceArgs a) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float bsum[32];
+  __shared__ __align__(16) float bsum[32];
   __shared__ float gmax[32];
   const int m = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
   if (t < a.world && !wait_count(a.sig + t, a.expect[t], a.wait_ns))
@@ -87,8 +87,17 @@ __global__ void __launch_bounds__(1024) k_tp_reduce_norm(TpReduceArgs a) {
   const float b = warp_tree_sum(__fmul_rn(xv, xv));
   if (lane == 0) bsum[warp] = b;
   __syncthreads();
+  float4 b4[8];                           // the 32 block sums at once, then in block order
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b4[i] = reinterpret_cast<const float4 *>(bsum)[i];
   float ss = 0.0f;
-  for (int k = 0; k < 32; ++k) ss = __fadd_rn(ss, bsum[k]);   // block order
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    ss = __fadd_rn(ss, b4[i].x);
+    ss = __fadd_rn(ss, b4[i].y);
+    ss = __fadd_rn(ss, b4[i].z);
+    ss = __fadd_rn(ss, b4[i].w);
+  }
   ss = __fadd_rn(__fmul_rn(ss, a.inv), kEps);
   const float r = rsqrt_ref(ss);
   const float hv = __fmul_rn(__fmul_rn(xv, r), a.w[t]);
