@@ -45,8 +45,13 @@ namespace dec {
 using namespace tcx;
 
 constexpr int NCW = 4;                  // softmax warps
-constexpr int THREADS = (NCW + 2) * 32;
-constexpr int PRODUCER = NCW, MMA_WARP = NCW + 1;
+// With two V slots (at most 3 CTAs per SM) the K and V pages come from two
+// producer warps, so a K copy never queues behind a V slot that waits for the
+// softmax (256 pairs: 38.9 against 42.1 us); with one V slot (4 CTAs per SM)
+// one producer warp interleaves them (the seventh warp cost more than it gave).
+template <int VS>
+__host__ __device__ constexpr int threads_of() { return (NCW + (VS == 2 ? 3 : 2)) * 32; }
+constexpr int PRODUCER = NCW, MMA_WARP = NCW + 1, VPRODUCER = NCW + 2;
 constexpr int TAB_CACHE = 512;          // page-table entries kept in shared memory
 constexpr int TMEM_COLS = 64;           // QK slots at 0 and 16, PV slots at 32 and 48
 constexpr unsigned kErrPage = 2u;       // a page index >= num_pages (copy skipped)
@@ -100,7 +105,7 @@ __device__ __forceinline__ uint32_t page_of(const S &sm, const uint16_t *table, 
 }
 
 template <int VS>
-__global__ void __launch_bounds__(THREADS, VS == 1 ? 4 : 3)
+__global__ void __launch_bounds__(threads_of<VS>(), VS == 1 ? 4 : 3)
     k_attention_decode(const char *__restrict__ kpool, const char *__restrict__ vpool,
                        DecodeAttnArgs p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -121,6 +126,7 @@ __global__ void __launch_bounds__(THREADS, VS == 1 ? 4 : 3)
   const int G = (nb + 3) >> 2;                     // groups of 4 blocks
 
   // ---- set-up: B operands (zero except the rows written later), barriers, TMEM
+  constexpr int THREADS = threads_of<VS>();
   for (int i = tid * 4; i < 1024; i += THREADS * 4) {
     if (i >= 256) *reinterpret_cast<int *>(sm.qt + i) = 0;
     *reinterpret_cast<int *>(sm.pq[0] + i) = 0;
@@ -158,15 +164,26 @@ __global__ void __launch_bounds__(THREADS, VS == 1 ? 4 : 3)
 
   float den[2] = {0.0f, 0.0f}, res[2] = {0.0f, 0.0f};   // softmax threads: value column tid
 
-  if (warp == PRODUCER) {
-    // ---- producer: K(0), K(1), V(0), K(2), V(1), ..., K(G-1), V(G-2), V(G-1)
+  if (warp == PRODUCER || (VS == 2 && warp == VPRODUCER)) {
+    // ---- producers.  Two V slots: K(0), K(1), ... through the 2-slot K ring
+    // (this warp) and V(0), V(1), ... through the V slots (the other producer
+    // warp).  One V slot: one warp issues K(0), K(1), V(0), K(2), V(1), ...,
+    // K(G-1), V(G-2), V(G-1).
     const int r4 = lane >> 3, c16 = lane & 7;     // lane: 16-byte chunk c16 of rows 4i + r4
-    for (int it = 0; it < 2 * G; ++it) {
+    const int n_it = VS == 2 ? G : 2 * G;
+    for (int it = 0; it < n_it; ++it) {
       int g, isv;
-      if (it == 0) { g = 0; isv = 0; }
-      else if (it == 2 * G - 1) { g = G - 1; isv = 1; }
-      else { g = (it + 1) >> 1; isv = !(it & 1); if (isv) g -= 1; }
-      // it odd -> K((it+1)/2), it even (>0) -> V(it/2 - 1)
+      if (VS == 2) {
+        g = it;
+        isv = warp == VPRODUCER;
+      } else if (it == 0) {
+        g = 0; isv = 0;
+      } else if (it == 2 * G - 1) {
+        g = G - 1; isv = 1;
+      } else {                                    // it odd -> K((it+1)/2), it even -> V(it/2 - 1)
+        g = (it + 1) >> 1; isv = !(it & 1); if (isv) g -= 1;
+      }
+      const char *pool = isv ? vpool : kpool;
       unsigned long long *full;
       int8_t(*dst)[4096];
       if (!isv) {
@@ -180,7 +197,6 @@ __global__ void __launch_bounds__(THREADS, VS == 1 ? 4 : 3)
         full = &sm.vfull[vslot];
         dst = sm.vbuf[vslot];
       }
-      const char *pool = isv ? vpool : kpool;
       const int first = 4 * g, count = min(4, nb - first);
       for (int q = 0; q < count; ++q) {
         const uint32_t page = page_of(sm, table, first + q);
@@ -418,7 +434,7 @@ static int launch_decode(bool pdl, dim3 grid, size_t smem, cudaStream_t s, const
     q3h::set_cuda_error(attr_err);
     return Q3_ERR_CUDA;
   }
-  return q3h::launch_ex(pdl, dec::k_attention_decode<VS>, grid, dim3(dec::THREADS), smem, s,
+  return q3h::launch_ex(pdl, dec::k_attention_decode<VS>, grid, dim3(dec::threads_of<VS>()), smem, s,
                         static_cast<const char *>(k_pool), static_cast<const char *>(v_pool), a);
 }
 
