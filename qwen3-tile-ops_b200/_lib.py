@@ -120,6 +120,7 @@ SIGS = {
     "q3_exp_rows": [VP, VP, C.c_void_p],
     "q3_exp2_rows": [VP, VP, C.c_void_p],
     "q3_exp2_selfcheck": [C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p],
+    "q3_quant_selfcheck": [C.c_uint32, C.c_uint32, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p],
     "q3_last_cuda_error": [],
     "q3_device_check": [],
     "q3_launch_count": [],

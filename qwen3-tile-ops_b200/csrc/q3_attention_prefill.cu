@@ -297,13 +297,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       den = __fadd_rn(__fmul_rn(den, corr), psum);
       m = mn;
       uint32_t w2[2];
+      if (quant_rcp_ok(pm)) {                       // one reciprocal for the 8 codes
+        const float rpm = __frcp_rn(pm);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint32_t b0 = static_cast<uint8_t>(quant1(pv[4 * c + 0], pm));
-        const uint32_t b1 = static_cast<uint8_t>(quant1(pv[4 * c + 1], pm));
-        const uint32_t b2 = static_cast<uint8_t>(quant1(pv[4 * c + 2], pm));
-        const uint32_t b3 = static_cast<uint8_t>(quant1(pv[4 * c + 3], pm));
-        w2[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t b0 = static_cast<uint8_t>(quant1_rcp(pv[4 * c + 0], pm, rpm));
+          const uint32_t b1 = static_cast<uint8_t>(quant1_rcp(pv[4 * c + 1], pm, rpm));
+          const uint32_t b2 = static_cast<uint8_t>(quant1_rcp(pv[4 * c + 2], pm, rpm));
+          const uint32_t b3 = static_cast<uint8_t>(quant1_rcp(pv[4 * c + 3], pm, rpm));
+          w2[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t b0 = static_cast<uint8_t>(quant1(pv[4 * c + 0], pm));
+          const uint32_t b1 = static_cast<uint8_t>(quant1(pv[4 * c + 1], pm));
+          const uint32_t b2 = static_cast<uint8_t>(quant1(pv[4 * c + 2], pm));
+          const uint32_t b3 = static_cast<uint8_t>(quant1(pv[4 * c + 3], pm));
+          w2[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
       }
       // keys 8 pt .. : 16-key chunk pt / 2, bytes 8 (pt % 2) .. of the row's 16
       *reinterpret_cast<uint2 *>(sm.pq[slot] + (pt >> 1) * (8 * 2 * ROWS) + (r >> 3) * 128 +

@@ -215,6 +215,28 @@ __device__ __forceinline__ int quant1(float x, float scale) {
   return q != q ? 0 : v;                 // (selects, no branch)
 }
 
+// quant1 with the quotient from a correctly rounded reciprocal r = 1/scale
+// (one per scale, shared by its elements) and Markstein's correction: with r
+// within half an ulp of 1/s and q0 = x r within one ulp of x/s, the residual
+// e = x - q0 s is exact and fma(e, r, q0) is the correctly rounded x/s
+// (P. Markstein, IBM J. Res. Dev. 34(1), 1990).  The caller keeps s within
+// [2^-100, 2^100] (no underflow in e); quotients of 2^16 and beyond, where the
+// theorem's no-overflow condition may fail, saturate to +-127 as the clamped
+// quotient does, and NaN x gives 0.  Equal to quant1(x, s) for every x there.
+__device__ __forceinline__ int quant1_rcp(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-q0, s, x);
+  const float q = __fmaf_rn(e, r, q0);
+  int v = __float2int_rn(q);
+  v = v > 127 ? 127 : v;
+  v = v < -127 ? -127 : v;
+  v = fabsf(q0) >= 65536.0f ? (x > 0.0f ? 127 : -127) : v;   // (and +-inf)
+  return x != x ? 0 : v;
+}
+__host__ __device__ __forceinline__ bool quant_rcp_ok(float s) {
+  return s >= 7.888609052210118e-31f && s <= 1.2676506002282294e30f;   // 2^-100 .. 2^100
+}
+
 // 1/sqrt with two roundings (ref_qwen3.py:37-38)
 __device__ __forceinline__ float rsqrt_ref(float x) {
   return __fdiv_rn(1.0f, __fsqrt_rn(x));

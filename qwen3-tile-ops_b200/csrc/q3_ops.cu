@@ -397,6 +397,32 @@ __global__ void k_exp2_selfcheck(uint32_t lo, uint32_t hi, unsigned long long *c
   }
 }
 
+// quant1_rcp against quant1 for every float32 x in [lo, hi) and the scale s
+__global__ void k_quant_selfcheck(uint32_t lo, uint32_t hi, float s, unsigned long long *count,
+                                  uint32_t *first_bad) {
+  const float r = __frcp_rn(s);
+  const uint64_t n = static_cast<uint64_t>(hi) - lo;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t b = lo + static_cast<uint32_t>(i);
+    const float x = __uint_as_float(b);
+    if (quant1_rcp(x, s, r) != quant1(x, s)) {
+      atomicAdd(count, 1ull);
+      atomicMin(first_bad, b);
+    }
+  }
+}
+
+extern "C" int q3_quant_selfcheck(uint32_t lo_bits, uint32_t hi_bits, float scale,
+                                  unsigned long long *count, uint32_t *first_bad, void *stream) {
+  if (!count || !first_bad) return Q3_ERR_NULL;
+  if (hi_bits < lo_bits || !quant_rcp_ok(scale)) return Q3_ERR_SHAPE;
+  if (hi_bits == lo_bits) return Q3_OK;
+  k_quant_selfcheck<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(lo_bits, hi_bits, scale, count,
+                                                                first_bad);
+  return launch_status();
+}
+
 extern "C" int q3_exp2_selfcheck(uint32_t lo_bits, uint32_t hi_bits, unsigned long long *count,
                                  uint32_t *first_bad, void *stream) {
   if (!count || !first_bad) return Q3_ERR_NULL;

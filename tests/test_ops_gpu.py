@@ -364,6 +364,30 @@ def test_exp2_short_evaluation_exhaustive(q3):
     assert bad == 0, f"{bad} inputs differ, first bit pattern {int(first.item()) & 0xffffffff:#010x}"
 
 
+def test_quant_from_reciprocal_exhaustive(q3):
+    """The int8 code from a shared reciprocal of the scale (Markstein's
+    correction) equals the code from the IEEE quotient (ref_qwen3.py:69-76) on
+    EVERY float32 x -- NaN, infinities, subnormals and the double-rounding ties
+    at half-integers included -- for scales at powers of two, next to them, at
+    the ends of the allowed range and with seeded random mantissas."""
+    lib = q3._lib.lib()
+    rng = np.random.default_rng(7)
+    scales = [2.0 ** e for e in (-100, -30, -7, 0, 5, 40, 100)]
+    scales += [float(np.nextafter(F(2.0 ** e), F(0))) for e in (-7, 0, 3)]
+    scales += [float(np.nextafter(F(2.0 ** e), F(np.inf))) for e in (-7, 0, 3)]
+    scales += [float(F(m) * F(2.0) ** F(e)) for m, e in
+               zip(rng.uniform(1.0, 2.0, 12), rng.integers(-60, 60, 12))]
+    scales += [float(F(v) / F(127)) for v in rng.uniform(1e-4, 1.0, 6)]   # absmax / 127
+    count = torch.zeros(1, dtype=torch.int64, device="cuda")
+    first = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    for sc in scales:
+        for lo, hi in ((0x00000000, 0x80000000), (0x80000000, 0xFFFFFFFF)):
+            assert lib.q3_quant_selfcheck(lo, hi, sc, count.data_ptr(), first.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    bad = int(count.item())
+    assert bad == 0, f"{bad} codes differ, first bit pattern {int(first.item()) & 0xffffffff:#010x}"
+
+
 # ---------------------------------------------------------------- attention
 def _pool_from_contiguous(k8, ks, v8, vs, kv_heads, table):
     """Scatter contiguous K/V [T][kv_heads*128] into pages following `table`."""
