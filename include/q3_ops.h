@@ -527,10 +527,12 @@ int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream);
 int q3_exp2_selfcheck(uint32_t lo_bits, uint32_t hi_bits, unsigned long long *count,
                       uint32_t *first_bad, void *stream);
 
-/* No counterpart in the reference: self-check of the int8 requantisation from
- * a shared reciprocal (Markstein's correction of x * (1/scale), used where one
- * scale serves many codes) against the IEEE quotient: every float32 bit
- * pattern x in [lo_bits, hi_bits) with the given scale (2^-100 .. 2^100);
+/* No counterpart in the reference: self-check of the library's int8
+ * requantisation -- the code from a shared reciprocal (Markstein's correction
+ * of x * (1/scale), used where one scale serves many codes) and the code from
+ * the IEEE quotient, both rounded in float -- against the quotient rounded by
+ * the float -> int conversion: every float32 bit pattern x in
+ * [lo_bits, hi_bits) with the given scale (2^-100 .. 2^100);
  * *count (device, caller-zeroed) gains the codes that differ and *first_bad
  * (device, caller-set to 0xffffffff) the smallest differing x. */
 int q3_quant_selfcheck(uint32_t lo_bits, uint32_t hi_bits, float scale, unsigned long long *count,

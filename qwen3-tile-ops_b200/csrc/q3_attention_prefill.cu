@@ -297,25 +297,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       den = __fadd_rn(__fmul_rn(den, corr), psum);
       m = mn;
       uint32_t w2[2];
-      if (quant_rcp_ok(pm)) {                       // one reciprocal for the 8 codes
-        const float rpm = __frcp_rn(pm);
+      int pq8[KPK];
+      quant_n(pv, pm, pq8);                         // one reciprocal for the 8 codes
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t b0 = static_cast<uint8_t>(quant1_rcp(pv[4 * c + 0], pm, rpm));
-          const uint32_t b1 = static_cast<uint8_t>(quant1_rcp(pv[4 * c + 1], pm, rpm));
-          const uint32_t b2 = static_cast<uint8_t>(quant1_rcp(pv[4 * c + 2], pm, rpm));
-          const uint32_t b3 = static_cast<uint8_t>(quant1_rcp(pv[4 * c + 3], pm, rpm));
-          w2[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t b0 = static_cast<uint8_t>(quant1(pv[4 * c + 0], pm));
-          const uint32_t b1 = static_cast<uint8_t>(quant1(pv[4 * c + 1], pm));
-          const uint32_t b2 = static_cast<uint8_t>(quant1(pv[4 * c + 2], pm));
-          const uint32_t b3 = static_cast<uint8_t>(quant1(pv[4 * c + 3], pm));
-          w2[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-        }
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t b0 = static_cast<uint8_t>(pq8[4 * c + 0]);
+        const uint32_t b1 = static_cast<uint8_t>(pq8[4 * c + 1]);
+        const uint32_t b2 = static_cast<uint8_t>(pq8[4 * c + 2]);
+        const uint32_t b3 = static_cast<uint8_t>(pq8[4 * c + 3]);
+        w2[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
       }
       // keys 8 pt .. : 16-key chunk pt / 2, bytes 8 (pt % 2) .. of the row's 16
       *reinterpret_cast<uint2 *>(sm.pq[slot] + (pt >> 1) * (8 * 2 * ROWS) + (r >> 3) * 128 +
@@ -344,12 +334,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float scale = __fmul_rn(omx, kInv127);
     if (active) {
       uint32_t w4[KPC / 4];
+      int o8[KPC];
+      quant_n(res, scale, o8);
 #pragma unroll
       for (int c = 0; c < KPC / 4; ++c) {
-        const uint32_t b0 = static_cast<uint8_t>(quant1(res[4 * c + 0], scale));
-        const uint32_t b1 = static_cast<uint8_t>(quant1(res[4 * c + 1], scale));
-        const uint32_t b2 = static_cast<uint8_t>(quant1(res[4 * c + 2], scale));
-        const uint32_t b3 = static_cast<uint8_t>(quant1(res[4 * c + 3], scale));
+        const uint32_t b0 = static_cast<uint8_t>(o8[4 * c + 0]);
+        const uint32_t b1 = static_cast<uint8_t>(o8[4 * c + 1]);
+        const uint32_t b2 = static_cast<uint8_t>(o8[4 * c + 2]);
+        const uint32_t b3 = static_cast<uint8_t>(o8[4 * c + 3]);
         w4[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
       }
       uint4 *dst = reinterpret_cast<uint4 *>(p.o8 + grow * p.o_rb + h * 128 + KPC * pt);

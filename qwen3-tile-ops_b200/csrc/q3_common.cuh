@@ -206,13 +206,18 @@ __device__ __forceinline__ void exp_ref_fast_n(float (&v)[N], const unsigned lon
   exp2_cr_fast_n(x, v, tab);
 }
 
-// rne(x / scale) saturated to +-127, NaN -> 0 (ref_qwen3.py:69-76)
-__device__ __forceinline__ int quant1(float x, float scale) {
-  const float q = __fdiv_rn(x, scale);
-  int v = __float2int_rn(q);
-  v = v > 127 ? 127 : v;
-  v = v < -127 ? -127 : v;
+// rne(x / scale) saturated to +-127, NaN -> 0 (ref_qwen3.py:69-76).  The
+// quotient is clamped to [-127, 127] in float and rounded to an integer by the
+// 1.5 * 2^23 shifter: ties to even, as rint, and clamping to integer bounds
+// before the rounding gives what clamping after it does.  No float -> int
+// conversion runs (those issue on a narrow pipe).
+__device__ __forceinline__ int quant1_from_quotient(float q) {
+  const float c = fminf(fmaxf(q, -127.0f), 127.0f);
+  const int v = __float_as_int(__fadd_rn(c, 12582912.0f)) - 0x4B400000;
   return q != q ? 0 : v;                 // (selects, no branch)
+}
+__device__ __forceinline__ int quant1(float x, float scale) {
+  return quant1_from_quotient(__fdiv_rn(x, scale));
 }
 
 // quant1 with the quotient from a correctly rounded reciprocal r = 1/scale
@@ -226,15 +231,27 @@ __device__ __forceinline__ int quant1(float x, float scale) {
 __device__ __forceinline__ int quant1_rcp(float x, float s, float r) {
   const float q0 = __fmul_rn(x, r);
   const float e = __fmaf_rn(-q0, s, x);
-  const float q = __fmaf_rn(e, r, q0);
-  int v = __float2int_rn(q);
-  v = v > 127 ? 127 : v;
-  v = v < -127 ? -127 : v;
-  v = fabsf(q0) >= 65536.0f ? (x > 0.0f ? 127 : -127) : v;   // (and +-inf)
+  float q = __fmaf_rn(e, r, q0);
+  q = fabsf(q0) >= 65536.0f ? q0 : q;   // saturates with q0's sign (q may be NaN there)
+  q = fminf(fmaxf(q, -127.0f), 127.0f);
+  const int v = __float_as_int(__fadd_rn(q, 12582912.0f)) - 0x4B400000;
   return x != x ? 0 : v;
 }
 __host__ __device__ __forceinline__ bool quant_rcp_ok(float s) {
   return s >= 7.888609052210118e-31f && s <= 1.2676506002282294e30f;   // 2^-100 .. 2^100
+}
+// quant1 of N values that share one scale (a warp-uniform choice): from one
+// reciprocal where quant_rcp_ok allows it, else from the quotients.
+template <int N>
+__device__ __forceinline__ void quant_n(const float (&x)[N], float s, int (&q)[N]) {
+  if (quant_rcp_ok(s)) {
+    const float r = __frcp_rn(s);
+#pragma unroll
+    for (int i = 0; i < N; ++i) q[i] = quant1_rcp(x[i], s, r);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) q[i] = quant1(x[i], s);
+  }
 }
 
 // 1/sqrt with two roundings (ref_qwen3.py:37-38)

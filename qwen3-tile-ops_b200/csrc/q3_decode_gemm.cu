@@ -358,10 +358,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int k = 0; k < 4; ++k) mx = fmaxf(mx, fabsf(v[k]));
         mx = warp_tree_max(mx);
         const float scale = __fmul_rn(mx, kInv127);
+        int qv[4];
+        quant_n(v, scale, qv);
         if (h < p.heads) {
           int8_t *dst = p.q8 + static_cast<size_t>(m) * p.heads * 128 + h * 128;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = static_cast<int8_t>(quant1(v[k], scale));
+          for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = static_cast<int8_t>(qv[k]);
           if (lane == 0) p.qs[m * p.heads + h] = scale;
         } else {
           const int kvh = is_v ? h - p.heads - p.kv_heads : h - p.heads;
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int kw = p.kv_heads * 128;
           int8_t *dst = reinterpret_cast<int8_t *>(is_v ? p.pv : p.pk) + row * kw + kvh * 128;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = static_cast<int8_t>(quant1(v[k], scale));
+          for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = static_cast<int8_t>(qv[k]);
           if (lane == 0)
             reinterpret_cast<float *>(is_v ? p.pvs : p.pks)[row * p.kv_heads + kvh] = scale;
         }
@@ -426,8 +428,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         const float scale = __fmul_rn(mx, kInv127);
         const int grp = tile / 2;
         int8_t *dst = p.s8 + static_cast<size_t>(m) * p.I + grp * 256;
+        int qv[8];
+        quant_n(sw, scale, qv);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) dst[lane + 32 * k] = static_cast<int8_t>(quant1(sw[k], scale));
+        for (int k = 0; k < 8; ++k) dst[lane + 32 * k] = static_cast<int8_t>(qv[k]);
         if (lane == 0) p.ss[static_cast<size_t>(m) * (p.I / 256) + grp] = scale;
       }
     }

@@ -393,7 +393,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               const float scale = __fmul_rn(mx, kInv127);
               int8_t *q = reinterpret_cast<int8_t *>(p.q8 + (long)(m0 + m) * p.q8_rb) + row0;
 #pragma unroll
-              for (int k = 0; k < 8; ++k) q[lane + 32 * k] = static_cast<int8_t>(quant1(v[k], scale));
+              int qv[8];
+              quant_n(v, scale, qv);
+#pragma unroll
+              for (int k = 0; k < 8; ++k) q[lane + 32 * k] = static_cast<int8_t>(qv[k]);
               if (lane == 0)
                 *reinterpret_cast<float *>(p.qs + (long)(m0 + m) * p.qs_rb + (row0 / 256) * 4) = scale;
             }
@@ -450,7 +453,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             const float scale = __fmul_rn(mx, kInv127);
             int8_t *q = reinterpret_cast<int8_t *>(p.q8 + (long)(m0 + m) * p.q8_rb) + r0;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) q[lane + 32 * k] = static_cast<int8_t>(quant1(v[k], scale));
+            int qv[4];
+            quant_n(v, scale, qv);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) q[lane + 32 * k] = static_cast<int8_t>(qv[k]);
             if (lane == 0)
               *reinterpret_cast<float *>(p.qs + (long)(m0 + m) * p.qs_rb + (r0 / 128) * 4) = scale;
           }

@@ -397,7 +397,18 @@ __global__ void k_exp2_selfcheck(uint32_t lo, uint32_t hi, unsigned long long *c
   }
 }
 
-// quant1_rcp against quant1 for every float32 x in [lo, hi) and the scale s
+// The int8 code as the reference forms it: the IEEE quotient, rounded to
+// nearest even by the float -> int conversion, then saturated; NaN -> 0.
+__device__ int quant1_conv(float x, float s) {
+  const float q = __fdiv_rn(x, s);
+  int v = __float2int_rn(q);
+  v = v > 127 ? 127 : v;
+  v = v < -127 ? -127 : v;
+  return q != q ? 0 : v;
+}
+
+// quant1 and quant1_rcp against quant1_conv for every float32 x in [lo, hi)
+// and the scale s
 __global__ void k_quant_selfcheck(uint32_t lo, uint32_t hi, float s, unsigned long long *count,
                                   uint32_t *first_bad) {
   const float r = __frcp_rn(s);
@@ -406,7 +417,8 @@ __global__ void k_quant_selfcheck(uint32_t lo, uint32_t hi, float s, unsigned lo
        i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
     const uint32_t b = lo + static_cast<uint32_t>(i);
     const float x = __uint_as_float(b);
-    if (quant1_rcp(x, s, r) != quant1(x, s)) {
+    const int want = quant1_conv(x, s);
+    if (quant1_rcp(x, s, r) != want || quant1(x, s) != want) {
       atomicAdd(count, 1ull);
       atomicMin(first_bad, b);
     }

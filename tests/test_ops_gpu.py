@@ -365,11 +365,13 @@ def test_exp2_short_evaluation_exhaustive(q3):
 
 
 def test_quant_from_reciprocal_exhaustive(q3):
-    """The int8 code from a shared reciprocal of the scale (Markstein's
-    correction) equals the code from the IEEE quotient (ref_qwen3.py:69-76) on
-    EVERY float32 x -- NaN, infinities, subnormals and the double-rounding ties
-    at half-integers included -- for scales at powers of two, next to them, at
-    the ends of the allowed range and with seeded random mantissas."""
+    """The int8 codes the kernels form -- from a shared reciprocal of the scale
+    (Markstein's correction) and from the IEEE quotient, each clamped and
+    rounded in float -- equal the IEEE quotient rounded by the float -> int
+    conversion and saturated (ref_qwen3.py:69-76) on EVERY float32 x -- NaN,
+    infinities, subnormals and the double-rounding ties at half-integers
+    included -- for scales at powers of two, next to them, at the ends of the
+    allowed range and with seeded random mantissas."""
     lib = q3._lib.lib()
     rng = np.random.default_rng(7)
     scales = [2.0 ** e for e in (-100, -30, -7, 0, 5, 40, 100)]
