@@ -528,14 +528,16 @@ int q3_exp2_selfcheck(uint32_t lo_bits, uint32_t hi_bits, unsigned long long *co
                       uint32_t *first_bad, void *stream);
 
 /* No counterpart in the reference: self-check of the library's int8
- * requantisation -- the code from a shared reciprocal (Markstein's correction
- * of x * (1/scale), used where one scale serves many codes) and the code from
- * the IEEE quotient, both rounded in float -- against the quotient rounded by
- * the float -> int conversion: every float32 bit pattern x in
- * [lo_bits, hi_bits) with the given scale (2^-100 .. 2^100);
- * *count (device, caller-zeroed) gains the codes that differ and *first_bad
- * (device, caller-set to 0xffffffff) the smallest differing x. */
-int q3_quant_selfcheck(uint32_t lo_bits, uint32_t hi_bits, float scale, unsigned long long *count,
+ * requantisation against the IEEE quotient rounded by the float -> int
+ * conversion and saturated.  With the scale s = amax * (1/127) formed as the
+ * kernels form it: the code from the quotient rounded in float, for every
+ * float32 bit pattern x in [lo_bits, hi_bits); and the code from a shared
+ * reciprocal of s (Markstein's correction, no clamp), used where s is the scale
+ * of the values' own absolute maximum, for those x with |x| <= amax and NaN.
+ * amax finite and >= 0; *count (device, caller-zeroed) gains the codes that
+ * differ and *first_bad (device, caller-set to 0xffffffff) the smallest
+ * differing x. */
+int q3_quant_selfcheck(uint32_t lo_bits, uint32_t hi_bits, float amax, unsigned long long *count,
                        uint32_t *first_bad, void *stream);
 
 /* ---- misc ---------------------------------------------------------------- */

@@ -255,14 +255,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       float s[KPK], ksv[KPK], vsv[KPK];
       *reinterpret_cast<float4 *>(&ksv[0]) = *reinterpret_cast<const float4 *>(&sm.ks[st][KPK * pt]);
       *reinterpret_cast<float4 *>(&ksv[4]) = *reinterpret_cast<const float4 *>(&sm.ks[st][KPK * pt + 4]);
+      // every key of the block at or before every row of this warp: no mask
+      const bool open = 32 * j + 31 <= r0 + qd * 32;
       float bm = kNegInf;
+      if (open) {
 #pragma unroll
-      for (int i = 0; i < KPK; ++i) {
-        const int key = 32 * j + KPK * pt + i;
-        s[i] = (key <= pos)
-                   ? __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a[i]), ksv[i]), qsc), p.qk_scale)
-                   : kNegInf;
-        bm = fmaxf(bm, s[i]);
+        for (int i = 0; i < KPK; ++i) {
+          s[i] = __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a[i]), ksv[i]), qsc), p.qk_scale);
+          bm = fmaxf(bm, s[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < KPK; ++i) {
+          const int key = 32 * j + KPK * pt + i;
+          s[i] = (key <= pos)
+                     ? __fmul_rn(__fmul_rn(__fmul_rn(i2f_small(a[i]), ksv[i]), qsc), p.qk_scale)
+                     : kNegInf;
+          bm = fmaxf(bm, s[i]);
+        }
       }
       sm.xmax[slot][r][pt] = bm;
       rows_sync(qd);
@@ -279,11 +289,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float ps = tree8_sum(s);
       *reinterpret_cast<float4 *>(&vsv[0]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt]);
       *reinterpret_cast<float4 *>(&vsv[4]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt + 4]);
+      if (open) {
 #pragma unroll
-      for (int i = 0; i < KPK; ++i) {
-        const int key = 32 * j + KPK * pt + i;
-        pv[i] = (key <= pos) ? __fmul_rn(s[i], vsv[i]) : 0.0f;
-        am = fmaxf(am, fabsf(pv[i]));
+        for (int i = 0; i < KPK; ++i) {
+          pv[i] = __fmul_rn(s[i], vsv[i]);
+          am = fmaxf(am, fabsf(pv[i]));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < KPK; ++i) {
+          const int key = 32 * j + KPK * pt + i;
+          pv[i] = (key <= pos) ? __fmul_rn(s[i], vsv[i]) : 0.0f;
+          am = fmaxf(am, fabsf(pv[i]));
+        }
       }
       sm.xsum[slot][r][pt] = ps;
       sm.xam[slot][r][pt] = am;
@@ -298,7 +316,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       m = mn;
       uint32_t w2[2];
       int pq8[KPK];
-      quant_n(pv, pm, pq8);                         // one reciprocal for the 8 codes
+      quant_n_absmax(pv, pm, pq8);                         // one reciprocal for the 8 codes
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const uint32_t b0 = static_cast<uint8_t>(pq8[4 * c + 0]);
@@ -335,7 +353,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (active) {
       uint32_t w4[KPC / 4];
       int o8[KPC];
-      quant_n(res, scale, o8);
+      quant_n_absmax(res, scale, o8);
 #pragma unroll
       for (int c = 0; c < KPC / 4; ++c) {
         const uint32_t b0 = static_cast<uint8_t>(o8[4 * c + 0]);

@@ -220,34 +220,38 @@ __device__ __forceinline__ int quant1(float x, float scale) {
   return quant1_from_quotient(__fdiv_rn(x, scale));
 }
 
-// quant1 with the quotient from a correctly rounded reciprocal r = 1/scale
-// (one per scale, shared by its elements) and Markstein's correction: with r
-// within half an ulp of 1/s and q0 = x r within one ulp of x/s, the residual
-// e = x - q0 s is exact and fma(e, r, q0) is the correctly rounded x/s
-// (P. Markstein, IBM J. Res. Dev. 34(1), 1990).  The caller keeps s within
-// [2^-100, 2^100] (no underflow in e); quotients of 2^16 and beyond, where the
-// theorem's no-overflow condition may fail, saturate to +-127 as the clamped
-// quotient does, and NaN x gives 0.  Equal to quant1(x, s) for every x there.
-__device__ __forceinline__ int quant1_rcp(float x, float s, float r) {
+// quant1 of a value x under the scale s = RN(amax * RN(1/127)) of an absolute
+// maximum amax >= |x| (every requantisation of the path has this form), from
+// a correctly rounded reciprocal r = 1/s shared by the values of the scale and
+// Markstein's correction: with r within half an ulp of 1/s and q0 = x r within
+// one ulp of x/s, the residual e = x - q0 s is exact and fma(e, r, q0) is the
+// correctly rounded x/s (P. Markstein, IBM J. Res. Dev. 34(1), 1990).  The
+// caller keeps s within [2^-100, 2^100] (quant_rcp_ok: s is normal, so its two
+// roundings are relative errors below 2^-24 each, and e does not underflow).
+// Then |x/s| <= 127 (1 + 2^-24)^2 < 127.5, so the rounded quotient needs no
+// clamp to +-127 and cannot overflow; it is rounded to an integer by the
+// 1.5 * 2^23 shifter (ties to even, as rint).  NaN x gives 0.  Equal to
+// quant1(x, s) for every such x (q3_quant_selfcheck).
+__device__ __forceinline__ int quant1_rcp_absmax(float x, float s, float r) {
   const float q0 = __fmul_rn(x, r);
   const float e = __fmaf_rn(-q0, s, x);
-  float q = __fmaf_rn(e, r, q0);
-  q = fabsf(q0) >= 65536.0f ? q0 : q;   // saturates with q0's sign (q may be NaN there)
-  q = fminf(fmaxf(q, -127.0f), 127.0f);
+  const float q = __fmaf_rn(e, r, q0);
   const int v = __float_as_int(__fadd_rn(q, 12582912.0f)) - 0x4B400000;
   return x != x ? 0 : v;
 }
 __host__ __device__ __forceinline__ bool quant_rcp_ok(float s) {
   return s >= 7.888609052210118e-31f && s <= 1.2676506002282294e30f;   // 2^-100 .. 2^100
 }
-// quant1 of N values that share one scale (a warp-uniform choice): from one
-// reciprocal where quant_rcp_ok allows it, else from the quotients.
+// quant1 of N values under the scale of their absolute maximum (s =
+// RN(amax * kInv127), amax = max |x[i]| over these values and any others of
+// the scale; a warp-uniform choice): from one reciprocal where quant_rcp_ok
+// allows it, else from the quotients.
 template <int N>
-__device__ __forceinline__ void quant_n(const float (&x)[N], float s, int (&q)[N]) {
+__device__ __forceinline__ void quant_n_absmax(const float (&x)[N], float s, int (&q)[N]) {
   if (quant_rcp_ok(s)) {
     const float r = __frcp_rn(s);
 #pragma unroll
-    for (int i = 0; i < N; ++i) q[i] = quant1_rcp(x[i], s, r);
+    for (int i = 0; i < N; ++i) q[i] = quant1_rcp_absmax(x[i], s, r);
   } else {
 #pragma unroll
     for (int i = 0; i < N; ++i) q[i] = quant1(x[i], s);

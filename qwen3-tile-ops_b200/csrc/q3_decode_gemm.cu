@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         mx = warp_tree_max(mx);
         const float scale = __fmul_rn(mx, kInv127);
         int qv[4];
-        quant_n(v, scale, qv);
+        quant_n_absmax(v, scale, qv);
         if (h < p.heads) {
           int8_t *dst = p.q8 + static_cast<size_t>(m) * p.heads * 128 + h * 128;
 #pragma unroll
@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int grp = tile / 2;
         int8_t *dst = p.s8 + static_cast<size_t>(m) * p.I + grp * 256;
         int qv[8];
-        quant_n(sw, scale, qv);
+        quant_n_absmax(sw, scale, qv);
 #pragma unroll
         for (int k = 0; k < 8; ++k) dst[lane + 32 * k] = static_cast<int8_t>(qv[k]);
         if (lane == 0) p.ss[static_cast<size_t>(m) * (p.I / 256) + grp] = scale;

@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               int8_t *q = reinterpret_cast<int8_t *>(p.q8 + (long)(m0 + m) * p.q8_rb) + row0;
 #pragma unroll
               int qv[8];
-              quant_n(v, scale, qv);
+              quant_n_absmax(v, scale, qv);
 #pragma unroll
               for (int k = 0; k < 8; ++k) q[lane + 32 * k] = static_cast<int8_t>(qv[k]);
               if (lane == 0)
@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             int8_t *q = reinterpret_cast<int8_t *>(p.q8 + (long)(m0 + m) * p.q8_rb) + r0;
 #pragma unroll
             int qv[4];
-            quant_n(v, scale, qv);
+            quant_n_absmax(v, scale, qv);
 #pragma unroll
             for (int k = 0; k < 4; ++k) q[lane + 32 * k] = static_cast<int8_t>(qv[k]);
             if (lane == 0)

@@ -407,30 +407,36 @@ __device__ int quant1_conv(float x, float s) {
   return q != q ? 0 : v;
 }
 
-// quant1 and quant1_rcp against quant1_conv for every float32 x in [lo, hi)
-// and the scale s
-__global__ void k_quant_selfcheck(uint32_t lo, uint32_t hi, float s, unsigned long long *count,
+// For every float32 x in [lo, hi) and the scale s = RN(amax * kInv127), as the
+// kernels form it: quant1 against quant1_conv, and, for |x| <= amax and NaN x,
+// the form of quant_n_absmax (from the reciprocal when quant_rcp_ok(s), else
+// quant1) against quant1_conv.
+__global__ void k_quant_selfcheck(uint32_t lo, uint32_t hi, float amax, unsigned long long *count,
                                   uint32_t *first_bad) {
-  const float r = __frcp_rn(s);
+  const float s = __fmul_rn(amax, kInv127);
+  const bool rcp = quant_rcp_ok(s);
+  const float r = rcp ? __frcp_rn(s) : 0.0f;
   const uint64_t n = static_cast<uint64_t>(hi) - lo;
   for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
     const uint32_t b = lo + static_cast<uint32_t>(i);
     const float x = __uint_as_float(b);
     const int want = quant1_conv(x, s);
-    if (quant1_rcp(x, s, r) != want || quant1(x, s) != want) {
+    bool bad = quant1(x, s) != want;
+    if (!(fabsf(x) > amax)) bad |= (rcp ? quant1_rcp_absmax(x, s, r) : quant1(x, s)) != want;
+    if (bad) {
       atomicAdd(count, 1ull);
       atomicMin(first_bad, b);
     }
   }
 }
 
-extern "C" int q3_quant_selfcheck(uint32_t lo_bits, uint32_t hi_bits, float scale,
+extern "C" int q3_quant_selfcheck(uint32_t lo_bits, uint32_t hi_bits, float amax,
                                   unsigned long long *count, uint32_t *first_bad, void *stream) {
   if (!count || !first_bad) return Q3_ERR_NULL;
-  if (hi_bits < lo_bits || !quant_rcp_ok(scale)) return Q3_ERR_SHAPE;
+  if (hi_bits < lo_bits || !(amax >= 0.0f && amax < INFINITY)) return Q3_ERR_SHAPE;
   if (hi_bits == lo_bits) return Q3_OK;
-  k_quant_selfcheck<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(lo_bits, hi_bits, scale, count,
+  k_quant_selfcheck<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(lo_bits, hi_bits, amax, count,
                                                                 first_bad);
   return launch_status();
 }

@@ -110,7 +110,7 @@ __global__ void k_prefill_scatter(const int8_t *k8, const int8_t *v8, const floa
 using q3::kEps;
 using q3::kInv127;
 using q3::quant1;
-using q3::quant_n;
+using q3::quant_n_absmax;
 using q3::rsqrt_ref;
 using q3::warp_tree_max;
 
@@ -161,7 +161,7 @@ __global__ void k_norm_quant_1024(const float *__restrict__ x, const float *__re
     for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(hv[i]));
     const float scale = __fmul_rn(warp_tree_max(am), kInv127);
     int qv[8];
-    quant_n(hv, scale, qv);
+    quant_n_absmax(hv, scale, qv);
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const uint32_t b0 = static_cast<uint8_t>(qv[4 * c + 0]);

@@ -365,26 +365,28 @@ def test_exp2_short_evaluation_exhaustive(q3):
 
 
 def test_quant_from_reciprocal_exhaustive(q3):
-    """The int8 codes the kernels form -- from a shared reciprocal of the scale
-    (Markstein's correction) and from the IEEE quotient, each clamped and
-    rounded in float -- equal the IEEE quotient rounded by the float -> int
-    conversion and saturated (ref_qwen3.py:69-76) on EVERY float32 x -- NaN,
-    infinities, subnormals and the double-rounding ties at half-integers
-    included -- for scales at powers of two, next to them, at the ends of the
-    allowed range and with seeded random mantissas."""
+    """The int8 codes the kernels form equal the IEEE quotient rounded by the
+    float -> int conversion and saturated (ref_qwen3.py:69-76): the quotient
+    rounded in float on EVERY float32 x, and the shared-reciprocal form
+    (Markstein's correction, no clamp: the scale is amax / 127 of the values'
+    own absolute maximum) on every x with |x| <= amax and NaN -- subnormals and
+    the double-rounding ties at half-integers included -- for absolute maxima
+    at powers of two, next to them, at and beyond the ends of the reciprocal's
+    range, at 127 times a power of two and with seeded random mantissas."""
     lib = q3._lib.lib()
     rng = np.random.default_rng(7)
-    scales = [2.0 ** e for e in (-100, -30, -7, 0, 5, 40, 100)]
-    scales += [float(np.nextafter(F(2.0 ** e), F(0))) for e in (-7, 0, 3)]
-    scales += [float(np.nextafter(F(2.0 ** e), F(np.inf))) for e in (-7, 0, 3)]
-    scales += [float(F(m) * F(2.0) ** F(e)) for m, e in
-               zip(rng.uniform(1.0, 2.0, 12), rng.integers(-60, 60, 12))]
-    scales += [float(F(v) / F(127)) for v in rng.uniform(1e-4, 1.0, 6)]   # absmax / 127
+    amaxes = [0.0] + [2.0 ** e for e in (-94, -93, -40, -7, 0, 5, 40, 106, 108)]
+    amaxes += [float(np.nextafter(F(2.0 ** e), F(0))) for e in (-7, 0, 3)]
+    amaxes += [float(np.nextafter(F(2.0 ** e), F(np.inf))) for e in (-7, 0, 3)]
+    amaxes += [float(F(127) * F(2.0) ** F(e)) for e in (-20, 0, 20)]
+    amaxes += [float(F(m) * F(2.0) ** F(e)) for m, e in
+               zip(rng.uniform(1.0, 2.0, 10), rng.integers(-80, 100, 10))]
+    amaxes += [float(F(v)) for v in rng.uniform(1e-4, 1.0, 6)]
     count = torch.zeros(1, dtype=torch.int64, device="cuda")
     first = torch.full((1,), -1, dtype=torch.int32, device="cuda")
-    for sc in scales:
+    for am in amaxes:
         for lo, hi in ((0x00000000, 0x80000000), (0x80000000, 0xFFFFFFFF)):
-            assert lib.q3_quant_selfcheck(lo, hi, sc, count.data_ptr(), first.data_ptr(), None) == 0
+            assert lib.q3_quant_selfcheck(lo, hi, am, count.data_ptr(), first.data_ptr(), None) == 0
     torch.cuda.synchronize()
     bad = int(count.item())
     assert bad == 0, f"{bad} codes differ, first bit pattern {int(first.item()) & 0xffffffff:#010x}"
