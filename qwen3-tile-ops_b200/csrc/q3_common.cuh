@@ -129,32 +129,39 @@ static __device__ const unsigned long long g_exp2_t256[Q3_EXP2_T256_N] = Q3_EXP2
 // to exp2_cr_t on every float32 input (q3_exp2_selfcheck).
 // `tab` is g_exp2_t256 or a copy of it in shared memory (the index varies per
 // lane: a shared copy serves a warp's lookups without the L1 tag traffic).
+// The shifter's bit pattern u = 0x4B400000 + k gives k's low 8 bits (the table
+// index) as u & 255 and (k >> 8) << 23 (the exponent step, mod 2^32) as
+// (u << 15) & 0xFF800000, since 0x4B400000 is a multiple of 2^22.
+__device__ __forceinline__ unsigned exp2_step_bits(unsigned ub) { return (ub << 15) & 0xFF800000u; }
+
 __device__ __forceinline__ float exp2_cr_fast_t(float x, const unsigned long long *tab) {
   if (!(x >= -125.0f && x < 128.0f)) return exp2_cr_t(x, g_exp2_frac64);
   const float u = __fadd_rn(__fmul_rn(x, 256.0f), 12582912.0f);
   const float kf = __fsub_rn(u, 12582912.0f);
-  const int k = __float_as_int(u) - 0x4B400000;
+  const unsigned ub = __float_as_uint(u);
   const double r = static_cast<double>(__fmaf_rn(kf, -0.00390625f, x));   // exact
   double p = __fma_rn(0.009618129107628477, r, 0.05550410866482158);      // ln2^4/4!, ln2^3/3!
   p = __fma_rn(p, r, 0.24022650695910072);                                 // ln2^2/2!
   p = __fma_rn(p, r, 0.6931471805599453);                                  // ln2
-  const double t = __longlong_as_double(static_cast<long long>(tab[k & 255]));
+  const double t = __longlong_as_double(static_cast<long long>(tab[ub & 255u]));
   const double y = __fma_rn(__dmul_rn(t, r), p, t);
   const unsigned low = static_cast<unsigned>(__double_as_longlong(y)) & 0x1FFFFFFFu;
   if (low - ((1u << 28) - 64u) <= 128u) return exp2_cr_t(x, g_exp2_frac64);
-  return __int_as_float(__float_as_int(__double2float_rn(y)) + ((k >> 8) << 23));
+  return __uint_as_float(__float_as_uint(__double2float_rn(y)) + exp2_step_bits(ub));
 }
 
 // exp2_cr_fast_t of N values at once: every value takes the common path without
 // a branch (so the N evaluations interleave: one chain after another would
 // leave the double pipes waiting), inputs below -151 give 0 there as well, and
-// the rare rest -- x in [-151, -125), x >= 128 or NaN, or a double result near
-// a float32 rounding midpoint -- is redone by exp2_cr_t afterwards.  Same
-// results as exp2_cr_fast_t value by value.
+// when any value is of the rare rest -- x in [-151, -125), x >= 128 or NaN, or
+// a double result near a float32 rounding midpoint -- all N are redone by
+// exp2_cr_t afterwards (one flag instead of a mask: the redo is rare and
+// exp2_cr_t is exact for every input).  Same results as exp2_cr_fast_t value by
+// value.
 template <int N>
 __device__ __forceinline__ void exp2_cr_fast_n(const float (&x)[N], float (&y)[N],
                                                const unsigned long long *tab) {
-  unsigned redo = 0;
+  bool redo = false;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     const float xi = x[i];
@@ -162,24 +169,23 @@ __device__ __forceinline__ void exp2_cr_fast_n(const float (&x)[N], float (&y)[N
     const float xc = in ? xi : 0.0f;                      // keeps the arithmetic finite
     const float u = __fadd_rn(__fmul_rn(xc, 256.0f), 12582912.0f);
     const float kf = __fsub_rn(u, 12582912.0f);
-    const int k = __float_as_int(u) - 0x4B400000;
+    const unsigned ub = __float_as_uint(u);
     const double r = static_cast<double>(__fmaf_rn(kf, -0.00390625f, xc));   // exact
     double p = __fma_rn(0.009618129107628477, r, 0.05550410866482158);
     p = __fma_rn(p, r, 0.24022650695910072);
     p = __fma_rn(p, r, 0.6931471805599453);
-    const double t = __longlong_as_double(static_cast<long long>(tab[k & 255]));
+    const double t = __longlong_as_double(static_cast<long long>(tab[ub & 255u]));
     const double yd = __fma_rn(__dmul_rn(t, r), p, t);
     const unsigned low = static_cast<unsigned>(__double_as_longlong(yd)) & 0x1FFFFFFFu;
     const bool hard = low - ((1u << 28) - 64u) <= 128u;
-    const float fy = __int_as_float(__float_as_int(__double2float_rn(yd)) + ((k >> 8) << 23));
+    const float fy = __uint_as_float(__float_as_uint(__double2float_rn(yd)) + exp2_step_bits(ub));
     const bool zero = xi < -151.0f;
     y[i] = zero ? 0.0f : fy;
-    if (in ? hard : !zero) redo |= 1u << i;
+    redo |= in ? hard : !zero;
   }
   if (redo) {
 #pragma unroll
-    for (int i = 0; i < N; ++i)
-      if (redo >> i & 1u) y[i] = exp2_cr_t(x[i], g_exp2_frac64);
+    for (int i = 0; i < N; ++i) y[i] = exp2_cr_t(x[i], g_exp2_frac64);
   }
 }
 
