@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(512) k_attention_paged(AttnArgs p) {
 
   if (!active) return;
   // ---- 1/den, per-head output quantisation (attention_gqa.h:522-546)
-  const float rden = __fdiv_rn(1.0f, den);
+  const float rden = __frcp_rn(den);
   float o[4];
   float mx = 0.0f;
 #pragma unroll

@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(threads_of<VS>(), VS == 1 ? 4 : 3)
   float o[2], mx[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    o[h] = __fmul_rn(res[h], __fdiv_rn(1.0f, den[h]));
+    o[h] = __fmul_rn(res[h], __frcp_rn(den[h]));
     mx[h] = warp_tree_max(fabsf(o[h]));
   }
   if (lane == 0) { sm.red[warp][0] = mx[0]; sm.red[warp][1] = mx[1]; }

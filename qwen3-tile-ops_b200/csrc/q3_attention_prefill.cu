@@ -88,7 +88,7 @@ __device__ __forceinline__ void rows_sync(int qd) {
   asm volatile("bar.sync %0, %1;" ::"r"(2 + qd), "n"(KP * 32) : "memory");
 }
 __device__ __forceinline__ bool wait_or_abort(unsigned long long *b, uint32_t par, int *abort) {
-  if (mbar_wait(b, par, abort)) return true;
+  if (mbar_wait(b, par, abort, 1000000u)) return true;   // suspend up to 1 ms per try
   if (!*reinterpret_cast<volatile int *>(abort)) atomicOr(&g_pattn_error, kErrWait);
   *reinterpret_cast<volatile int *>(abort) = 1;
   return false;
@@ -315,16 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       den = __fadd_rn(__fmul_rn(den, corr), psum);
       m = mn;
       uint32_t w2[2];
-      int pq8[KPK];
-      quant_n_absmax(pv, pm, pq8);                         // one reciprocal for the 8 codes
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint32_t b0 = static_cast<uint8_t>(pq8[4 * c + 0]);
-        const uint32_t b1 = static_cast<uint8_t>(pq8[4 * c + 1]);
-        const uint32_t b2 = static_cast<uint8_t>(pq8[4 * c + 2]);
-        const uint32_t b3 = static_cast<uint8_t>(pq8[4 * c + 3]);
-        w2[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-      }
+      quant_pack_absmax(pv, pm, w2);                       // one reciprocal for the 8 codes
       // keys 8 pt .. : 16-key chunk pt / 2, bytes 8 (pt % 2) .. of the row's 16
       *reinterpret_cast<uint2 *>(sm.pq[slot] + (pt >> 1) * (8 * 2 * ROWS) + (r >> 3) * 128 +
                                  (r & 7) * 16 + (pt & 1) * 8) = make_uint2(w2[0], w2[1]);
@@ -337,7 +328,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     pv_update(J - 1, corr_prev, pmax_prev);
 
     // ---- 1/den, per-head output quantisation (attention_gqa.h:522-546)
-    const float rden = __fdiv_rn(1.0f, den);
+    const float rden = __frcp_rn(den);
     float mx = 0.0f;
 #pragma unroll
     for (int d = 0; d < KPC; ++d) {
@@ -352,16 +343,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float scale = __fmul_rn(omx, kInv127);
     if (active) {
       uint32_t w4[KPC / 4];
-      int o8[KPC];
-      quant_n_absmax(res, scale, o8);
-#pragma unroll
-      for (int c = 0; c < KPC / 4; ++c) {
-        const uint32_t b0 = static_cast<uint8_t>(o8[4 * c + 0]);
-        const uint32_t b1 = static_cast<uint8_t>(o8[4 * c + 1]);
-        const uint32_t b2 = static_cast<uint8_t>(o8[4 * c + 2]);
-        const uint32_t b3 = static_cast<uint8_t>(o8[4 * c + 3]);
-        w4[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-      }
+      quant_pack_absmax(res, scale, w4);
       uint4 *dst = reinterpret_cast<uint4 *>(p.o8 + grow * p.o_rb + h * 128 + KPC * pt);
 #pragma unroll
       for (int c = 0; c < KPC / 16; ++c) dst[c] = make_uint4(w4[4 * c], w4[4 * c + 1], w4[4 * c + 2], w4[4 * c + 3]);

@@ -264,9 +264,42 @@ __device__ __forceinline__ void quant_n_absmax(const float (&x)[N], float s, int
   }
 }
 
+// The codes of quant_n_absmax for N values (N a multiple of 4) packed four to a
+// word, code i in byte i % 4 of word i / 4.  The float bits of q + 1.5 * 2^23
+// carry the code in their low byte (0x4B400000 has a zero low byte), so byte
+// permutes gather them without the subtraction; a NaN among the values (one
+// check of their sum: NaN propagates, and a false alarm only costs time) sends
+// this thread through the per-value selects that give NaN the code 0.
+template <int N>
+__device__ __forceinline__ void quant_pack_absmax(const float (&x)[N], float s, uint32_t (&w)[N / 4]) {
+  uint32_t b[N];
+  if (quant_rcp_ok(s)) {
+    const float r = __frcp_rn(s);
+    float chk = 0.0f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const float q0 = __fmul_rn(x[i], r);
+      const float e = __fmaf_rn(-q0, s, x[i]);
+      b[i] = __float_as_uint(__fadd_rn(__fmaf_rn(e, r, q0), 12582912.0f));
+      chk = __fadd_rn(chk, x[i]);
+    }
+    if (chk != chk) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) b[i] = x[i] != x[i] ? 0u : b[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) b[i] = static_cast<uint32_t>(quant1(x[i], s));
+  }
+#pragma unroll
+  for (int c = 0; c < N / 4; ++c)
+    w[c] = __byte_perm(__byte_perm(b[4 * c], b[4 * c + 1], 0x0040),
+                       __byte_perm(b[4 * c + 2], b[4 * c + 3], 0x0040), 0x5410);
+}
+
 // 1/sqrt with two roundings (ref_qwen3.py:37-38)
 __device__ __forceinline__ float rsqrt_ref(float x) {
-  return __fdiv_rn(1.0f, __fsqrt_rn(x));
+  return __frcp_rn(__fsqrt_rn(x));
 }
 
 // max as np.where(b > a, b, a) (ref_qwen3.py:57-58)

@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             float e = __fadd_rn(en[tt * 4 + k], 1.0f);
-            e = __fdiv_rn(1.0f, e);
+            e = __frcp_rn(e);
             sw[tt * 4 + k] = __fmul_rn(__fmul_rn(gv[tt][k], e), uv[tt][k]);
             mx = fmaxf(mx, fabsf(sw[tt * 4 + k]));
           }

@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(NT) k_gemm_group_simt(GemmArgs p) {
       const float gt = acc[m];
       float e = exp_ref(__fmul_rn(gt, -1.0f));
       e = __fadd_rn(e, 1.0f);
-      e = __fdiv_rn(1.0f, e);
+      e = __frcp_rn(e);
       acc[m] = __fmul_rn(__fmul_rn(gt, e), acc2[DUAL ? m : 0]);
       const float mx = warp_tree_max(fabsf(acc[m]));
       if (lane == 0) sRed[m][wid] = mx;

@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (c0 + i < mvalid) {
               const float gt = accf[0][i];
               float e = __fadd_rn(en[i], 1.0f);
-              e = __fdiv_rn(1.0f, e);
+              e = __frcp_rn(e);
               sw = __fmul_rn(__fmul_rn(gt, e), accf[C::NACC - 1][i]);
             }
             sm.xchg[t * 128 + f][c0 + i] = sw;

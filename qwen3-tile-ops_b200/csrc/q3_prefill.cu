@@ -110,7 +110,7 @@ __global__ void k_prefill_scatter(const int8_t *k8, const int8_t *v8, const floa
 using q3::kEps;
 using q3::kInv127;
 using q3::quant1;
-using q3::quant_n_absmax;
+using q3::quant_pack_absmax;
 using q3::rsqrt_ref;
 using q3::warp_tree_max;
 
@@ -160,16 +160,10 @@ __global__ void k_norm_quant_1024(const float *__restrict__ x, const float *__re
 #pragma unroll
     for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(hv[i]));
     const float scale = __fmul_rn(warp_tree_max(am), kInv127);
-    int qv[8];
-    quant_n_absmax(hv, scale, qv);
+    uint32_t w[2];
+    quant_pack_absmax(hv, scale, w);
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const uint32_t b0 = static_cast<uint8_t>(qv[4 * c + 0]);
-      const uint32_t b1 = static_cast<uint8_t>(qv[4 * c + 1]);
-      const uint32_t b2 = static_cast<uint8_t>(qv[4 * c + 2]);
-      const uint32_t b3 = static_cast<uint8_t>(qv[4 * c + 3]);
-      reinterpret_cast<uint32_t *>(qrow + 128 * (2 * g + c))[lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-    }
+    for (int c = 0; c < 2; ++c) reinterpret_cast<uint32_t *>(qrow + 128 * (2 * g + c))[lane] = w[c];
     if (lane == 0) hs[static_cast<size_t>(row) * 4 + g] = scale;
   }
 }

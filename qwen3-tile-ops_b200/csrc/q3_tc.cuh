@@ -33,18 +33,31 @@ __device__ __forceinline__ uint64_t gtime() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// bounded wait for the completion of the phase with parity `par`
-__device__ __forceinline__ bool mbar_wait(unsigned long long *b, uint32_t par, const int *abort) {
+// Bounded wait for the completion of the phase with parity `par`: gives up
+// (false) when *abort is set or after about one second.  `sleep_ns` > 0 lets
+// each try_wait suspend the thread for up to that long while the phase is
+// incomplete (it resumes when the phase completes), so warps that mostly wait
+// take fewer issue slots from the others.
+__device__ __forceinline__ bool mbar_wait(unsigned long long *b, uint32_t par, const int *abort,
+                                          uint32_t sleep_ns = 0) {
   const uint32_t a = su32(b);
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(a), "r"(par)
-        : "memory");
+    if (sleep_ns)
+      asm volatile(
+          "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+          " selp.u32 %0, 1, 0, p;\n}"
+          : "=r"(ok)
+          : "r"(a), "r"(par), "r"(sleep_ns)
+          : "memory");
+    else
+      asm volatile(
+          "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+          " selp.u32 %0, 1, 0, p;\n}"
+          : "=r"(ok)
+          : "r"(a), "r"(par)
+          : "memory");
     if (ok) return true;
     if ((it & 127) == 0) {
       if (abort && *reinterpret_cast<const volatile int *>(abort)) return false;
