@@ -519,8 +519,9 @@ int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream);
 
 /* No counterpart in the reference: self-check of the device evaluations of
  * the correctly rounded exp2 (the short one, also in its batched branch-free
- * form, against the longer double-precision one it falls back to near rounding
- * midpoints).  Every float32 bit pattern in [lo_bits, hi_bits) is evaluated
+ * form and, for inputs <= 0, -inf and NaN, in the batched form for such
+ * inputs, against the longer double-precision one it falls back to near
+ * rounding midpoints).  Every float32 bit pattern in [lo_bits, hi_bits) is evaluated
  * each way; *count (device, caller-zeroed)
  * gains the number of results that differ and *first_bad (device, caller-set
  * to 0xffffffff) the smallest differing bit pattern. */

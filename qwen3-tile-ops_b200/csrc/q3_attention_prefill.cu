@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       float am = 0.0f;
 #pragma unroll
       for (int i = 0; i < KPK; ++i) s[i] = __fsub_rn(s[i], mn);
-      exp_ref_fast_n(s, sm.t256);                                             // p
+      exp_ref_fast_n<KPK, true>(s, sm.t256);                  // p (s - m' <= 0)
       const float ps = tree8_sum(s);
       *reinterpret_cast<float4 *>(&vsv[0]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt]);
       *reinterpret_cast<float4 *>(&vsv[4]) = *reinterpret_cast<const float4 *>(&sm.vs[st][KPK * pt + 4]);

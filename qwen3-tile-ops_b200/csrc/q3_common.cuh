@@ -157,15 +157,16 @@ __device__ __forceinline__ float exp2_cr_fast_t(float x, const unsigned long lon
 // a double result near a float32 rounding midpoint -- all N are redone by
 // exp2_cr_t afterwards (one flag instead of a mask: the redo is rare and
 // exp2_cr_t is exact for every input).  Same results as exp2_cr_fast_t value by
-// value.
-template <int N>
+// value.  NONPOS: the caller's inputs are <= 0, -inf or NaN (a softmax's
+// s - max), so the upper end of the range needs no test.
+template <int N, bool NONPOS = false>
 __device__ __forceinline__ void exp2_cr_fast_n(const float (&x)[N], float (&y)[N],
                                                const unsigned long long *tab) {
   bool redo = false;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     const float xi = x[i];
-    const bool in = xi >= -125.0f && xi < 128.0f;
+    const bool in = NONPOS ? xi >= -125.0f : (xi >= -125.0f && xi < 128.0f);
     const float xc = in ? xi : 0.0f;                      // keeps the arithmetic finite
     const float u = __fadd_rn(__fmul_rn(xc, 256.0f), 12582912.0f);
     const float kf = __fsub_rn(u, 12582912.0f);
@@ -203,13 +204,14 @@ __device__ __forceinline__ float exp_ref_fast(float x) {
 __device__ __forceinline__ float exp_ref_fast_t(float x, const unsigned long long *tab) {
   return exp2_cr_fast_t(__fmul_rn(x, __uint_as_float(kLog2eBits)), tab);
 }
-// exp(v[i]) in place for N values (exp_ref_fast_t value by value)
-template <int N>
+// exp(v[i]) in place for N values (exp_ref_fast_t value by value); NONPOS as
+// for exp2_cr_fast_n (log2(e) v keeps the sign of v)
+template <int N, bool NONPOS = false>
 __device__ __forceinline__ void exp_ref_fast_n(float (&v)[N], const unsigned long long *tab) {
   float x[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) x[i] = __fmul_rn(v[i], __uint_as_float(kLog2eBits));
-  exp2_cr_fast_n(x, v, tab);
+  exp2_cr_fast_n<N, NONPOS>(x, v, tab);
 }
 
 // rne(x / scale) saturated to +-127, NaN -> 0 (ref_qwen3.py:69-76).  The

@@ -375,7 +375,8 @@ extern "C" int q3_exp2_rows(const q3_view *x, const q3_view *out, void *stream) 
   return exp_common(x, out, 1, stream);
 }
 
-// every float32 bit pattern b in [lo, hi): exp2_cr_fast(b) against exp2_cr_t(b)
+// every float32 bit pattern b in [lo, hi): exp2_cr_fast(b), exp2_cr_fast_n and (for
+// b <= 0, -inf and the negative NaNs) its NONPOS form against exp2_cr_t(b)
 __global__ void k_exp2_selfcheck(uint32_t lo, uint32_t hi, unsigned long long *count,
                                  uint32_t *first_bad) {
   const uint64_t n = static_cast<uint64_t>(hi) - lo;
@@ -390,7 +391,12 @@ __global__ void k_exp2_selfcheck(uint32_t lo, uint32_t hi, unsigned long long *c
 #pragma unroll
     for (int j = 0; j < 8; ++j) xs[j] = __uint_as_float(b ^ static_cast<uint32_t>(j));
     exp2_cr_fast_n(xs, ys, g_exp2_t256);
-    if (__float_as_uint(f) != __float_as_uint(d) || __float_as_uint(ys[0]) != __float_as_uint(d)) {
+    bool bad = __float_as_uint(f) != __float_as_uint(d) || __float_as_uint(ys[0]) != __float_as_uint(d);
+    if ((b >> 31) || b == 0u) {   // and the form for inputs <= 0, -inf or NaN
+      exp2_cr_fast_n<8, true>(xs, ys, g_exp2_t256);
+      bad |= __float_as_uint(ys[0]) != __float_as_uint(d);
+    }
+    if (bad) {
       atomicAdd(count, 1ull);
       atomicMin(first_bad, b);
     }

@@ -352,12 +352,13 @@ def test_exp2_short_evaluation_exhaustive(q3):
     """The short evaluation of the correctly rounded exp2 that every kernel
     uses (256-entry table, degree-4 polynomial) gives the same bits as the
     longer double-precision one (itself pinned above and to the mpmath
-    hard-case table) on EVERY float32 input in (-151, 128) plus +-0: about
-    2.25e9 inputs."""
+    hard-case table) on EVERY float32 input in [0, 128) and every negative
+    one -- -0, -inf and the negative NaNs included, where the softmax's form
+    for non-positive inputs is checked too: about 3.2e9 inputs."""
     lib = q3._lib.lib()
     count = torch.zeros(1, dtype=torch.int64, device="cuda")
     first = torch.full((1,), -1, dtype=torch.int32, device="cuda")
-    for lo, hi in ((0x00000000, 0x43000000), (0x80000000, 0xC3170000)):
+    for lo, hi in ((0x00000000, 0x43000000), (0x80000000, 0xFFFFFFFF)):
         assert lib.q3_exp2_selfcheck(lo, hi, count.data_ptr(), first.data_ptr(), None) == 0
     torch.cuda.synchronize()
     bad = int(count.item())
