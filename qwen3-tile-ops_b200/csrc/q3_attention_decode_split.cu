@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(THREADS, 4)
                                ? 1.0f
                                : exp_ref(lane == 1 ? __fsub_rn(mp1, mj1) : __fsub_rn(mp0, mj0));
           float prv[2] = {__fsub_rn(s0r[g], mj0), __fsub_rn(s1r[g], mj1)};   // one batch
-          exp_ref_fast_n(prv, g_exp2_t256);
+          exp_ref_fast_n<2, true>(prv, g_exp2_t256);   // s - m_j <= 0
           const float pr0 = prv[0], pr1 = prv[1];
           const float psm0 = warp_tree_sum(pr0), psm1 = warp_tree_sum(pr1);
           const float pv0 = (t < kv_len) ? __fmul_rn(pr0, vs) : 0.0f;
