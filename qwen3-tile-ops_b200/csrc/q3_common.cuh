@@ -236,7 +236,7 @@ __device__ __forceinline__ int quant1(float x, float scale) {
 // correctly rounded x/s (P. Markstein, IBM J. Res. Dev. 34(1), 1990).  The
 // caller keeps s within [2^-100, 2^100] (quant_rcp_ok: s is normal, so its two
 // roundings are relative errors below 2^-24 each, and e does not underflow).
-// Then |x/s| <= 127 (1 + 2^-24)^2 < 127.5, so the rounded quotient needs no
+// Then |x/s| <= 127 / (1 - 2^-24)^2 < 127.5, so the rounded quotient needs no
 // clamp to +-127 and cannot overflow; it is rounded to an integer by the
 // 1.5 * 2^23 shifter (ties to even, as rint).  NaN x gives 0.  Equal to
 // quant1(x, s) for every such x (q3_quant_selfcheck).

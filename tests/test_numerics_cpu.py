@@ -141,14 +141,15 @@ def test_reciprocal_requantisation_matches_quotient():
 
 
 def test_absmax_scale_bounds_the_quotient():
-    """|x / s| <= amax / s = 1 / ((1 + d1) RN(1/127)) stays below 127.5 for a
-    scale in [2^-100, 2^100]: the reciprocal form needs no clamp."""
+    """|x / s| <= amax / s = 127 / ((1 + d1)(1 + d2)) <= 127 / (1 - 2^-24)^2,
+    below 127.5, for a scale in [2^-100, 2^100] (d1, d2 the relative errors of
+    the two roundings): the reciprocal form needs no clamp."""
     rng = np.random.default_rng(5)
     for amax in _amaxes(rng, 200):
         s = rn32(amax * KINV127)
         if TWO ** -100 <= s <= TWO ** 100:
             assert amax / s < Fraction(255, 2)
-            assert amax / s <= 127 * (1 + TWO ** -24) ** 2
+            assert amax / s <= 127 / (1 - TWO ** -24) ** 2
 
 
 def test_shifter_rounding_is_rint_and_keeps_the_low_byte():
